@@ -1,0 +1,102 @@
+// Shared device/host helpers for the B200 graft-train library.
+//
+// Conventions kept from the reference (Hinedes/GLT):
+//  * bf16 rounding is the bias trick `bits += ((bits>>16)&1) + 0x7FFF`
+//    (src/kernels_elementwise_impl.inc:575-580, src/gemm_impl.inc:69-80,
+//    src/checkpoint_impl.inc:49-57).  It equals IEEE RNE for every finite
+//    value and differs only in NaN payload handling, so every bf16 store in
+//    this library uses it to stay bit-identical with the reference files.
+//  * Errors never throw across the C ABI: every entry point returns a
+//    GltStatus and records a message readable through glt_last_error().
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include "../../include/glt_graft.h"
+
+namespace glt {
+
+// Records a formatted error message for glt_last_error() (thread local).
+void set_error(const char* fmt, ...);
+// Convenience: record message, return status.
+int fail(int status, const char* fmt, ...);
+
+}  // namespace glt
+
+#define GLT_CUDA_TRY(expr)                                                        \
+  do {                                                                            \
+    cudaError_t _e = (expr);                                                      \
+    if (_e != cudaSuccess) {                                                      \
+      return ::glt::fail(GLT_ECUDA, "%s:%d: %s -> %s", __FILE__, __LINE__, #expr, \
+                         cudaGetErrorString(_e));                                 \
+    }                                                                             \
+  } while (0)
+
+#define GLT_TRY(expr)          \
+  do {                         \
+    int _s = (expr);           \
+    if (_s != GLT_OK) return _s; \
+  } while (0)
+
+#define GLT_LAUNCH_CHECK() GLT_CUDA_TRY(cudaGetLastError())
+
+// ----------------------------------------------------------------------------
+// bf16 <-> f32 (bit-level, reference rounding)
+// ----------------------------------------------------------------------------
+__host__ __device__ __forceinline__ float bf16_bits_to_f32(uint16_t v) {
+  uint32_t bits = static_cast<uint32_t>(v) << 16;
+  float f;
+#ifdef __CUDA_ARCH__
+  f = __uint_as_float(bits);
+#else
+  __builtin_memcpy(&f, &bits, 4);
+#endif
+  return f;
+}
+
+__host__ __device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {
+  uint32_t bits;
+#ifdef __CUDA_ARCH__
+  bits = __float_as_uint(f);
+#else
+  __builtin_memcpy(&bits, &f, 4);
+#endif
+  bits += ((bits >> 16) & 1u) + 0x7FFFu;
+  return static_cast<uint16_t>(bits >> 16);
+}
+
+// Packs two floats into one 32-bit word of two bf16 (lo = a, hi = b).
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  return static_cast<uint32_t>(f32_to_bf16_bits(a)) |
+         (static_cast<uint32_t>(f32_to_bf16_bits(b)) << 16);
+}
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+
+// Round-trip an fp32 value through bf16 (reference rounding).
+__device__ __forceinline__ float round_bf16(float f) {
+  return bf16_bits_to_f32(f32_to_bf16_bits(f));
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Device-side error word: kernels that give up a bounded wait write a code
+// into this per-device word (they never trap); the host reads it back with
+// glt_device_error().  Allocated lazily once per device.
+namespace glt {
+unsigned int* device_error_word();
+}
+#define GLT_DEVERR_MBAR_TIMEOUT 1u
+#define GLT_DEVERR_BAD_SHAPE 2u

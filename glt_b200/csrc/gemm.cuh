@@ -1,0 +1,197 @@
+// Host-side launch machinery for the tcgen05 GEMM plus the epilogue functors
+// shared by every contraction of the grafted decoder step.
+#pragma once
+
+#include <climits>
+
+#include "tc_gemm.cuh"
+
+namespace glt {
+
+// One operand of a GEMM in the row-major views described in tc_gemm.cuh.
+struct Operand {
+  const void* ptr;   // bf16, 16-byte aligned
+  int64_t ld;        // leading dimension in elements (multiple of 8)
+  bool mn_major;     // false: [rows][K];  true: [K][rows]
+};
+
+// Encodes a 2-D bf16 tensor map with 128-byte swizzle:
+//   dims {inner, outer}, row stride `ld` elements, box {64, box_outer}.
+int make_tmap_bf16(CUtensorMap* tm, const void* base, uint64_t inner, uint64_t outer,
+                   uint64_t ld, uint32_t box_outer);
+
+int num_sms();
+// Sets the dynamic-smem attribute of `func` to `bytes` once per process.
+int ensure_smem_attr(const void* func, int bytes);
+
+// ---------------------------------------------------------------------------
+// Launcher
+// ---------------------------------------------------------------------------
+template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi>
+int launch_gemm(const Operand& A, const Operand& B, int M, int N, int K, const Epi& epi,
+                cudaStream_t stream, int k_splits = 1, const Operand* A2 = nullptr,
+                int a2_n_tile = INT_MAX, int group_m = 8) {
+  using namespace tc;
+  if (M <= 0 || N <= 0 || K <= 0) return GLT_OK;
+  if (A.mn_major != A_MN || B.mn_major != B_MN)
+    return fail(GLT_EINVAL, "launch_gemm: operand major-ness mismatch");
+  CUtensorMap ta, ta2, tb;
+  // A: K-major [M][K] -> dims {K, M}, box {64, 128};  MN-major [K][M] -> {M, K}, box {64, 64}
+  if (!A_MN) {
+    GLT_TRY(make_tmap_bf16(&ta, A.ptr, K, M, A.ld, BM));
+  } else {
+    GLT_TRY(make_tmap_bf16(&ta, A.ptr, M, K, A.ld, 64));
+  }
+  if (A2) {
+    if (A2->mn_major != A_MN) return fail(GLT_EINVAL, "launch_gemm: A2 major-ness mismatch");
+    if (!A_MN) {
+      GLT_TRY(make_tmap_bf16(&ta2, A2->ptr, K, M, A2->ld, BM));
+    } else {
+      GLT_TRY(make_tmap_bf16(&ta2, A2->ptr, M, K, A2->ld, 64));
+    }
+  } else {
+    ta2 = ta;
+  }
+  if (!B_MN) {
+    GLT_TRY(make_tmap_bf16(&tb, B.ptr, K, N, B.ld, BN));
+  } else {
+    GLT_TRY(make_tmap_bf16(&tb, B.ptr, N, K, B.ld, 64));
+  }
+  GemmShape shape;
+  shape.M = M;
+  shape.N = N;
+  shape.K = K;
+  shape.k_splits = k_splits < 1 ? 1 : k_splits;
+  shape.a2_n_tile = A2 ? a2_n_tile : INT_MAX;
+  shape.group_m = group_m;
+  shape.err = device_error_word();
+  if (!shape.err) return fail(GLT_ECUDA, "device error word unavailable");
+  auto kern = tc_gemm_kernel<BN, STAGES, A_MN, B_MN, Epi>;
+  constexpr int smem = SmemLayout<BN, STAGES>::TOTAL;
+  GLT_TRY(ensure_smem_attr(reinterpret_cast<const void*>(kern), smem));
+  const int units = ((M + BM - 1) / BM) * ((N + BN - 1) / BN) * shape.k_splits;
+  const int grid = units < num_sms() ? units : num_sms();
+  kern<<<grid, NUM_THREADS, smem, stream>>>(ta, ta2, tb, shape, epi);
+  GLT_LAUNCH_CHECK();
+  return GLT_OK;
+}
+
+// Picks a k-split so that the work units fill the SMs (weight-grad GEMMs have
+// few output tiles and a long K = token dimension).
+inline int pick_k_splits(int M, int N, int K, int bn) {
+  const int tiles = ((M + 127) / 128) * ((N + bn - 1) / bn);
+  const int sms = num_sms();
+  if (tiles >= sms) return 1;
+  int s = (2 * sms + tiles - 1) / tiles;  // aim for ~2 waves of units
+  const int max_s = K / (tc::BK * 4);    // keep >= 4 k-blocks per split
+  if (s > max_s) s = max_s;
+  return s < 1 ? 1 : s;
+}
+
+// ---------------------------------------------------------------------------
+// Epilogues
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void red_add_f32(float* p, float v) {
+  asm volatile("red.global.add.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
+}
+
+// C (fp32) = alpha * acc + beta * C;  with `atomic`, C += alpha * acc (split-K).
+template <int BN>
+struct EpiF32 {
+  float* C;
+  int64_t ldc;
+  int M, N;
+  float alpha, beta;
+  int atomic;
+  int vec_ok;  // C, ldc and N allow 16-byte vector access
+  __device__ __forceinline__ void operator()(const tc::EpiCtx<BN>& c) const {
+#pragma unroll 1
+    for (int j = 0; j < BN; j += 32) {
+      float v[32];
+      c.load(j, v);
+      if (c.row >= M) continue;
+      const int col0 = c.n0 + j;
+      if (col0 >= N) continue;
+      float* dst = C + static_cast<int64_t>(c.row) * ldc + col0;
+      if (atomic) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (col0 + i < N) red_add_f32(dst + i, alpha * v[i]);
+      } else if (vec_ok && col0 + 32 <= N) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+          float4 o;
+          if (beta != 0.f) {
+            const float4 old = *reinterpret_cast<const float4*>(dst + i);
+            o = make_float4(alpha * v[i] + beta * old.x, alpha * v[i + 1] + beta * old.y,
+                            alpha * v[i + 2] + beta * old.z, alpha * v[i + 3] + beta * old.w);
+          } else {
+            o = make_float4(alpha * v[i], alpha * v[i + 1], alpha * v[i + 2], alpha * v[i + 3]);
+          }
+          *reinterpret_cast<float4*>(dst + i) = o;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (col0 + i < N) dst[i] = alpha * v[i] + (beta != 0.f ? beta * dst[i] : 0.f);
+      }
+    }
+  }
+};
+
+// C (bf16) = bf16(acc [+ R]) where R is an optional bf16 residual (may alias C).
+template <int BN>
+struct EpiBF16 {
+  uint16_t* C;
+  int64_t ldc;
+  const uint16_t* R;
+  int64_t ldr;
+  int M, N;
+  int vec_ok;
+  __device__ __forceinline__ void operator()(const tc::EpiCtx<BN>& c) const {
+#pragma unroll 1
+    for (int j = 0; j < BN; j += 32) {
+      float v[32];
+      c.load(j, v);
+      if (c.row >= M) continue;
+      const int col0 = c.n0 + j;
+      if (col0 >= N) continue;
+      uint16_t* dst = C + static_cast<int64_t>(c.row) * ldc + col0;
+      if (vec_ok && col0 + 32 <= N) {
+        if (R) {
+          const uint16_t* rr = R + static_cast<int64_t>(c.row) * ldr + col0;
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            const uint4 r4 = *reinterpret_cast<const uint4*>(rr + i);
+            v[i + 0] += bf16_lo(r4.x); v[i + 1] += bf16_hi(r4.x);
+            v[i + 2] += bf16_lo(r4.y); v[i + 3] += bf16_hi(r4.y);
+            v[i + 4] += bf16_lo(r4.z); v[i + 5] += bf16_hi(r4.z);
+            v[i + 6] += bf16_lo(r4.w); v[i + 7] += bf16_hi(r4.w);
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          uint4 o;
+          o.x = pack_bf16x2(v[i + 0], v[i + 1]);
+          o.y = pack_bf16x2(v[i + 2], v[i + 3]);
+          o.z = pack_bf16x2(v[i + 4], v[i + 5]);
+          o.w = pack_bf16x2(v[i + 6], v[i + 7]);
+          *reinterpret_cast<uint4*>(dst + i) = o;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          if (col0 + i < N) {
+            float x = v[i];
+            if (R) x += bf16_bits_to_f32(R[static_cast<int64_t>(c.row) * ldr + col0 + i]);
+            dst[i] = f32_to_bf16_bits(x);
+          }
+        }
+      }
+    }
+  }
+};
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace glt

@@ -1,0 +1,185 @@
+// Runtime plumbing: error strings, per-device error word, tensor-map
+// encoding through the driver entry point (no link-time libcuda
+// dependency, so the library also loads on GPU-less hosts for the host-only
+// entry points), and the generic glt_gemm entry point.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <mutex>
+#include <unordered_map>
+
+#include "common.cuh"
+#include "gemm.cuh"
+
+namespace glt {
+
+static thread_local char t_err[1024] = "";
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_err, sizeof(t_err), fmt, ap);
+  va_end(ap);
+}
+
+int fail(int status, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_err, sizeof(t_err), fmt, ap);
+  va_end(ap);
+  return status;
+}
+
+static std::mutex g_mu;
+
+unsigned int* device_error_word() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  static std::unordered_map<int, unsigned int*> words;
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = words.find(dev);
+  if (it != words.end()) return it->second;
+  unsigned int* p = nullptr;
+  if (cudaMalloc(&p, sizeof(unsigned int)) != cudaSuccess) return nullptr;
+  if (cudaMemset(p, 0, sizeof(unsigned int)) != cudaSuccess) return nullptr;
+  words[dev] = p;
+  return p;
+}
+
+int num_sms() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!cached[dev]) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = v > 0 ? v : 148;
+  }
+  return cached[dev];
+}
+
+int ensure_smem_attr(const void* func, int bytes) {
+  static std::unordered_map<const void*, int> done;
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = done.find(func);
+  if (it != done.end() && it->second >= bytes) return GLT_OK;
+  cudaError_t e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess)
+    return fail(GLT_ECUDA, "cudaFuncSetAttribute(smem=%d): %s", bytes, cudaGetErrorString(e));
+  done[func] = bytes;
+  return GLT_OK;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static bool tried = false;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+int make_tmap_bf16(CUtensorMap* tm, const void* base, uint64_t inner, uint64_t outer,
+                   uint64_t ld, uint32_t box_outer) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return fail(GLT_ECUDA, "cuTensorMapEncodeTiled unavailable");
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0)
+    return fail(GLT_EINVAL, "tensor map base %p not 16-byte aligned", base);
+  if ((ld * 2) % 16 != 0)
+    return fail(GLT_EINVAL, "tensor map row stride %llu elements not a multiple of 8",
+                (unsigned long long)ld);
+  if (ld < inner) return fail(GLT_EINVAL, "tensor map ld %llu < inner %llu",
+                              (unsigned long long)ld, (unsigned long long)inner);
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {64, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(GLT_ECUDA, "cuTensorMapEncodeTiled failed (%d): inner=%llu outer=%llu ld=%llu",
+                (int)r, (unsigned long long)inner, (unsigned long long)outer,
+                (unsigned long long)ld);
+  return GLT_OK;
+}
+
+}  // namespace glt
+
+using namespace glt;
+
+extern "C" const char* glt_last_error(void) { return glt::t_err; }
+extern "C" const char* glt_version(void) { return "glt_b200 0.1.0 (sm_100a)"; }
+
+extern "C" int glt_device_error(unsigned int* out_code) {
+  unsigned int* w = device_error_word();
+  if (!w) return fail(GLT_ECUDA, "no device error word");
+  unsigned int v = 0;
+  GLT_CUDA_TRY(cudaMemcpy(&v, w, sizeof(v), cudaMemcpyDeviceToHost));
+  GLT_CUDA_TRY(cudaMemset(w, 0, sizeof(v)));
+  if (out_code) *out_code = v;
+  return GLT_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Generic GEMM entry
+// ---------------------------------------------------------------------------
+template <bool AMN, bool BMN>
+static int gemm_dispatch(const Operand& a, const Operand& b, void* C, int64_t ldc, int c_dtype,
+                         int M, int N, int K, float alpha, float beta, cudaStream_t st) {
+  const bool vec = aligned16(C) && (ldc % 8 == 0) && (N % 8 == 0);
+  if (c_dtype == 1) {
+    if (alpha != 1.f || beta != 0.f)
+      return fail(GLT_EINVAL, "glt_gemm: bf16 output supports alpha=1, beta=0 only");
+    if (N >= 2048) {
+      EpiBF16<256> e{static_cast<uint16_t*>(C), ldc, nullptr, 0, M, N, vec ? 1 : 0};
+      return launch_gemm<256, 4, AMN, BMN>(a, b, M, N, K, e, st);
+    }
+    EpiBF16<128> e{static_cast<uint16_t*>(C), ldc, nullptr, 0, M, N, vec ? 1 : 0};
+    return launch_gemm<128, 6, AMN, BMN>(a, b, M, N, K, e, st);
+  }
+  const int splits = (beta == 0.f) ? pick_k_splits(M, N, K, 128) : 1;
+  if (splits > 1) {
+    GLT_CUDA_TRY(cudaMemset2DAsync(C, ldc * 4, 0, static_cast<size_t>(N) * 4, M, st));
+    EpiF32<128> e{static_cast<float*>(C), ldc, M, N, alpha, 0.f, 1, vec ? 1 : 0};
+    return launch_gemm<128, 6, AMN, BMN>(a, b, M, N, K, e, st, splits);
+  }
+  if (N >= 2048) {
+    EpiF32<256> e{static_cast<float*>(C), ldc, M, N, alpha, beta, 0, vec ? 1 : 0};
+    return launch_gemm<256, 4, AMN, BMN>(a, b, M, N, K, e, st);
+  }
+  EpiF32<128> e{static_cast<float*>(C), ldc, M, N, alpha, beta, 0, vec ? 1 : 0};
+  return launch_gemm<128, 6, AMN, BMN>(a, b, M, N, K, e, st);
+}
+
+extern "C" int glt_gemm(const void* A, int64_t lda, int a_mn, const void* B, int64_t ldb,
+                        int b_mn, void* C, int64_t ldc, int c_dtype, int M, int N, int K,
+                        float alpha, float beta, void* stream) {
+  if (!A || !B || !C) return fail(GLT_EINVAL, "glt_gemm: null pointer");
+  if (M < 0 || N < 0 || K < 0) return fail(GLT_EINVAL, "glt_gemm: negative size");
+  if (c_dtype != 0 && c_dtype != 1) return fail(GLT_EINVAL, "glt_gemm: c_dtype must be 0 or 1");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Operand a{A, lda, a_mn != 0}, b{B, ldb, b_mn != 0};
+  if (a_mn) {
+    if (b_mn) return gemm_dispatch<true, true>(a, b, C, ldc, c_dtype, M, N, K, alpha, beta, st);
+    return gemm_dispatch<true, false>(a, b, C, ldc, c_dtype, M, N, K, alpha, beta, st);
+  }
+  if (b_mn) return gemm_dispatch<false, true>(a, b, C, ldc, c_dtype, M, N, K, alpha, beta, st);
+  return gemm_dispatch<false, false>(a, b, C, ldc, c_dtype, M, N, K, alpha, beta, st);
+}

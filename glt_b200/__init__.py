@@ -1,10 +1,10 @@
 """B200-native (sm_100a) grafted-MLP training library.
 
 The compute path is the in-tree CUDA library ``libglt_b200.so`` (C ABI in
-``include/glt_graft.h``); this package is its Python host binding and the
-host-side mirror of the reference's graft interface.
+``include/glt_graft.h``).  ``glt_b200.graft`` is the host-side mirror of the
+reference's graft interface; importing it (or ``glt_b200._lib``) loads the
+library and raises ImportError when it is missing -- there is no fallback.
+``python -m glt_b200.build`` compiles the library in-tree.
 """
-from . import _lib  # noqa: F401  (fails loudly when the CUDA library is missing)
-from ._lib import GltError, check, last_error  # noqa: F401
 
-__all__ = ["GltError", "check", "last_error"]
+__all__ = ["graft"]

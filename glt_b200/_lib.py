@@ -35,6 +35,34 @@ def _load() -> C.CDLL:
 lib = _load()
 
 _vp, _i32, _i64, _f32, _u32 = C.c_void_p, C.c_int, C.c_int64, C.c_float, C.c_uint
+_u64 = C.c_uint64
+
+
+class GltModelConfig(C.Structure):
+    """ctypes mirror of GltModelConfig (include/glt_graft.h)."""
+    _fields_ = [
+        ("hidden_dim", _i32), ("intermediate_dim", _i32), ("slice_dim", _i32), ("vocab_size", _i32),
+        ("num_layers", _i32), ("num_heads", _i32), ("num_kv_heads", _i32), ("head_dim", _i32),
+        ("max_domains", _i32), ("domain_id", _i32), ("layout", _i32), ("tie_embeddings", _i32),
+        ("rms_norm_eps", _f32), ("lm_loss_scale", _f32), ("lambda_silence", _f32), ("rope_theta", _f32),
+        ("graft_layer_start", _i32), ("graft_layer_end", _i32),
+        ("graft_proj_gate", _i32), ("graft_proj_up", _i32), ("graft_proj_down", _i32),
+        ("allow_expansion_trap", _i32),
+        ("adam_beta1", _f32), ("adam_beta2", _f32), ("adam_eps", _f32), ("adam_weight_decay", _f32),
+        ("gradient_clip_norm", _f32),
+        ("lr_warmup_steps", _i32), ("lr_peak", _f32),
+        ("no_rope_mask_len", _i32), ("no_rope_mask", _i32 * 256),
+    ]
+
+
+class GltStepStats(C.Structure):
+    _fields_ = [(n, _f32) for n in (
+        "lm_loss", "silence_loss", "domain_graft_energy", "ood_graft_energy",
+        "domain_ood_energy_ratio", "total_loss", "lr", "grad_norm")]
+
+
+_cfgp = C.POINTER(GltModelConfig)
+_fp = C.POINTER(C.c_void_p)
 
 # (name, restype, argtypes) for every exported symbol; tests check that each
 # declaration of include/glt_graft.h appears here and in the library.
@@ -44,6 +72,25 @@ SIGNATURES: dict[str, tuple] = {
     "glt_device_error": (_i32, [C.POINTER(_u32)]),
     "glt_gemm": (_i32, [_vp, _i64, _i32, _vp, _i64, _i32, _vp, _i64, _i32,
                         _i32, _i32, _i32, _f32, _f32, _vp]),
+    "glt_config_default": (_i32, [_cfgp]),
+    "glt_config_validate": (_i32, [_cfgp, _i32, _i32]),
+    "glt_get_lr": (_f32, [_cfgp, _i32, _i32]),
+    "glt_delta_offset": (_i64, [_i32, _i32, _i32, _i32]),
+    "glt_model_create": (_i32, [_cfgp, _i32, _i32, _i32, C.POINTER(_vp)]),
+    "glt_model_destroy": (_i32, [_vp]),
+    "glt_model_memory": (_i32, [_vp, C.POINTER(_i64), C.POINTER(_i64)]),
+    "glt_model_init_random": (_i32, [_vp, _u64, _f32, _f32, _f32]),
+    "glt_model_set_weight": (_i32, [_vp, _i32, _i32, _vp, _i64, _i32, _vp]),
+    "glt_model_graft_buffers": (_i32, [_vp, _fp, _fp, _fp, _fp, C.POINTER(_i64)]),
+    "glt_model_refresh_graft": (_i32, [_vp, _vp]),
+    "glt_train_step": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, C.POINTER(GltStepStats), _vp]),
+    "glt_forward": (_i32, [_vp, _vp, _i32, _i32, _vp, _vp]),
+    "glt_block_step": (_i32, [_vp, _vp, _vp, _f32, _i32, C.POINTER(_f32), _vp, _vp, _vp]),
+    "glt_model_activation": (_i32, [_vp, _i32, _i32, C.POINTER(_vp), C.POINTER(_i64)]),
+    "glt_dp_unique_id": (_i32, [_vp, _i32]),
+    "glt_dp_init": (_i32, [_vp, _vp, _i32, _i32]),
+    "glt_dp_finalize": (_i32, [_vp]),
+    "glt_memcpy": (_i32, [_vp, _vp, _i64, _vp, _i32]),
 }
 
 for _name, (_res, _args) in SIGNATURES.items():

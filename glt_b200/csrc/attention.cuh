@@ -1,0 +1,33 @@
+// Causal GQA attention of the decoder layer (reference: layer_forward_impl.inc:25-59
+// forward with at::scaled_dot_product_attention, attention_autograd_impl.inc:1-39
+// backward by autograd re-run).  Flash-style: the [T, T] score matrix is never
+// materialised; GQA is handled by indexing (no repeat_interleave copies).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace glt {
+
+struct AttnShape {
+  int B, T, nh, nkv, hd;
+  int64_t ld_qkv;   // row stride of the packed [q | k | v] activation (elements)
+  int64_t ld_o;     // row stride of O / dO (elements)
+  float scale;      // 1/sqrt(hd)
+};
+
+// In-place half-split RoPE on the q and k parts of the packed qkv rows
+// (rope_impl.inc:8-39).  cos/sin tables are [T, hd/2] fp32.  inverse = 1
+// applies the transpose rotation (used on dq/dk in the backward pass).
+int rope_apply(uint16_t* qkv, const AttnShape& s, const float* cos_t, const float* sin_t,
+               int inverse, int apply_q, int apply_k, cudaStream_t st);
+
+// O = softmax(Q K^T * scale, causal) V, lse = logsumexp per (b, h, t).
+int flash_fwd(const uint16_t* qkv, uint16_t* o, float* lse, const AttnShape& s, cudaStream_t st);
+
+// Backward: dqkv (bf16, same packing as qkv) from dO, O, lse.  Needs fp32
+// workspaces dq_acc [B*T, nh*hd] and dsum [B*nh*T].
+int flash_bwd(const uint16_t* qkv, const uint16_t* o, const uint16_t* dout, const float* lse,
+              uint16_t* dqkv, float* dq_acc, float* dsum, const AttnShape& s, cudaStream_t st);
+
+}  // namespace glt

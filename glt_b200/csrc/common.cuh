@@ -41,7 +41,16 @@ int fail(int status, const char* fmt, ...);
     if (_s != GLT_OK) return _s; \
   } while (0)
 
-#define GLT_LAUNCH_CHECK() GLT_CUDA_TRY(cudaGetLastError())
+namespace glt {
+// Counts this library's kernel launches (glt_launch_count).
+void count_launch();
+}  // namespace glt
+
+#define GLT_LAUNCH_CHECK()           \
+  do {                               \
+    ::glt::count_launch();           \
+    GLT_CUDA_TRY(cudaGetLastError()); \
+  } while (0)
 
 // ----------------------------------------------------------------------------
 // bf16 <-> f32 (bit-level, reference rounding)

@@ -1,0 +1,123 @@
+// Data parallelism: each rank runs its own microbatch; the only exchange is a
+// sum all-reduce of the graft gradients (base weights are frozen), issued per
+// layer on a dedicated stream as soon as that layer's weight-grad GEMMs have
+// finished, so it overlaps the backward of the layers below.  Clip and AdamW
+// then run replicated on identical (mean) gradients.  The reference is
+// single-GPU; this is the new exchange step of the multi-GPU path.
+//
+// NCCL is resolved with dlopen at dp_init, so the library loads (and its
+// single-GPU paths run) without NCCL present.
+#include <dlfcn.h>
+#include <nccl.h>
+#include <string.h>
+
+#include "common.cuh"
+#include "model.cuh"
+
+namespace glt {
+namespace {
+
+struct NcclApi {
+  void* handle = nullptr;
+  ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                            cudaStream_t) = nullptr;
+  ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+  const char* (*GetErrorString)(ncclResult_t) = nullptr;
+};
+
+NcclApi g_nccl;
+
+int load_nccl() {
+  if (g_nccl.handle) return GLT_OK;
+  const char* names[] = {"libnccl.so.2", "libnccl.so"};
+  void* h = nullptr;
+  for (const char* n : names) {
+    h = dlopen(n, RTLD_NOW | RTLD_GLOBAL);
+    if (h) break;
+  }
+  if (!h) return fail(GLT_ENCCL, "cannot dlopen libnccl.so.2: %s", dlerror());
+  g_nccl.GetUniqueId = reinterpret_cast<decltype(g_nccl.GetUniqueId)>(dlsym(h, "ncclGetUniqueId"));
+  g_nccl.CommInitRank = reinterpret_cast<decltype(g_nccl.CommInitRank)>(dlsym(h, "ncclCommInitRank"));
+  g_nccl.AllReduce = reinterpret_cast<decltype(g_nccl.AllReduce)>(dlsym(h, "ncclAllReduce"));
+  g_nccl.CommDestroy = reinterpret_cast<decltype(g_nccl.CommDestroy)>(dlsym(h, "ncclCommDestroy"));
+  g_nccl.CommAbort = reinterpret_cast<decltype(g_nccl.CommAbort)>(dlsym(h, "ncclCommAbort"));
+  g_nccl.GetErrorString =
+      reinterpret_cast<decltype(g_nccl.GetErrorString)>(dlsym(h, "ncclGetErrorString"));
+  if (!g_nccl.GetUniqueId || !g_nccl.CommInitRank || !g_nccl.AllReduce || !g_nccl.CommDestroy)
+    return fail(GLT_ENCCL, "libnccl is missing required symbols");
+  g_nccl.handle = h;
+  return GLT_OK;
+}
+
+const char* nccl_err(ncclResult_t r) {
+  return g_nccl.GetErrorString ? g_nccl.GetErrorString(r) : "nccl error";
+}
+
+}  // namespace
+
+int Model::dp_init(const void* unique_id, int rank, int world) {
+  if (world < 1 || rank < 0 || rank >= world) return fail(GLT_EINVAL, "bad rank/world");
+  if (nccl_comm) return fail(GLT_ESTATE, "data parallelism already initialised");
+  if (world == 1) {
+    dp_rank = 0;
+    dp_world = 1;
+    return GLT_OK;
+  }
+  GLT_TRY(load_nccl());
+  ncclUniqueId id;
+  memcpy(&id, unique_id, sizeof(id));
+  ncclComm_t comm = nullptr;
+  ncclResult_t r = g_nccl.CommInitRank(&comm, world, id, rank);
+  if (r != ncclSuccess) return fail(GLT_ENCCL, "ncclCommInitRank: %s", nccl_err(r));
+  nccl_comm = comm;
+  dp_rank = rank;
+  dp_world = world;
+  return GLT_OK;
+}
+
+int Model::dp_allreduce_layer(int l) {
+  if (dp_world <= 1) return GLT_OK;
+  const size_t n = static_cast<size_t>(3) * S * H;
+  float* buf = grad + static_cast<int64_t>(3) * l * S * H;
+  GLT_CUDA_TRY(cudaStreamWaitEvent(comm_stream, layer_done[l], 0));
+  ncclResult_t r = g_nccl.AllReduce(buf, buf, n, ncclFloat32, ncclSum,
+                                    static_cast<ncclComm_t>(nccl_comm), comm_stream);
+  if (r != ncclSuccess) return fail(GLT_ENCCL, "ncclAllReduce: %s", nccl_err(r));
+  return GLT_OK;
+}
+
+void Model::dp_shutdown() {
+  if (nccl_comm) {
+    cudaStreamSynchronize(comm_stream);
+    g_nccl.CommDestroy(static_cast<ncclComm_t>(nccl_comm));
+    nccl_comm = nullptr;
+  }
+  dp_world = 1;
+}
+
+}  // namespace glt
+
+extern "C" int glt_dp_unique_id(void* out, int out_bytes) {
+  if (!out || out_bytes < static_cast<int>(sizeof(ncclUniqueId)))
+    return glt::fail(GLT_EINVAL, "unique id buffer must hold %d bytes", (int)sizeof(ncclUniqueId));
+  GLT_TRY(glt::load_nccl());
+  ncclUniqueId id;
+  ncclResult_t r = glt::g_nccl.GetUniqueId(&id);
+  if (r != ncclSuccess) return glt::fail(GLT_ENCCL, "ncclGetUniqueId: %s", glt::nccl_err(r));
+  memcpy(out, &id, sizeof(id));
+  return GLT_OK;
+}
+
+extern "C" int glt_dp_init(GltModel* m, const void* unique_id, int rank, int world) {
+  if (!m || (!unique_id && world > 1)) return glt::fail(GLT_EINVAL, "null argument");
+  return reinterpret_cast<glt::Model*>(m)->dp_init(unique_id, rank, world);
+}
+
+extern "C" int glt_dp_finalize(GltModel* m) {
+  if (!m) return glt::fail(GLT_EINVAL, "null model");
+  reinterpret_cast<glt::Model*>(m)->dp_shutdown();
+  return GLT_OK;
+}

@@ -1,0 +1,144 @@
+// Model handle behind the opaque GltModel* of the C ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <vector>
+
+#include "../../include/glt_graft.h"
+#include "kernels_mem.cuh"
+
+namespace glt {
+
+int config_default(GltModelConfig* c);
+int config_validate(const GltModelConfig* c, int batch_size, int mode);
+float get_lr(const GltModelConfig* c, int step, int total_steps);
+
+struct Layer {
+  // frozen weights (bf16)
+  uint16_t* in_norm = nullptr;    // [D]
+  uint16_t* wqkv = nullptr;       // [(nh + 2 nkv) hd, D]  q rows, k rows, v rows
+  uint16_t* wo = nullptr;         // [D, nh hd]
+  uint16_t* post_norm = nullptr;  // [D]
+  uint16_t* w_gu = nullptr;       // [2F', D] interleaved gate/up 128-row blocks (+ graft rows)
+  uint16_t* w_d = nullptr;        // [D, F'] (+ graft columns = Delta_down^T)
+  // saved activations
+  float* var1 = nullptr;          // [M] input-norm mean square
+  uint16_t* qkv = nullptr;        // [M, QKV] after RoPE
+  uint16_t* o = nullptr;          // [M, nh hd]
+  float* lse = nullptr;           // [B, nh, T]
+  uint16_t* x_post = nullptr;     // [M, D] after attention residual
+  uint16_t* x_ffn = nullptr;      // [M, D] post-attention RMSNorm output
+  float* var2 = nullptr;          // [M]
+  float* esq = nullptr;           // [3][M] per-token sum of squares of gate/up/down deltas
+  uint16_t* dd = nullptr;         // [M, D] delta_down (bf16), for the silence gradient
+};
+
+struct Model {
+  GltModelConfig cfg{};
+  int kind = 0;
+  int B = 0, T = 0, M = 0, D = 0, F = 0, S = 0, H = 0, V = 0, L = 0;
+  int nh = 0, nkv = 0, hd = 0, QKV = 0, AD = 0;
+  int F_pad = 0, S_pad = 0, FF = 0;
+  std::vector<int> enabled;  // [3L] should_graft_proj
+  int active_grafts = 0;
+  bool shadow_baked = false;
+
+  // parameters
+  uint16_t* embed = nullptr;
+  uint16_t* lm_head = nullptr;
+  uint16_t* final_norm = nullptr;
+  std::vector<Layer> layers;
+  void* graft_mem = nullptr;
+  size_t graft_bytes = 0;
+  int64_t graft_numel = 0;
+  float* gw = nullptr;
+  float* grad = nullptr;
+  float* adam_m = nullptr;
+  float* adam_v = nullptr;
+
+  // arena
+  void* arena = nullptr;
+  size_t arena_bytes = 0;
+  std::vector<uint16_t*> xs;   // [L+1] residual stream at layer boundaries
+  float* esq_all = nullptr;    // [L][3][M]
+  uint16_t* xn = nullptr;
+  uint16_t* h = nullptr;
+  float* dx = nullptr;
+  float* dtmp = nullptr;
+  uint16_t* dy_b = nullptr;
+  uint16_t* dyg_b = nullptr;
+  uint16_t* dh = nullptr;
+  uint16_t* dgu = nullptr;
+  uint16_t* hg = nullptr;
+  uint16_t* dqkv = nullptr;
+  uint16_t* dout_b = nullptr;
+  float* dq_acc = nullptr;
+  float* dsum = nullptr;
+  uint16_t* xf = nullptr;
+  float* varf = nullptr;
+  float* var_in = nullptr;
+  uint16_t* logits = nullptr;
+  int ce_rows = 0;
+  float* cos_t = nullptr;
+  float* sin_t = nullptr;
+  DevStats* stats = nullptr;
+  DevStats* pinned_stats = nullptr;
+  int* d_enabled = nullptr;
+  uint16_t** d_gu_ptrs = nullptr;
+  uint16_t** d_wd_ptrs = nullptr;
+  int32_t* ids = nullptr;
+  int32_t* ood = nullptr;
+  float last_lr = 0.f;
+
+  // data parallel (NCCL, loaded at run time)
+  void* nccl_comm = nullptr;
+  int dp_rank = 0, dp_world = 1;
+  cudaStream_t comm_stream = nullptr;
+  std::vector<cudaEvent_t> layer_done;
+  cudaEvent_t comm_done = nullptr;
+  bool own_stream_events = false;
+
+  ~Model();
+  int setup(const GltModelConfig& c, int batch, int seq, int kind);
+  int allocate();
+  MirrorTargets mirror() const;
+  int set_weight(int layer, int which, const void* src, int64_t numel, int host, cudaStream_t st);
+  int init_random(uint64_t seed, float std, float graft_std, float graft_down_std);
+  int refresh_graft(cudaStream_t st);
+  bool rope_on(int l) const;
+  int ffn_forward(int l, const uint16_t* x_in, uint16_t* x_out, float* var_out, bool use_graft,
+                  cudaStream_t st);
+  int forward_layer(int l, bool use_graft, cudaStream_t st);
+  int ffn_backward(int l, cudaStream_t st);
+  int backward_layer(int l, cudaStream_t st);
+  int load_inputs(const int32_t* ids_in, const int32_t* ood_in, int host, cudaStream_t st);
+  int forward_all(bool use_graft, cudaStream_t st);
+  int train_step(const int32_t* ids_in, const int32_t* ood_in, int host, int step,
+                 int total_steps, GltStepStats* out, cudaStream_t st);
+  int finish_step(int step, int total_steps, GltStepStats* out, cudaStream_t st);
+  int forward_logits(const int32_t* ids_in, int host, int use_graft, uint16_t* out,
+                     cudaStream_t st);
+  int block_step(const uint16_t* x, const float* y, float lr, int step, float* loss,
+                 uint16_t* out, float* dx_out, cudaStream_t st);
+  int activation(int which, int layer, void** ptr, int64_t* numel);
+
+  // per-kind kernel timing (GLT_PROF_*)
+  bool prof_on = false;
+  std::vector<cudaEvent_t> ev_free;
+  struct LiveEv { int kind; cudaEvent_t a, b; };
+  std::vector<LiveEv> ev_live;
+  double prof_ms[GLT_PROF_KINDS] = {};
+  int64_t prof_n[GLT_PROF_KINDS] = {};
+  int prof_begin(int kind, cudaStream_t st);
+  void prof_end(int idx, cudaStream_t st);
+  int prof_collect();
+
+  // dp.cu
+  int dp_init(const void* unique_id, int rank, int world);
+  int dp_allreduce_layer(int l);
+  void dp_shutdown();
+};
+
+}  // namespace glt

@@ -8,6 +8,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <atomic>
 #include <mutex>
 #include <unordered_map>
 
@@ -34,6 +35,9 @@ int fail(int status, const char* fmt, ...) {
 }
 
 static std::mutex g_mu;
+static std::atomic<unsigned long long> g_launches{0};
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 unsigned int* device_error_word() {
   int dev = 0;
@@ -134,6 +138,21 @@ extern "C" int glt_device_error(unsigned int* out_code) {
   GLT_CUDA_TRY(cudaMemcpy(&v, w, sizeof(v), cudaMemcpyDeviceToHost));
   GLT_CUDA_TRY(cudaMemset(w, 0, sizeof(v)));
   if (out_code) *out_code = v;
+  return GLT_OK;
+}
+
+extern "C" int glt_launch_count(uint64_t* out) {
+  if (!out) return fail(GLT_EINVAL, "null argument");
+  *out = g_launches.load(std::memory_order_relaxed);
+  return GLT_OK;
+}
+
+extern "C" int glt_memcpy(void* dst, const void* src, int64_t bytes, void* stream, int sync) {
+  if (bytes < 0 || (bytes > 0 && (!dst || !src))) return fail(GLT_EINVAL, "glt_memcpy: bad args");
+  if (bytes == 0) return GLT_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  GLT_CUDA_TRY(cudaMemcpyAsync(dst, src, static_cast<size_t>(bytes), cudaMemcpyDefault, st));
+  if (sync) GLT_CUDA_TRY(cudaStreamSynchronize(st));
   return GLT_OK;
 }
 

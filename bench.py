@@ -1,0 +1,381 @@
+#!/usr/bin/env python
+"""Graft-train throughput at the Llama-3-8B shape.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one full grafted training step of the decoder (embedding, 32
+layers with attention and the [base | graft] SwiGLU MLP, LM head + CE on
+domain tokens, OOD silence loss, backward with FFN recompute, all-reduce of
+the graft gradients across ranks, global-norm clip, graft-only AdamW) over a
+16 x 2048-token microbatch per GPU.  Prints one JSON line (rank 0).
+
+value  tokens/s of the whole job with the token ids already on the device
+       (CUDA events on the step stream, max over ranks);
+e2e    the same metric through glt_train_step with pinned-host inputs copied
+       in and the step statistics read back every step;
+roofline  the dominant kernel (the gate/up GEMM with fused SwiGLU) timed live
+       with CUDA events around each of its launches inside the timed region;
+cpu_baseline  the fp32 CPU oracle on this host's cores, one decoder layer on
+       a bounded token sample, extrapolated per token.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WORKLOADS = {
+    # name: (layers, hidden, ffn, slice, heads, kv_heads, head_dim, vocab, theta, tie, batch, seq)
+    "c3": dict(num_layers=32, hidden_dim=4096, intermediate_dim=14336, slice_dim=1024, num_heads=32,
+               num_kv_heads=8, head_dim=128, vocab_size=128256, rope_theta=500000.0,
+               tie_embeddings=0, batch=16, seq=2048,
+               label="llama3-8b graft-train (BASELINE config 3): 32L d4096 ffn14336 + graft 1024, "
+                     "32q/8kv hd128, vocab 128256, 16x2048 tokens/GPU"),
+    "c2": dict(num_layers=24, hidden_dim=896, intermediate_dim=4864, slice_dim=512, num_heads=14,
+               num_kv_heads=2, head_dim=64, vocab_size=151936, rope_theta=1000000.0,
+               tie_embeddings=1, batch=8, seq=1024,
+               label="qwen2.5-0.5b graft-train (BASELINE config 2): 24L d896 ffn4864 + graft 512, "
+                     "14q/2kv hd64, vocab 151936, 8x1024 tokens/GPU"),
+}
+METRIC = "graft-train tokens/s at Llama-3-8B shape, 1-8 B200; MLP GEMM % of bf16 peak"
+# ncu DRAM traffic (bytes read + written) of one gate/up GEMM launch at the
+# config-3 shape; filled from profiles/ once captured, else None.
+GATE_UP_TRAFFIC_BYTES = None
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return dict(hbm=d["hbm_gbs"], tf=d["bf16_tflops"], tf_sus=d["bf16_tflops_sustained"],
+                    src="measured")
+    except Exception:  # noqa: BLE001
+        return dict(hbm=6650.0, tf=1590.0, tf_sus=1400.0, src="fallback")
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:  # noqa: BLE001
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.out = ""
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except Exception:  # noqa: BLE001
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        for line in (self.out or "").splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append(dict(sm=float(parts[1]), max=float(parts[2]), power=float(parts[3]),
+                                 hw=parts[5], hwt=parts[6], swt=parts[7], pcap=parts[8]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        reasons = set()
+        for r in rows:
+            for k, name in (("hw", "hw_slowdown"), ("hwt", "hw_thermal_slowdown"),
+                            ("swt", "sw_thermal_slowdown"), ("pcap", "sw_power_cap")):
+                if r[k].lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(r["sm"] for r in rows),
+                "sm_max_mhz": max(r["max"] for r in rows),
+                "power_w_max": max(r["power"] for r in rows),
+                "samples": len(rows), "reasons": sorted(reasons)}
+
+
+# ---------------------------------------------------------------------------
+# CPU oracle baseline (bounded sample, extrapolated)
+# ---------------------------------------------------------------------------
+def cpu_oracle_sample(wl: dict, tokens: int, reps: int = 2):
+    """Times one grafted decoder layer (forward + reference-structured backward)
+    of the fp32 CPU oracle on `tokens` tokens; returns (seconds per layer pass, cores)."""
+    import torch
+    from oracle import ref_math as rm
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    rc = rm.GraftConfig(hidden_dim=wl["hidden_dim"], intermediate_dim=wl["intermediate_dim"],
+                        slice_dim=wl["slice_dim"], vocab_size=wl["vocab_size"], num_layers=1,
+                        num_heads=wl["num_heads"], num_kv_heads=wl["num_kv_heads"],
+                        head_dim=wl["head_dim"], rope_theta=wl["rope_theta"], graft_layer_start=0,
+                        graft_layer_end=0, graft_proj_gate=1, graft_proj_up=1, graft_proj_down=1,
+                        layout="concat").finalize()
+    g = torch.Generator().manual_seed(0)
+    D, F = rc.hidden_dim, rc.intermediate_dim
+    nh, nkv, hd = rc.num_heads, rc.num_kv_heads, rc.head_dim
+
+    def rn(*s):
+        return torch.randn(*s, generator=g) * 0.02
+
+    lw = dict(in_norm=torch.ones(D), wq=rn(nh * hd, D), wk=rn(nkv * hd, D), wv=rn(nkv * hd, D),
+              wo=rn(D, nh * hd), post_norm=torch.ones(D), wg=rn(F, D), wu=rn(F, D), wd=rn(D, F))
+    delta = rn(3 * rc.slice_dim * rc.h_slice_dim)
+    x = torch.randn(1, tokens, D, generator=g)
+    ood = torch.zeros(tokens, dtype=torch.int32)
+    ood[tokens // 2:] = 1
+    times = []
+    for i in range(reps + 1):
+        t0 = time.perf_counter()
+        y, saved = rm.layer_forward(x, lw, delta, rc, 0)
+        grad = torch.zeros_like(delta)
+        rm.layer_backward(torch.randn_like(y) * 1e-3, lw, delta, saved, rc, 0, ood, 1e-4, grad)
+        dt = time.perf_counter() - t0
+        if i:
+            times.append(dt)
+    return statistics.median(times), cores
+
+
+def run_reference_arm(args, wl):
+    """--impl reference: the reference's CPU path is the fp32 oracle port (the
+    HIP/ROCm reference cannot be built here); each step is a bounded sample."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    tokens = args.cpu_tokens
+    per = []
+    for i in range(args.warmup + args.steps):
+        s, cores = cpu_oracle_sample(wl, tokens, reps=1)
+        if i >= args.warmup:
+            per.append(s)
+    sec_layer = statistics.median(per)
+    tok_s = tokens / (sec_layer * wl["num_layers"])
+    line = {
+        "impl": "reference", "metric": METRIC, "value": tok_s, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": wl["batch"] * wl["seq"] / tok_s * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: N(0,0.02) weights, N(0,1) activations",
+        "config": {"workload": wl["label"], "global_batch": wl["batch"], "seq_len": wl["seq"],
+                   "parallelism": "cpu"},
+        "cpu_baseline": {"value": tok_s, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"fp32 CPU oracle: one grafted decoder layer forward+backward on "
+                                   f"1x{tokens} tokens per step, extrapolated to "
+                                   f"{wl['num_layers']} layers (LM head excluded)"},
+        "e2e": {"value": tok_s, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c3")
+    ap.add_argument("--cpu-tokens", type=int, default=512)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    wl = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        return run_reference_arm(args, wl)
+
+    import torch
+    from glt_b200 import _lib
+    from glt_b200 import graft as G
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+
+    B, T = wl["batch"], wl["seq"]
+    cfg = G.GraftConfig(
+        hidden_dim=wl["hidden_dim"], intermediate_dim=wl["intermediate_dim"], slice_dim=wl["slice_dim"],
+        vocab_size=wl["vocab_size"], num_layers=wl["num_layers"], num_heads=wl["num_heads"],
+        num_kv_heads=wl["num_kv_heads"], head_dim=wl["head_dim"], rope_theta=wl["rope_theta"],
+        tie_embeddings=wl["tie_embeddings"], layout=G.LAYOUT_CONCAT, graft_layer_start=0,
+        graft_layer_end=wl["num_layers"] - 1, graft_proj_gate=1, graft_proj_up=1, graft_proj_down=1,
+        allow_expansion_trap=1, lambda_silence=5.0, lr_peak=2e-4, lr_warmup_steps=20)
+    model = G.GraftModel(cfg, B, T)
+    # replicas start identical; graft down N(0,0.02) so no zero-skipping shortcut exists
+    model.init_random(seed=1234, std=0.02, graft_std=0.02, graft_down_std=0.02)
+    if world > 1:
+        uid = [G.GraftModel.dp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        model.dp_init(uid[0], rank, world)
+
+    gen = torch.Generator(device="cuda").manual_seed(1000 + rank)
+    ids = torch.randint(0, wl["vocab_size"], (B, T), device="cuda", dtype=torch.int32, generator=gen)
+    ood = torch.zeros(B, T, dtype=torch.int32, device="cuda")
+    ood[B // 2:] = 1
+    total_steps = args.warmup + args.steps
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v: float) -> float:
+        if not dist:
+            return v
+        t = torch.tensor([v], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    step = 0
+    for _ in range(args.warmup):
+        model.train_step(ids, ood, step, total_steps, want_stats=False)
+        step += 1
+    barrier()
+    smi_index = local
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        try:
+            smi_index = int(vis.split(",")[local])
+        except ValueError:
+            pass
+    launches0 = C.c_uint64()
+    _lib.check(_lib.lib.glt_launch_count(C.byref(launches0)))
+    _lib.check(_lib.lib.glt_model_profile(model.handle, 1))
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(smi_index) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            model.train_step(ids, ood, step, total_steps, want_stats=False)
+            step += 1
+        e1.record(stream)
+        torch.cuda.synchronize()
+    _lib.check(_lib.lib.glt_model_profile(model.handle, 0))
+    launches1 = C.c_uint64()
+    _lib.check(_lib.lib.glt_launch_count(C.byref(launches1)))
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    tokens_per_step = world * B * T
+    value = tokens_per_step / (ms / 1e3)
+
+    # per-kind kernel times over the timed region
+    K = 17
+    kms = (C.c_double * K)()
+    kn = (C.c_int64 * K)()
+    _lib.check(_lib.lib.glt_model_profile_read(model.handle, kms, kn, 1))
+    M = B * T
+    D, F, S, L = wl["hidden_dim"], wl["intermediate_dim"], wl["slice_dim"], wl["num_layers"]
+    Fp = F + S
+    gu_flops = 2.0 * M * D * 2 * Fp                      # one gate/up launch
+    gu_ms = kms[0] / max(kn[0], 1)
+    pk = peaks()
+    achieved = gu_flops / (gu_ms / 1e3) / 1e12
+    mlp_alg = (12.0 * D * Fp + 6.0 * D * S) * M * L      # per step, recompute excluded
+    mlp_kinds = (0, 1, 2, 6, 7, 8, 9, 10)
+    mlp_ms = sum(kms[k] for k in mlp_kinds) / args.steps
+    mlp_exec = mlp_alg + (4.0 * D * Fp + 2.0 * D * S) * M * L  # + recompute + delta_down
+    roofline = {
+        "kernel": "tc_gemm_kernel<256,4,K,K,EpiSwiGLUFwd> (gate/up GEMM + fused SwiGLU)",
+        "bound": "tensor", "achieved": achieved, "peak": pk["tf_sus"], "unit": "TFLOP/s",
+        "frac": achieved / pk["tf_sus"],
+        "peak_note": f"{pk['src']} bf16_tflops_sustained (kernel timed inside a long step)",
+        "traffic": GATE_UP_TRAFFIC_BYTES,
+        "algorithmic_flops_per_launch": gu_flops, "avg_launch_ms": gu_ms,
+        "mlp_gemm": {
+            "pct_of_peak_algorithmic": 100.0 * mlp_alg / (mlp_ms / 1e3) / 1e12 / pk["tf_sus"],
+            "executed_tflops": mlp_exec / (mlp_ms / 1e3) / 1e12,
+            "ms_per_step": mlp_ms,
+            "definition": "(12*D*F' + 6*D*S) * tokens * layers / time of all MLP GEMM kernels "
+                          "(recompute time included, its FLOPs not)",
+        },
+    }
+    names = ["gate_up_fwd", "down_fwd", "delta_down", "qkv", "o_proj", "attn_fwd", "dh",
+             "recompute_swiglu_bwd", "wgrad_down", "wgrad_gate_up", "dx_gate_up", "do",
+             "attn_bwd", "dx_qkv", "lm_head", "lm_dx", "cross_entropy"]
+    kernels = {n: {"ms_per_step": kms[i] / args.steps, "launches_per_step": kn[i] / args.steps}
+               for i, n in enumerate(names)}
+
+    # e2e: public API with pinned host buffers, stats read back every step
+    e2e = None
+    if not args.no_e2e:
+        h_ids = ids.cpu().pin_memory()
+        h_ood = ood.cpu().pin_memory()
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            model.train_step(h_ids, h_ood, step, total_steps + args.steps, want_stats=True)
+            step += 1
+        torch.cuda.synchronize()
+        e2e_s = max_over_ranks((time.perf_counter() - t0) / args.steps)
+        e2e = {"value": tokens_per_step / e2e_s, "unit": "tokens/s",
+               "h2d_bytes_per_step": 2 * M * 4, "d2h_bytes_per_step": 32}
+    if world > 1:
+        model.dp_finalize()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sec, cores = cpu_oracle_sample(wl, args.cpu_tokens)
+        cpu = {"value": args.cpu_tokens / (sec * L), "unit": "tokens/s", "cores": cores,
+               "kind": "port",
+               "sample": f"fp32 CPU oracle: one grafted decoder layer forward+backward on "
+                         f"1x{args.cpu_tokens} tokens (median of 2 after 1 warm-up), extrapolated "
+                         f"to {L} layers (LM head excluded)"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: uniform-random token ids, seeded N(0,0.02) random-init weights",
+            "config": {"workload": wl["label"], "global_batch": world * B, "seq_len": T,
+                       "parallelism": f"dp{world}", "graft": "concat [base | graft], gate+up+down",
+                       "l2": "no flush: weights (16 GB) and activations exceed the 126 MB L2"},
+            "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu,
+            "clocks": clk.summary(),
+            "gpu_launches": int(launches1.value - launches0.value),
+            "kernels": kernels,
+        }
+        print(json.dumps(line), flush=True)
+    model.close()
+    if dist:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

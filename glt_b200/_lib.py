@@ -91,6 +91,9 @@ SIGNATURES: dict[str, tuple] = {
     "glt_dp_init": (_i32, [_vp, _vp, _i32, _i32]),
     "glt_dp_finalize": (_i32, [_vp]),
     "glt_memcpy": (_i32, [_vp, _vp, _i64, _vp, _i32]),
+    "glt_launch_count": (_i32, [C.POINTER(_u64)]),
+    "glt_model_profile": (_i32, [_vp, _i32]),
+    "glt_model_profile_read": (_i32, [_vp, C.POINTER(C.c_double), C.POINTER(_i64), _i32]),
 }
 
 for _name, (_res, _args) in SIGNATURES.items():

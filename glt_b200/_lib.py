@@ -94,6 +94,29 @@ SIGNATURES: dict[str, tuple] = {
     "glt_launch_count": (_i32, [C.POINTER(_u64)]),
     "glt_model_profile": (_i32, [_vp, _i32]),
     "glt_model_profile_read": (_i32, [_vp, C.POINTER(C.c_double), C.POINTER(_i64), _i32]),
+    "glt_attention_fwd": (_i32, [_vp, _i64, _vp, _i64, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _vp]),
+    "glt_attention_bwd": (_i32, [_vp, _i64, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _i32, _i32, _i32,
+                                 _i32, _i32, _vp]),
+    "glt_rope": (_i32, [_vp, _i64, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _vp]),
+    "glt_rmsnorm_fwd": (_i32, [_vp, _vp, _vp, _vp, _i32, _i32, _f32, _vp]),
+    "glt_rmsnorm_bwd": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _f32, _vp]),
+    "glt_arena_create": (_i32, [_i64, C.POINTER(_vp)]),
+    "glt_arena_destroy": (_i32, [_vp]),
+    "glt_graft_op": (_i32, [_i32, _i32, _i32, _i32, _vp, _vp, _vp, _i32, _i64, _vp, _i32, _i64,
+                            _vp, _i64, _f32, _f32, _vp, _vp]),
+    "glt_shadow_bake": (_i32, [_vp, _i64, _vp, _i32, _i32, _i32, _i32, _i32, _vp]),
+    "glt_apply_graft_to_shadow": (_i32, [_cfgp, _vp, _vp, _vp, _i64, _i64, _vp,
+                                         C.POINTER(_i32), _vp]),
+    "glt_checkpoint_save": (_i32, [C.c_char_p, _vp, _i64, _i32, C.c_char_p, _i32, _i32, _i32,
+                                   _i32, _i32]),
+    "glt_checkpoint_load": (_i32, [C.c_char_p, _vp, _i64, _i32, _i32, C.c_char_p, _i32, _i32,
+                                   _i32, C.POINTER(_i32)]),
+    "glt_model_save_checkpoint": (_i32, [_vp, C.c_char_p, C.c_char_p, _i32]),
+    "glt_model_load_checkpoint": (_i32, [_vp, C.c_char_p, C.c_char_p, _i32]),
+    "glt_load_bin": (_i32, [C.c_char_p, C.POINTER(_i32), C.POINTER(_i32), _vp, _i64]),
+    "glt_batch_walk_start": (_i32, [_u64, _i32, _i32, C.POINTER(_i32), C.POINTER(_i32)]),
+    "glt_batch_step": (_i32, [_vp, _i32, _vp, _i32, _i32, _i32, C.POINTER(_i32), C.POINTER(_i32),
+                              _vp, _vp]),
 }
 
 for _name, (_res, _args) in SIGNATURES.items():

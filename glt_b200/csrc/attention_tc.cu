@@ -1,0 +1,351 @@
+// Causal GQA flash-attention forward on the 5th-generation tensor cores.
+//
+// One CTA per (128-query tile, head, batch); 6 warps:
+//   warp 0      TMA producer: the Q tile once, then 64-key K/V tiles into a
+//               3-stage ring (128B swizzle, plain per-CTA loads, no multicast)
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer:
+//                 S_j = Q.K_j^T   (M=128, N=64,  K=hd; both operands K-major)
+//                 O  += P_j.V_j   (M=128, N=hd,  K=64; P K-major, V MN-major)
+//               S_{j+1} is issued before O += P_j.V_j so the softmax of tile j
+//               overlaps the next QK^T.
+//   warps 2..5  softmax: thread i owns query row i (= TMEM lane i); reads its
+//               S row with tcgen05.ld, keeps the running max / sum, writes the
+//               bf16 probabilities into a 128B-swizzled smem tile that is the
+//               K-major A operand of the PV product, and writes the output.
+// TMEM: two S buffers (64 columns each) + O (hd columns).
+// The O rescale of online softmax is conditional: the running max used for
+// the exponentials only moves when a row's max grows by more than 2^8, so the
+// O read-modify-write in TMEM (which must wait for the previous PV product)
+// is rare; p = exp2(s - m) stays <= 256, well inside fp32/bf16 range, and the
+// final normalisation uses the same m for O and the row sum.
+// All mbarrier waits are bounded (tc::mbar_wait); a timeout sets the device
+// error word and the CTA drains instead of hanging.
+#include <math.h>
+
+#include "attention.cuh"
+#include "common.cuh"
+#include "gemm.cuh"
+#include "tc_gemm.cuh"
+
+namespace glt {
+namespace {
+
+using namespace tc;
+
+constexpr int AQ = 128;      // query rows per CTA
+constexpr int AK = 64;       // keys per tile
+constexpr int KV_STAGES = 3;
+constexpr float LOG2E_F = 1.4426950408889634f;
+constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+template <int HD>
+struct FwdSmem {
+  static constexpr uint32_t Q_BYTES = AQ * HD * 2;          // HD/64 blocks of [128 x 128B]
+  static constexpr uint32_t K_BYTES = AK * HD * 2;          // HD/64 blocks of [64 x 128B]
+  static constexpr uint32_t V_BYTES = AK * HD * 2;          // HD/64 chunks of [64 x 128B]
+  static constexpr uint32_t P_BYTES = AQ * AK * 2;          // [128 x 128B]
+  static constexpr uint32_t OFF_Q = 0;
+  static constexpr uint32_t OFF_K = OFF_Q + Q_BYTES;
+  static constexpr uint32_t OFF_V = OFF_K + KV_STAGES * K_BYTES;
+  static constexpr uint32_t OFF_P = OFF_V + KV_STAGES * V_BYTES;
+  static constexpr uint32_t OFF_BAR = OFF_P + 2 * P_BYTES;
+  static constexpr uint32_t NUM_BARS = 1 + 2 * KV_STAGES + 2 + 2 + 2 + 2 + 1;
+  static constexpr uint32_t TOTAL = 1024 + OFF_BAR + NUM_BARS * 8 + 16;
+};
+
+template <int HD>
+__global__ void __launch_bounds__(192, 1)
+    attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
+                       const __grid_constant__ CUtensorMap tm_kv, uint16_t* __restrict__ o,
+                       float* __restrict__ lse, AttnShape s, unsigned int* err) {
+  using L = FwdSmem<HD>;
+  constexpr uint32_t TMEM_COLS = 256;   // S0 | S1 | O (HD <= 128)
+  constexpr uint32_t ID_S = make_idesc(AK, false, false);
+  constexpr uint32_t ID_PV = make_idesc(HD, false, true);
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::OFF_BAR);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = q_full + 1;
+  uint64_t* kv_empty = kv_full + KV_STAGES;
+  uint64_t* s_full = kv_empty + KV_STAGES;  // [2]
+  uint64_t* s_free = s_full + 2;            // [2]
+  uint64_t* p_full = s_free + 2;            // [2]
+  uint64_t* p_free = p_full + 2;            // [2]  (= PV product done)
+  uint64_t* drain = p_free + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  __shared__ int abort_flag;
+  volatile int& s_abort = abort_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = gridDim.x - 1 - blockIdx.x;   // heaviest tiles first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int kvh = h / (s.nh / s.nkv);
+  const int n_kv = (qt * AQ + AQ) / AK;        // causal: keys < (qt+1)*128
+  const int row_base = b * s.T;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < KV_STAGES; ++i) { mbar_init(&kv_full[i], 1); mbar_init(&kv_empty[i], 1); }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 4);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&p_free[i], 1);
+    }
+    mbar_init(drain, 1);
+    s_abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_kv);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t sQ = smem_u32(sm + L::OFF_Q);
+  const uint32_t sK = smem_u32(sm + L::OFF_K);
+  const uint32_t sV = smem_u32(sm + L::OFF_V);
+  const uint32_t sP = smem_u32(sm + L::OFF_P);
+
+  if (warp == 0) {
+    // ------------------------------ producer ------------------------------
+    if (lane == 0) {
+      const int qcol = h * HD, kcol = (s.nh + kvh) * HD, vcol = (s.nh + s.nkv + kvh) * HD;
+      mbar_arrive_expect_tx(q_full, L::Q_BYTES);
+#pragma unroll
+      for (int c = 0; c < HD / 64; ++c)
+        tma_load_2d(sm + L::OFF_Q + c * (AQ * 128), &tm_q, q_full, qcol + 64 * c, row_base + qt * AQ);
+      for (int j = 0; j < n_kv && !s_abort; ++j) {
+        const int st = j % KV_STAGES;
+        if (!mbar_wait(&kv_empty[st], ((j / KV_STAGES) & 1) ^ 1, err)) { s_abort = 1; break; }
+        mbar_arrive_expect_tx(&kv_full[st], L::K_BYTES + L::V_BYTES);
+        uint8_t* kb = sm + L::OFF_K + st * L::K_BYTES;
+        uint8_t* vb = sm + L::OFF_V + st * L::V_BYTES;
+#pragma unroll
+        for (int c = 0; c < HD / 64; ++c) {
+          tma_load_2d(kb + c * (AK * 128), &tm_kv, &kv_full[st], kcol + 64 * c, row_base + j * AK);
+          tma_load_2d(vb + c * (AK * 128), &tm_kv, &kv_full[st], vcol + 64 * c, row_base + j * AK);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer ----------------------------
+    if (lane == 0) {
+      auto issue_s = [&](int j) -> bool {
+        const int st = j % KV_STAGES, sb = j & 1;
+        if (!mbar_wait(&kv_full[st], (j / KV_STAGES) & 1, err)) return false;
+        if (!mbar_wait(&s_free[sb], ((j >> 1) & 1) ^ 1, err)) return false;
+        tc_fence_after();
+        const uint32_t kb = sK + st * L::K_BYTES;
+#pragma unroll
+        for (int k = 0; k < HD / 16; ++k) {
+          const uint64_t ad = desc_kmajor(sQ + (k >> 2) * (AQ * 128), k & 3);
+          const uint64_t bd = desc_kmajor(kb + (k >> 2) * (AK * 128), k & 3);
+          umma_bf16(tmem + sb * AK, ad, bd, ID_S, k > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[sb]);
+        return true;
+      };
+      bool ok = mbar_wait(q_full, 0, err);
+      if (ok) { tc_fence_after(); ok = issue_s(0); }
+      for (int j = 0; ok && j < n_kv; ++j) {
+        if (j + 1 < n_kv && !issue_s(j + 1)) { ok = false; break; }
+        const int sb = j & 1, st = j % KV_STAGES;
+        if (!mbar_wait(&p_full[sb], (j >> 1) & 1, err)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t vb = sV + st * L::V_BYTES;
+        const uint32_t pb = sP + sb * L::P_BYTES;
+#pragma unroll
+        for (int k = 0; k < AK / 16; ++k) {
+          const uint64_t ad = desc_kmajor(pb, k);
+          const uint64_t bd = desc_mnmajor(vb, k);
+          umma_bf16(tmem + 2 * AK, ad, bd, ID_PV, (j > 0 || k > 0) ? 1u : 0u);
+        }
+        umma_commit(&p_free[sb]);
+        umma_commit(&kv_empty[st]);
+      }
+      if (!ok) s_abort = 1;
+    }
+  } else {
+    // ------------------------------- softmax ------------------------------
+    const int sub = warp & 3;
+    const int r = sub * 32 + lane;             // row in the tile / TMEM lane
+    const int qrow = qt * AQ + r;              // position in the sequence
+    const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
+    const float sl2 = s.scale * LOG2E_F;
+    float m_run = -INFINITY, l_run = 0.f;
+    for (int j = 0; j < n_kv; ++j) {
+      const int sb = j & 1;
+      if (!mbar_wait(&s_full[sb], (j >> 1) & 1, err)) { s_abort = 1; break; }
+      tc_fence_after();
+      float sv[AK];
+      {
+        float t[32];
+        tmem_ld32(tmem + lane_off + sb * AK, t);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) sv[i] = t[i];
+        tmem_ld32(tmem + lane_off + sb * AK + 32, t);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) sv[32 + i] = t[i];
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[sb]);
+      // scale + causal mask + tile max
+      float mt = -INFINITY;
+      const bool diag = (j + 1) * AK > qt * AQ;
+#pragma unroll
+      for (int i = 0; i < AK; ++i) {
+        float v = sv[i] * sl2;
+        if (diag && j * AK + i > qrow) v = -INFINITY;
+        sv[i] = v;
+        mt = fmaxf(mt, v);
+      }
+      const bool need = mt > m_run + RESCALE_THRESHOLD;   // includes the first tile
+      const float m_new = need ? fmaxf(m_run, mt) : m_run;
+      const float alpha = (m_run == -INFINITY) ? 0.f : exp2f(m_run - m_new);
+      // P buffer sb is free once the PV product of tile j-2 is done
+      if (j >= 2 && !mbar_wait(&p_free[sb], ((j - 2) >> 1) & 1, err)) { s_abort = 1; break; }
+      if (__any_sync(0xffffffffu, need) && j > 0) {
+        // O (TMEM) must be quiescent: wait for the PV product of tile j-1
+        if (!mbar_wait(&p_free[(j - 1) & 1], ((j - 1) >> 1) & 1, err)) { s_abort = 1; break; }
+        tc_fence_after();
+        const float f = need ? alpha : 1.f;
+#pragma unroll 1
+        for (int c = 0; c < HD; c += 32) {
+          float ov[32];
+          tmem_ld32(tmem + lane_off + 2 * AK + c, ov);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) ov[i] *= f;
+          tmem_st32(tmem + lane_off + 2 * AK + c, ov);
+        }
+        tmem_wait_st();
+      }
+      if (need) {
+        l_run *= alpha;
+        m_run = m_new;
+      }
+      // probabilities -> bf16 P row (128 bytes, swizzled 16-byte chunks)
+      float ls = 0.f;
+      const uint32_t prow = sP + sb * L::P_BYTES + r * 128;
+#pragma unroll
+      for (int c = 0; c < AK / 8; ++c) {
+        float p[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          p[i] = exp2f(sv[c * 8 + i] - m_run);
+          ls += p[i];
+        }
+        const uint32_t w0 = pack_bf16x2(p[0], p[1]), w1 = pack_bf16x2(p[2], p[3]);
+        const uint32_t w2 = pack_bf16x2(p[4], p[5]), w3 = pack_bf16x2(p[6], p[7]);
+        asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(prow + ((c ^ (r & 7)) << 4)),
+                     "r"(w0), "r"(w1), "r"(w2), "r"(w3)
+                     : "memory");
+      }
+      l_run += ls;
+      fence_proxy_async_smem();   // generic-proxy smem writes -> visible to the tensor core
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[sb]);
+    }
+    // epilogue: O / l -> bf16, lse
+    if (!s_abort && mbar_wait(&p_free[(n_kv - 1) & 1], ((n_kv - 1) >> 1) & 1, err)) {
+      tc_fence_after();
+      const float inv = 1.f / l_run;
+      uint16_t* orow = o + static_cast<int64_t>(row_base + qrow) * s.ld_o + h * HD;
+#pragma unroll 1
+      for (int c = 0; c < HD; c += 32) {
+        float ov[32];
+        tmem_ld32(tmem + lane_off + 2 * AK + c, ov);
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          uint4 w;
+          w.x = pack_bf16x2(ov[i] * inv, ov[i + 1] * inv);
+          w.y = pack_bf16x2(ov[i + 2] * inv, ov[i + 3] * inv);
+          w.z = pack_bf16x2(ov[i + 4] * inv, ov[i + 5] * inv);
+          w.w = pack_bf16x2(ov[i + 6] * inv, ov[i + 7] * inv);
+          *reinterpret_cast<uint4*>(orow + c + i) = w;
+        }
+      }
+      lse[(static_cast<int64_t>(b) * s.nh + h) * s.T + qrow] = (m_run + log2f(l_run)) / LOG2E_F;
+    } else {
+      s_abort = 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    if (s_abort) {
+      if (lane == 0) {
+        umma_commit(drain);
+        mbar_wait(drain, 0, err);
+      }
+      __syncwarp();
+    }
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+template <int HD>
+int launch_fwd_tc(const uint16_t* qkv, uint16_t* o, float* lse, const AttnShape& s,
+                  cudaStream_t st) {
+  const int64_t M = static_cast<int64_t>(s.B) * s.T;
+  CUtensorMap tq, tkv;
+  GLT_TRY(make_tmap_bf16(&tq, qkv, s.ld_qkv, M, s.ld_qkv, AQ));
+  GLT_TRY(make_tmap_bf16(&tkv, qkv, s.ld_qkv, M, s.ld_qkv, AK));
+  auto k = attn_fwd_tc_kernel<HD>;
+  constexpr int smem = FwdSmem<HD>::TOTAL;
+  GLT_TRY(ensure_smem_attr(reinterpret_cast<const void*>(k), smem));
+  dim3 grid(s.T / AQ, s.nh, s.B);
+  k<<<grid, 192, smem, st>>>(tq, tkv, o, lse, s, device_error_word());
+  GLT_LAUNCH_CHECK();
+  return GLT_OK;
+}
+
+}  // namespace
+
+int flash_fwd_tc(const uint16_t* qkv, uint16_t* o, float* lse, const AttnShape& s,
+                 cudaStream_t st) {
+  if (s.hd != 64 && s.hd != 128) return fail(GLT_EINVAL, "attention: head_dim %d unsupported", s.hd);
+  if (s.T % AQ) return fail(GLT_EINVAL, "attention (tcgen05): seq_len %d not a multiple of 128", s.T);
+  if (s.nkv <= 0 || s.nh % s.nkv) return fail(GLT_EINVAL, "attention: nh %% nkv != 0");
+  if (s.ld_qkv % 8 || s.ld_o % 8) return fail(GLT_EINVAL, "attention: strides not 16-byte");
+  return s.hd == 128 ? launch_fwd_tc<128>(qkv, o, lse, s, st) : launch_fwd_tc<64>(qkv, o, lse, s, st);
+}
+
+}  // namespace glt

@@ -1,0 +1,395 @@
+// Host-side I/O of the graft path: the GRFT checkpoint (src/checkpoint_impl.inc),
+// the .bin token files and the seeded batch walk (src/data_impl.inc,
+// grafting.hip:924-988).  Pure C++ (no device code) except for the optional
+// device source/destination of the checkpoint weights; these entry points
+// work on GPU-less hosts when given host buffers.
+#include <stdio.h>
+#include <string.h>
+#include <sys/stat.h>
+
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "model.cuh"
+
+namespace glt {
+namespace {
+
+constexpr uint32_t kGrftMagic = 0x54465247u;  // "GRFT" little endian
+constexpr uint8_t kGrftVersion = 4;
+
+bool is_dir(const char* p) {
+  struct stat s;
+  return stat(p, &s) == 0 && S_ISDIR(s.st_mode);
+}
+
+std::string parent_of(const std::string& p) {
+  const size_t k = p.find_last_of('/');
+  return k == std::string::npos ? std::string() : p.substr(0, k);
+}
+
+// The header text of build_safetensors_header (checkpoint_impl.inc:8-30),
+// byte for byte (values are not escaped, as in the reference).
+std::string grft_header(const char* session, int domain, int S, int H, int D, int L) {
+  const long long total = 3LL * L;
+  const long long nbytes = total * S * static_cast<long long>(H) * 2;
+  char buf[1024];
+  std::string s = "{\"__metadata__\":{\"session_id\":\"";
+  s += session ? session : "";
+  snprintf(buf, sizeof(buf),
+           "\",\"domain_id\":\"%d\",\"slice_dim\":\"%d\",\"h_slice_dim\":\"%d\",\"hidden_dim\":\"%d\","
+           "\"num_layers\":\"%d\"},\"delta_weights\":{\"dtype\":\"BF16\",\"shape\":[%lld,%d,%d],"
+           "\"data_offsets\":[0,%lld]}}",
+           domain, S, H, D, L, total, S, H, nbytes);
+  s += buf;
+  return s;
+}
+
+// ---- a small JSON reader, enough for safetensors headers ----
+struct Json {
+  const char* p;
+  const char* e;
+  bool ok = true;
+  void ws() { while (p < e && (*p == ' ' || *p == '\n' || *p == '\r' || *p == '\t' || *p == '\0')) ++p; }
+  bool eat(char c) { ws(); if (p < e && *p == c) { ++p; return true; } return false; }
+  bool str(std::string& out) {
+    ws();
+    if (p >= e || *p != '"') return ok = false;
+    ++p;
+    out.clear();
+    while (p < e && *p != '"') {
+      if (*p == '\\' && p + 1 < e) { ++p; }
+      out.push_back(*p++);
+    }
+    if (p >= e) return ok = false;
+    ++p;
+    return true;
+  }
+  bool num(long long& v) {
+    ws();
+    char* end = nullptr;
+    v = strtoll(p, &end, 10);
+    if (end == p) return ok = false;
+    p = end;
+    return true;
+  }
+  // Skips any value.
+  bool skip() {
+    ws();
+    if (p >= e) return ok = false;
+    if (*p == '"') { std::string t; return str(t); }
+    if (*p == '{' || *p == '[') {
+      const char open = *p, close = open == '{' ? '}' : ']';
+      ++p;
+      if (eat(close)) return true;
+      while (ok) {
+        if (open == '{') { std::string k; if (!str(k) || !eat(':')) return ok = false; }
+        if (!skip()) return false;
+        if (eat(',')) continue;
+        if (eat(close)) return true;
+        return ok = false;
+      }
+      return false;
+    }
+    while (p < e && *p != ',' && *p != '}' && *p != ']') ++p;
+    return true;
+  }
+};
+
+struct StHeader {
+  std::string dtype;
+  std::vector<long long> shape;
+  long long off0 = -1, off1 = -1;
+  bool has_tensor = false;
+  std::string session;
+  int domain = -1;
+};
+
+bool parse_header(const char* p, size_t n, StHeader& h) {
+  Json j{p, p + n};
+  if (!j.eat('{')) return false;
+  if (j.eat('}')) return true;
+  while (j.ok) {
+    std::string key;
+    if (!j.str(key) || !j.eat(':')) return false;
+    if (key == "__metadata__") {
+      if (!j.eat('{')) return false;
+      if (!j.eat('}')) {
+        while (j.ok) {
+          std::string k, v;
+          if (!j.str(k) || !j.eat(':') || !j.str(v)) return false;
+          if (k == "session_id") h.session = v;
+          if (k == "domain_id") h.domain = atoi(v.c_str());
+          if (j.eat(',')) continue;
+          if (j.eat('}')) break;
+          return false;
+        }
+      }
+    } else if (key == "delta_weights") {
+      h.has_tensor = true;
+      if (!j.eat('{')) return false;
+      while (j.ok) {
+        std::string k;
+        if (!j.str(k) || !j.eat(':')) return false;
+        if (k == "dtype") {
+          if (!j.str(h.dtype)) return false;
+        } else if (k == "shape" || k == "data_offsets") {
+          if (!j.eat('[')) return false;
+          std::vector<long long> v;
+          if (!j.eat(']')) {
+            while (true) {
+              long long x;
+              if (!j.num(x)) return false;
+              v.push_back(x);
+              if (j.eat(',')) continue;
+              if (j.eat(']')) break;
+              return false;
+            }
+          }
+          if (k == "shape") h.shape = v;
+          else if (v.size() == 2) { h.off0 = v[0]; h.off1 = v[1]; }
+        } else if (!j.skip()) {
+          return false;
+        }
+        if (j.eat(',')) continue;
+        if (j.eat('}')) break;
+        return false;
+      }
+    } else if (!j.skip()) {
+      return false;
+    }
+    if (j.eat(',')) continue;
+    if (j.eat('}')) return true;
+    return false;
+  }
+  return false;
+}
+
+bool read_file(const char* path, std::vector<char>& buf) {
+  FILE* f = fopen(path, "rb");
+  if (!f) return false;
+  fseek(f, 0, SEEK_END);
+  long n = ftell(f);
+  fseek(f, 0, SEEK_SET);
+  if (n < 0) { fclose(f); return false; }
+  buf.resize(static_cast<size_t>(n));
+  const size_t got = n ? fread(buf.data(), 1, static_cast<size_t>(n), f) : 0;
+  fclose(f);
+  return got == static_cast<size_t>(n);
+}
+
+}  // namespace
+
+int checkpoint_save(const char* path, const float* host_w, int64_t numel, const char* session,
+                    int domain, int S, int H, int D, int L) {
+  if (!path || !host_w) return fail(GLT_EINVAL, "null argument");
+  if (numel != 3LL * L * S * H) return fail(GLT_EINVAL, "weights numel %lld != 3*L*S*H", (long long)numel);
+  if (is_dir(path)) return fail(GLT_EIO, "save_safetensors: path is a directory, not a file: %s", path);
+  const std::string par = parent_of(path);
+  if (!par.empty() && !is_dir(par.c_str()))
+    return fail(GLT_EIO, "save_safetensors: parent directory does not exist: %s", par.c_str());
+  const std::string hdr = grft_header(session, domain, S, H, D, L);
+  const uint64_t pad = (8 - hdr.size() % 8) % 8;
+  const uint64_t hsize = hdr.size() + pad;
+  std::vector<uint16_t> bf(static_cast<size_t>(numel));
+  for (int64_t i = 0; i < numel; ++i) bf[static_cast<size_t>(i)] = f32_to_bf16_bits(host_w[i]);
+  FILE* f = fopen(path, "wb");
+  if (!f) return fail(GLT_EIO, "cannot open %s for writing", path);
+  const uint32_t magic = kGrftMagic;
+  const uint8_t ver = kGrftVersion;
+  bool ok = fwrite(&magic, 4, 1, f) == 1 && fwrite(&ver, 1, 1, f) == 1 &&
+            fwrite(&hsize, 8, 1, f) == 1 && fwrite(hdr.data(), 1, hdr.size(), f) == hdr.size();
+  for (uint64_t i = 0; ok && i < pad; ++i) ok = fputc(0, f) != EOF;
+  if (ok && numel) ok = fwrite(bf.data(), 2, bf.size(), f) == bf.size();
+  ok = (fclose(f) == 0) && ok;
+  if (!ok) return fail(GLT_EIO, "short write to %s", path);
+  return GLT_OK;
+}
+
+int checkpoint_load(const char* path, float* host_w, int64_t numel, int expected_domain,
+                    const char* session, int total_proj, int S, int H, int* file_domain) {
+  if (!path || !host_w) return fail(GLT_EINVAL, "null argument");
+  std::vector<char> buf;
+  if (!read_file(path, buf)) return fail(GLT_EIO, "cannot open checkpoint %s", path);
+  size_t off = 0;
+  uint32_t magic = 0;
+  if (buf.size() >= 5) memcpy(&magic, buf.data(), 4);
+  if (buf.size() >= 5 && magic == kGrftMagic) off = 5;  // GRFT magic + version byte
+  if (buf.size() < off + 8) return fail(GLT_EIO, "safetensors parse failed: file too small");
+  uint64_t hlen = 0;
+  memcpy(&hlen, buf.data() + off, 8);
+  if (hlen > buf.size() - off - 8) return fail(GLT_EIO, "safetensors parse failed: header past end of file");
+  StHeader h;
+  if (!parse_header(buf.data() + off + 8, static_cast<size_t>(hlen), h))
+    return fail(GLT_EIO, "safetensors parse failed: bad JSON header");
+  if (!h.has_tensor) return fail(GLT_EIO, "'delta_weights' not found in %s", path);
+  if (h.dtype != "BF16") return fail(GLT_EIO, "delta_weights dtype is not BF16");
+  if (h.shape.size() != 3 || h.shape[0] != total_proj || h.shape[1] != S || h.shape[2] != H)
+    return fail(GLT_EIO, "delta_weights shape mismatch. Expected [%d,%d,%d]", total_proj, S, H);
+  if (session && *session && !h.session.empty() && h.session != session)
+    return fail(GLT_EIO, "session_id mismatch! Checkpoint has '%s', current training session is '%s'",
+                h.session.c_str(), session);
+  if (h.domain != -1 && h.domain != expected_domain)
+    return fail(GLT_EIO, "checkpoint domain_id mismatch. Checkpoint has %d, current --domain-id is %d",
+                h.domain, expected_domain);
+  const int64_t n = static_cast<int64_t>(total_proj) * S * H;
+  if (numel != n) return fail(GLT_EINVAL, "destination holds %lld elements, need %lld", (long long)numel, (long long)n);
+  const uint64_t data0 = off + 8 + hlen;
+  if (h.off0 < 0 || h.off1 < h.off0 || data0 + static_cast<uint64_t>(h.off1) > buf.size() ||
+      static_cast<uint64_t>(h.off1 - h.off0) < static_cast<uint64_t>(n) * 2)
+    return fail(GLT_EIO, "truncated tensor data in %s", path);
+  const uint8_t* src = reinterpret_cast<const uint8_t*>(buf.data()) + data0 + h.off0;
+  for (int64_t i = 0; i < n; ++i) {
+    uint16_t b;
+    memcpy(&b, src + 2 * i, 2);
+    host_w[i] = bf16_bits_to_f32(b);
+  }
+  if (file_domain) *file_domain = h.domain;
+  return GLT_OK;
+}
+
+}  // namespace glt
+
+// ------------------------------- C ABI -------------------------------------
+static int copy_weights(void* dst, const void* src, int64_t bytes, int dst_host, int src_host) {
+  if (dst_host && src_host) {
+    memcpy(dst, src, static_cast<size_t>(bytes));
+    return GLT_OK;
+  }
+  GLT_CUDA_TRY(cudaMemcpy(dst, src, static_cast<size_t>(bytes), cudaMemcpyDefault));
+  return GLT_OK;
+}
+
+extern "C" int glt_checkpoint_save(const char* path, const float* weights, int64_t numel,
+                                   int src_is_host, const char* session_id, int domain_id,
+                                   int slice_dim, int h_slice_dim, int hidden_dim, int num_layers) {
+  if (!weights) return glt::fail(GLT_EINVAL, "null weights");
+  std::vector<float> host;
+  const float* hw = weights;
+  if (!src_is_host) {
+    host.resize(static_cast<size_t>(numel));
+    GLT_TRY(copy_weights(host.data(), weights, numel * 4, 1, 0));
+    hw = host.data();
+  }
+  return glt::checkpoint_save(path, hw, numel, session_id, domain_id, slice_dim, h_slice_dim,
+                              hidden_dim, num_layers);
+}
+
+extern "C" int glt_checkpoint_load(const char* path, float* weights, int64_t numel, int dst_is_host,
+                                   int expected_domain_id, const char* session_id,
+                                   int total_projections, int slice_dim, int h_slice_dim,
+                                   int* file_domain_id) {
+  if (!weights) return glt::fail(GLT_EINVAL, "null weights");
+  if (dst_is_host)
+    return glt::checkpoint_load(path, weights, numel, expected_domain_id, session_id,
+                                total_projections, slice_dim, h_slice_dim, file_domain_id);
+  std::vector<float> host(static_cast<size_t>(numel > 0 ? numel : 0));
+  GLT_TRY(glt::checkpoint_load(path, host.data(), numel, expected_domain_id, session_id,
+                               total_projections, slice_dim, h_slice_dim, file_domain_id));
+  return copy_weights(weights, host.data(), numel * 4, 0, 1);
+}
+
+extern "C" int glt_model_save_checkpoint(GltModel* m, const char* path, const char* session_id,
+                                         int domain_id) {
+  if (!m) return glt::fail(GLT_EINVAL, "null model");
+  glt::Model* mm = reinterpret_cast<glt::Model*>(m);
+  GLT_CUDA_TRY(cudaDeviceSynchronize());
+  return glt_checkpoint_save(path, mm->gw, mm->graft_numel, 0, session_id, domain_id, mm->S,
+                             mm->H, mm->D, mm->L);
+}
+
+extern "C" int glt_model_load_checkpoint(GltModel* m, const char* path, const char* session_id,
+                                         int expected_domain_id) {
+  if (!m) return glt::fail(GLT_EINVAL, "null model");
+  glt::Model* mm = reinterpret_cast<glt::Model*>(m);
+  GLT_TRY(glt_checkpoint_load(path, mm->gw, mm->graft_numel, 0, expected_domain_id, session_id,
+                              3 * mm->L, mm->S, mm->H, nullptr));
+  GLT_TRY(mm->refresh_graft(nullptr));
+  GLT_CUDA_TRY(cudaDeviceSynchronize());
+  return GLT_OK;
+}
+
+// ---------------------------- .bin + batch walk ----------------------------
+extern "C" int glt_load_bin(const char* path, int32_t* num_sequences, int32_t* seq_len,
+                            int32_t* tokens, int64_t capacity) {
+  if (!path || !num_sequences || !seq_len) return glt::fail(GLT_EINVAL, "null argument");
+  FILE* f = fopen(path, "rb");
+  if (!f) return glt::fail(GLT_EIO, "cannot open %s", path);
+  int32_t hdr[2];
+  if (fread(hdr, 4, 2, f) != 2) {
+    fclose(f);
+    return glt::fail(GLT_EIO, "failed reading header from %s", path);
+  }
+  // trust-boundary checks of load_bin (src/data_impl.inc:22-47)
+  if (hdr[0] <= 0 || hdr[1] <= 0) {
+    fclose(f);
+    return glt::fail(GLT_EIO, "invalid header in %s (num_sequences=%d, seq_len=%d)", path, hdr[0], hdr[1]);
+  }
+  const int64_t total = static_cast<int64_t>(hdr[0]) * hdr[1];
+  if (total > (1LL << 30)) {
+    fclose(f);
+    return glt::fail(GLT_EIO, "token count %lld in %s exceeds safety limit", (long long)total, path);
+  }
+  fseek(f, 0, SEEK_END);
+  const long end = ftell(f);
+  if (end - 8 < total * 4) {
+    fclose(f);
+    return glt::fail(GLT_EIO, "truncated token data in %s", path);
+  }
+  *num_sequences = hdr[0];
+  *seq_len = hdr[1];
+  if (tokens) {
+    if (capacity < total) {
+      fclose(f);
+      return glt::fail(GLT_EINVAL, "token buffer holds %lld, file has %lld", (long long)capacity, (long long)total);
+    }
+    fseek(f, 8, SEEK_SET);
+    if (fread(tokens, 4, static_cast<size_t>(total), f) != static_cast<size_t>(total)) {
+      fclose(f);
+      return glt::fail(GLT_EIO, "failed reading token data from %s", path);
+    }
+  }
+  fclose(f);
+  return GLT_OK;
+}
+
+static uint64_t mix_seed(uint64_t x) {  // grafting.hip:928-933
+  x += 0x9e3779b97f4a7c15ULL;
+  x = (x ^ (x >> 30)) * 0xbf58476d1ce4e5b9ULL;
+  x = (x ^ (x >> 27)) * 0x94d049bb133111ebULL;
+  return x ^ (x >> 31);
+}
+
+extern "C" int glt_batch_walk_start(uint64_t seed, int n_domain, int n_ood, int* domain_pos,
+                                    int* ood_pos) {
+  if (n_domain <= 0 || n_ood <= 0 || !domain_pos || !ood_pos)
+    return glt::fail(GLT_EINVAL, "bad arguments");
+  *domain_pos = static_cast<int>(mix_seed(seed) % static_cast<uint64_t>(n_domain));
+  *ood_pos = static_cast<int>(mix_seed(seed ^ 0x9e3779b97f4a7c15ULL) % static_cast<uint64_t>(n_ood));
+  return GLT_OK;
+}
+
+extern "C" int glt_batch_step(const int32_t* domain_tokens, int n_domain, const int32_t* ood_tokens,
+                              int n_ood, int seq_len, int batch_size, int* domain_pos, int* ood_pos,
+                              int32_t* ids_out, int32_t* ood_mask_out) {
+  if (!domain_tokens || !ood_tokens || !domain_pos || !ood_pos || !ids_out || !ood_mask_out)
+    return glt::fail(GLT_EINVAL, "null argument");
+  if (batch_size % 2 != 0) return glt::fail(GLT_EINVAL, "--batch-size must be even");
+  if (n_domain <= 0 || n_ood <= 0 || seq_len <= 0) return glt::fail(GLT_EINVAL, "empty corpus");
+  const int half = batch_size / 2;
+  const size_t T = static_cast<size_t>(seq_len);
+  for (int i = 0; i < half; ++i) {  // grafting.hip:965-973
+    const int ds = (*domain_pos + i) % n_domain;
+    memcpy(ids_out + i * T, domain_tokens + ds * T, T * 4);
+    memset(ood_mask_out + i * T, 0, T * 4);
+  }
+  *domain_pos = (*domain_pos + half) % n_domain;
+  for (int i = 0; i < half; ++i) {  // grafting.hip:975-983
+    const int os = (*ood_pos + i) % n_ood;
+    memcpy(ids_out + (half + i) * T, ood_tokens + os * T, T * 4);
+    for (size_t k = 0; k < T; ++k) ood_mask_out[(half + i) * T + k] = 1;
+  }
+  *ood_pos = (*ood_pos + half) % n_ood;
+  return GLT_OK;
+}

@@ -20,6 +20,11 @@ from ._lib import GltModelConfig, GltStepStats, check, lib
 LAYOUT_OVERLAY, LAYOUT_CONCAT = 0, 1
 MODEL_DECODER, MODEL_MLP_BLOCK = 0, 1
 W_EMBED, W_LM_HEAD, W_FINAL_NORM, W_IN_NORM, W_Q, W_K, W_V, W_O, W_POST_NORM, W_GATE, W_UP, W_DOWN = range(12)
+# per-kind kernel timing slots (GLT_PROF_* in include/glt_graft.h)
+PROF_NAMES = ["gate_up_fwd", "down_fwd", "delta_down", "qkv", "o_proj", "attn_fwd", "dh",
+              "recompute_swiglu_bwd", "wgrad_down", "wgrad_gate_up", "dx_gate_up", "do",
+              "attn_bwd", "dx_qkv", "lm_head", "lm_dx", "cross_entropy"]
+PROF_KINDS = len(PROF_NAMES)
 
 
 @dataclass
@@ -183,9 +188,15 @@ class GraftModel:
                               _stream()))
         return logits
 
-    def block_step(self, x: torch.Tensor, y: torch.Tensor, lr: float, step: int = 0):
+    def block_step(self, x: torch.Tensor, y: torch.Tensor, lr: float, step: int = 0,
+                   outputs: bool = True):
+        """MLP-block step; with outputs=False nothing is read back (no host sync)."""
         x = x.to(device="cuda", dtype=torch.bfloat16).contiguous()
         y = y.to(device="cuda", dtype=torch.float32).contiguous()
+        if not outputs:
+            check(lib.glt_block_step(self.handle, C.c_void_p(x.data_ptr()), C.c_void_p(y.data_ptr()),
+                                     lr, step, None, None, None, _stream()))
+            return None
         out = torch.empty_like(x)
         dx = torch.empty(x.shape, dtype=torch.float32, device="cuda")
         loss = C.c_float()
@@ -193,6 +204,15 @@ class GraftModel:
                                  lr, step, C.byref(loss), C.c_void_p(out.data_ptr()),
                                  C.c_void_p(dx.data_ptr()), _stream()))
         return dict(loss=loss.value, out=out, dx=dx)
+
+    def profile(self, enable: bool) -> None:
+        check(lib.glt_model_profile(self.handle, int(enable)))
+
+    def profile_read(self, reset: bool = True) -> tuple[list[float], list[int]]:
+        ms = (C.c_double * PROF_KINDS)()
+        n = (C.c_int64 * PROF_KINDS)()
+        check(lib.glt_model_profile_read(self.handle, ms, n, int(reset)))
+        return list(ms), list(n)
 
     # --- data parallel --------------------------------------------------------
     @staticmethod

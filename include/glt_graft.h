@@ -79,6 +79,97 @@ GLT_API int glt_gemm(const void* A, int64_t lda, int a_mn, const void* B, int64_
 
 
 /* ------------------------------------------------------------------------ */
+/* Workspace for the stand-alone graft ops (the reference's arena scratch,  */
+/* arena.d_bf16_temp, src/arena_impl.inc:14-126).                           */
+/* ------------------------------------------------------------------------ */
+typedef struct GltArena GltArena;
+GLT_API int glt_arena_create(int64_t scratch_bytes, GltArena** out);
+GLT_API int glt_arena_destroy(GltArena* arena);
+
+/* ------------------------------------------------------------------------ */
+/* The six graft GEMMs in general (overlay) geometry, one tcgen05 kernel.   */
+/* W is one projection's delta in storage orientation [S, H] row-major:     */
+/* fp32 (w_f32, rounded to bf16 like graft_gemm_fwd, gemm_impl.inc:398-405) */
+/* or its bf16 mirror (w_bf16, used when non-NULL).  x / dy are bf16        */
+/* (x_is_f32 / dy_is_f32 = 0) or fp32 (rounded to bf16 first, as           */
+/* grad_gemm does with dy, gemm_impl.inc:455, 525), with row strides in     */
+/* elements; out is fp32: out = alpha * (product) + beta * out.  Operands   */
+/* TMA cannot read in place are packed into `arena` (GLT_ENOMEM with the    */
+/* needed size if it is too small).                                         */
+/*   EXPAND_FWD     out[M,S] = x_h[M,H] . W^T   execute_expand_forward      */
+/*                                                (graft_ops_impl.inc:14-24) */
+/*   CONTRACT_FWD   out[M,H] = x_i[M,S] . W     execute_contract_forward    */
+/*                                                (graft_ops_impl.inc:33-114)*/
+/*   EXPAND_WGRAD   out[S,H] = dy[M,S]^T . x_h  execute_expand_grad_gemm    */
+/*                                                (graft_ops_impl.inc:120-132)*/
+/*   CONTRACT_WGRAD out[S,H] = x_i[M,S]^T . dy[M,H]                         */
+/*                  execute_contract_backward_storage_canonical (:214-228)  */
+/*   EXPAND_DGRAD   out[M,H] = dy[M,S] . W      ExpandInputGrad             */
+/*                  (layer_backward_impl.inc:277-342; this is the math of   */
+/*                  docs/test_contract_audit.py op 3 and of the reference's */
+/*                  ATen path)                                              */
+/*   CONTRACT_DGRAD out[M,S] = dy_h[M,H] . W^T  ContractInputGrad           */
+/*                  (layer_backward_impl.inc:117-155)                       */
+/* ------------------------------------------------------------------------ */
+#define GLT_GRAFT_EXPAND_FWD 0
+#define GLT_GRAFT_CONTRACT_FWD 1
+#define GLT_GRAFT_EXPAND_WGRAD 2
+#define GLT_GRAFT_CONTRACT_WGRAD 3
+#define GLT_GRAFT_EXPAND_DGRAD 4
+#define GLT_GRAFT_CONTRACT_DGRAD 5
+GLT_API int glt_graft_op(int op, int M, int S, int H, const float* w_f32, const uint16_t* w_bf16,
+                         const void* x, int x_is_f32, int64_t x_stride, const void* dy,
+                         int dy_is_f32, int64_t dy_stride, float* out, int64_t out_stride,
+                         float alpha, float beta, GltArena* arena, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Shadow bake (src/shadow_bake_impl.inc:15-128).                           */
+/* glt_shadow_bake: one projection, in place, bit-exact with the reference: */
+/*   mode 0 (expand):   base[i0+s, h0+h] = bf16(base + graft[s,h])          */
+/*   mode 1 (contract): base[h0+h, i0+s] = bf16(base + graft[s,h])          */
+/* glt_apply_graft_to_shadow: every grafted layer and projection of a model  */
+/* given per-layer device pointers (host arrays, NULL to skip a kind), the  */
+/* flat [3L,S,H] graft, and the caller's guard flag (g_shadow_baked): a    */
+/* second bake with the flag set returns GLT_ESTATE.  Synchronises.         */
+/* ------------------------------------------------------------------------ */
+GLT_API int glt_shadow_bake(uint16_t* base, int64_t base_stride, const float* graft, int S, int H,
+                            int i0, int h0, int mode, void* stream);
+/* (declared after GltModelConfig below) */
+
+/* ------------------------------------------------------------------------ */
+/* Layer kernels for callers that run their own layer loop.                 */
+/* qkv: packed rows [q heads | k heads | v heads] of B*T tokens (ld_qkv     */
+/* elements per row), bf16; o / dout: [B*T, nh*hd] rows with ld_o; lse:     */
+/* [B, nh, T] fp32 natural-log sum-exp of the scaled scores.               */
+/* Attention = causal GQA SDPA (layer_forward_impl.inc:41-49; K/V heads     */
+/* indexed, not repeat_interleave'd); backward = attention_bwd_autograd's  */
+/* gradient (attention_autograd_impl.inc:1-39) into dqkv (same packing),   */
+/* with fp32 workspaces dq_acc [B*T, nh*hd] and dsum [B*nh*T].             */
+/* impl: GLT_ATTN_TCGEN05 (tcgen05/TMEM kernel, seq_len % 128 == 0) or      */
+/* GLT_ATTN_MMA_SYNC (seq_len % 64 == 0).  hd: 64 or 128.                   */
+/* RoPE: half-split rotation in place on q and k (rope_impl.inc:8-64);      */
+/* inverse = 1 applies the transpose (its backward).                        */
+/* RMSNorm: rms_norm_fwd_kernel / rms_norm_bwd_kernel                       */
+/* (kernels_rmsnorm_kernels.inc:8-126); bwd adds resid (may be NULL).       */
+/* ------------------------------------------------------------------------ */
+#define GLT_ATTN_TCGEN05 0
+#define GLT_ATTN_MMA_SYNC 1
+GLT_API int glt_attention_fwd(const uint16_t* qkv, int64_t ld_qkv, uint16_t* o, int64_t ld_o,
+                              float* lse, int B, int T, int nh, int nkv, int hd, int impl,
+                              void* stream);
+GLT_API int glt_attention_bwd(const uint16_t* qkv, int64_t ld_qkv, const uint16_t* o,
+                              const uint16_t* dout, int64_t ld_o, const float* lse, uint16_t* dqkv,
+                              float* dq_acc, float* dsum, int B, int T, int nh, int nkv, int hd,
+                              void* stream);
+GLT_API int glt_rope(uint16_t* qkv, int64_t ld_qkv, int B, int T, int nh, int nkv, int hd,
+                     float theta, int inverse, void* stream);
+GLT_API int glt_rmsnorm_fwd(const uint16_t* x, const uint16_t* w, uint16_t* y, float* var, int M,
+                            int D, float eps, void* stream);
+GLT_API int glt_rmsnorm_bwd(const float* dy, const uint16_t* x, const uint16_t* w,
+                            const float* var, const float* resid, float* dx, int M, int D,
+                            float eps, void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* Configuration                                                            */
 /* Mirrors GraftConfig (src/config.hpp:40-91) plus the CLI-level values of  */
 /* grafting.hip:274-292.  layout selects the graft geometry:                */
@@ -115,6 +206,12 @@ GLT_API int glt_config_validate(const GltModelConfig* cfg, int batch_size, int m
 GLT_API float glt_get_lr(const GltModelConfig* cfg, int step, int total_steps);
 /* Flat offset of projection p of layer l in [3L,S,H] (src/graft_ops_impl.inc:5-7). */
 GLT_API int64_t glt_delta_offset(int layer, int proj, int slice_dim, int h_slice_dim);
+
+/* apply_graft_to_shadow (src/shadow_bake_impl.inc:58-128); see glt_shadow_bake. */
+GLT_API int glt_apply_graft_to_shadow(const GltModelConfig* cfg, uint16_t* const* gate,
+                                      uint16_t* const* up, uint16_t* const* down,
+                                      int64_t gate_up_stride, int64_t down_stride,
+                                      const float* graft, int* baked_flag, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* Model (frozen bf16 base + fp32 graft, one CUDA device per handle)        */
@@ -220,6 +317,46 @@ GLT_API int glt_model_activation(GltModel* m, int which, int layer, void** ptr, 
 #define GLT_PROF_KINDS 17
 GLT_API int glt_model_profile(GltModel* m, int enable);
 GLT_API int glt_model_profile_read(GltModel* m, double* ms, int64_t* launches, int reset);
+
+/* ------------------------------------------------------------------------ */
+/* GRFT checkpoint (src/checkpoint_impl.inc).  Bytes: u32 "GRFT" LE | u8 4  */
+/* | u64 header size (JSON NUL-padded to 8) | safetensors JSON | bf16      */
+/* delta_weights [3L,S,H] (bias-trick rounding, checkpoint_impl.inc:49-57). */
+/* save: save_safetensors (:32-89), refuses a directory or a missing parent */
+/* directory.  load: load_safetensors_checkpoint (:170-285): accepts the    */
+/* GRFT prefix or a legacy plain safetensors file, checks dtype, shape,     */
+/* session_id (when both are set) and domain_id (when present; the file's   */
+/* value is returned in *file_domain_id, -1 if missing).  Host-only when    */
+/* the weight buffers are host buffers (src_is_host / dst_is_host = 1).     */
+/* ------------------------------------------------------------------------ */
+GLT_API int glt_checkpoint_save(const char* path, const float* weights, int64_t numel,
+                                int src_is_host, const char* session_id, int domain_id,
+                                int slice_dim, int h_slice_dim, int hidden_dim, int num_layers);
+GLT_API int glt_checkpoint_load(const char* path, float* weights, int64_t numel, int dst_is_host,
+                                int expected_domain_id, const char* session_id,
+                                int total_projections, int slice_dim, int h_slice_dim,
+                                int* file_domain_id);
+/* Model-level save/load of its fp32 graft (load also refreshes the bf16 graft
+ * copies in the fused weights and leaves the Adam state untouched, like --checkpoint). */
+GLT_API int glt_model_save_checkpoint(GltModel* m, const char* path, const char* session_id,
+                                      int domain_id);
+GLT_API int glt_model_load_checkpoint(GltModel* m, const char* path, const char* session_id,
+                                      int expected_domain_id);
+
+/* ------------------------------------------------------------------------ */
+/* Token data (host).  .bin = [i32 nseq][i32 seq_len][i32 tokens...] with   */
+/* the checks of load_bin (src/data_impl.inc:9-58); tokens = NULL reads and */
+/* validates only the header.  The batch walk is grafting.hip:924-988:      */
+/* splitmix64-seeded start positions, then per step the first B/2 rows from */
+/* the domain corpus (mask 0) and the last B/2 from the OOD corpus (mask 1). */
+/* ------------------------------------------------------------------------ */
+GLT_API int glt_load_bin(const char* path, int32_t* num_sequences, int32_t* seq_len,
+                         int32_t* tokens, int64_t capacity);
+GLT_API int glt_batch_walk_start(uint64_t seed, int n_domain, int n_ood, int* domain_pos,
+                                 int* ood_pos);
+GLT_API int glt_batch_step(const int32_t* domain_tokens, int n_domain, const int32_t* ood_tokens,
+                           int n_ood, int seq_len, int batch_size, int* domain_pos, int* ood_pos,
+                           int32_t* ids_out, int32_t* ood_mask_out);
 
 /* ------------------------------------------------------------------------ */
 /* Data parallelism (new: the reference is single-GPU).  One process per   */

@@ -104,6 +104,8 @@ SIGNATURES: dict[str, tuple] = {
     "glt_arena_destroy": (_i32, [_vp]),
     "glt_graft_op": (_i32, [_i32, _i32, _i32, _i32, _vp, _vp, _vp, _i32, _i64, _vp, _i32, _i64,
                             _vp, _i64, _f32, _f32, _vp, _vp]),
+    "glt_graft_op_noalloc": (_i32, [_i32, _i32, _i32, _i32, _vp, _vp, _vp, _i32, _i64, _vp, _i32,
+                                    _i64, _vp, _i64, _f32, _f32, _vp]),
     "glt_shadow_bake": (_i32, [_vp, _i64, _vp, _i32, _i32, _i32, _i32, _i32, _vp]),
     "glt_apply_graft_to_shadow": (_i32, [_cfgp, _vp, _vp, _vp, _i64, _i64, _vp,
                                          C.POINTER(_i32), _vp]),

@@ -122,6 +122,23 @@ GLT_API int glt_graft_op(int op, int M, int S, int H, const float* w_f32, const 
                          int dy_is_f32, int64_t dy_stride, float* out, int64_t out_stride,
                          float alpha, float beta, GltArena* arena, void* stream);
 
+/* Allocation-free variant of glt_graft_op (same ops and arguments, no     */
+/* arena).  It has no counterpart in the reference.  It is for callers that */
+/* must not call cudaMalloc -- code inside a framework whose caching        */
+/* allocator owns the device memory, or latency-critical paths that cannot  */
+/* afford cudaMalloc's implicit device synchronisation.  Operands that need */
+/* staging go to a fixed 16 MiB workspace compiled into the library (held  */
+/* by every GPU that loads it until exit); larger staging needs return      */
+/* GLT_EINVAL.  The first call on a device looks up the workspace address   */
+/* (cudaGetSymbolAddress) and should come before any stream capture.  All   */
+/* calls on a device share the workspace: calls that may overlap on the GPU */
+/* race and must be serialised by the caller.                               */
+GLT_API int glt_graft_op_noalloc(int op, int M, int S, int H, const float* w_f32,
+                                 const uint16_t* w_bf16, const void* x, int x_is_f32,
+                                 int64_t x_stride, const void* dy, int dy_is_f32,
+                                 int64_t dy_stride, float* out, int64_t out_stride, float alpha,
+                                 float beta, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Shadow bake (src/shadow_bake_impl.inc:15-128).                           */
 /* glt_shadow_bake: one projection, in place, bit-exact with the reference: */

@@ -96,7 +96,7 @@ SIGNATURES: dict[str, tuple] = {
     "glt_model_profile_read": (_i32, [_vp, C.POINTER(C.c_double), C.POINTER(_i64), _i32]),
     "glt_attention_fwd": (_i32, [_vp, _i64, _vp, _i64, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _vp]),
     "glt_attention_bwd": (_i32, [_vp, _i64, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _i32, _i32, _i32,
-                                 _i32, _i32, _vp]),
+                                 _i32, _i32, _i32, _vp]),
     "glt_rope": (_i32, [_vp, _i64, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _vp]),
     "glt_rmsnorm_fwd": (_i32, [_vp, _vp, _vp, _vp, _i32, _i32, _f32, _vp]),
     "glt_rmsnorm_bwd": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _f32, _vp]),

@@ -507,28 +507,38 @@ int fwd_impl(const uint16_t* qkv, uint16_t* o, float* lse, const AttnShape& s, c
 }
 
 template <int HD>
-int bwd_impl(const uint16_t* qkv, const uint16_t* o, const uint16_t* dout, const float* lse,
-             uint16_t* dqkv, float* dq_acc, float* dsum, const AttnShape& s, cudaStream_t st) {
+int bwd_prep_impl(const uint16_t* o, const uint16_t* dout, float* dq_acc, float* dsum,
+                  const AttnShape& s, cudaStream_t st) {
   const int64_t M = static_cast<int64_t>(s.B) * s.T;
   GLT_CUDA_TRY(cudaMemsetAsync(dq_acc, 0, M * s.nh * HD * sizeof(float), st));
-  {
-    const int64_t warps = M * s.nh;
-    const int blocks = static_cast<int>((warps * 32 + 255) / 256);
-    bwd_dsum_kernel<HD><<<blocks, 256, 0, st>>>(o, dout, dsum, s);
-    GLT_LAUNCH_CHECK();
-  }
+  const int64_t warps = M * s.nh;
+  const int blocks = static_cast<int>((warps * 32 + 255) / 256);
+  bwd_dsum_kernel<HD><<<blocks, 256, 0, st>>>(o, dout, dsum, s);
+  GLT_LAUNCH_CHECK();
+  return GLT_OK;
+}
+
+int bwd_finish_impl(const float* dq_acc, uint16_t* dqkv, const AttnShape& s, cudaStream_t st) {
+  const int64_t M = static_cast<int64_t>(s.B) * s.T;
+  const int64_t n = M * s.nh * s.hd / 4;
+  int blocks = static_cast<int>((n + 255) / 256);
+  if (blocks > num_sms() * 16) blocks = num_sms() * 16;
+  dq_convert_kernel<<<blocks, 256, 0, st>>>(dq_acc, dqkv, M, s.nh * s.hd, s.ld_qkv);
+  GLT_LAUNCH_CHECK();
+  return GLT_OK;
+}
+
+template <int HD>
+int bwd_impl(const uint16_t* qkv, const uint16_t* o, const uint16_t* dout, const float* lse,
+             uint16_t* dqkv, float* dq_acc, float* dsum, const AttnShape& s, cudaStream_t st) {
+  GLT_TRY(bwd_prep_impl<HD>(o, dout, dq_acc, dsum, s, st));
   const int smem = 6 * 64 * HD * 2 + 64 * 64 * 2 + 4 * 64 * 4;
   auto k = flash_bwd_kernel<HD>;
   GLT_TRY(ensure_smem_attr(reinterpret_cast<const void*>(k), smem));
   dim3 grid(s.T / 64, s.nkv, s.B);
   k<<<grid, 128, smem, st>>>(qkv, dout, lse, dsum, dqkv, dq_acc, s);
   GLT_LAUNCH_CHECK();
-  const int64_t n = M * s.nh * HD / 4;
-  int blocks = static_cast<int>((n + 255) / 256);
-  if (blocks > num_sms() * 16) blocks = num_sms() * 16;
-  dq_convert_kernel<<<blocks, 256, 0, st>>>(dq_acc, dqkv, M, s.nh * HD, s.ld_qkv);
-  GLT_LAUNCH_CHECK();
-  return GLT_OK;
+  return bwd_finish_impl(dq_acc, dqkv, s, st);
 }
 
 int check_shape(const AttnShape& s) {
@@ -558,6 +568,17 @@ int rope_apply(uint16_t* qkv, const AttnShape& s, const float* cos_t, const floa
 int flash_fwd(const uint16_t* qkv, uint16_t* o, float* lse, const AttnShape& s, cudaStream_t st) {
   GLT_TRY(check_shape(s));
   return s.hd == 128 ? fwd_impl<128>(qkv, o, lse, s, st) : fwd_impl<64>(qkv, o, lse, s, st);
+}
+
+int attn_bwd_prep(const uint16_t* o, const uint16_t* dout, float* dq_acc, float* dsum,
+                  const AttnShape& s, cudaStream_t st) {
+  GLT_TRY(check_shape(s));
+  return s.hd == 128 ? bwd_prep_impl<128>(o, dout, dq_acc, dsum, s, st)
+                     : bwd_prep_impl<64>(o, dout, dq_acc, dsum, s, st);
+}
+
+int attn_bwd_finish(const float* dq_acc, uint16_t* dqkv, const AttnShape& s, cudaStream_t st) {
+  return bwd_finish_impl(dq_acc, dqkv, s, st);
 }
 
 int flash_bwd(const uint16_t* qkv, const uint16_t* o, const uint16_t* dout, const float* lse,

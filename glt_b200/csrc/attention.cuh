@@ -23,11 +23,23 @@ int rope_apply(uint16_t* qkv, const AttnShape& s, const float* cos_t, const floa
                int inverse, int apply_q, int apply_k, cudaStream_t st);
 
 // O = softmax(Q K^T * scale, causal) V, lse = logsumexp per (b, h, t).
+// flash_fwd: mma.sync kernel (seq_len % 64 == 0); flash_fwd_tc: tcgen05/TMEM
+// kernel (attention_tc.cu, seq_len % 128 == 0).  Same outputs.
 int flash_fwd(const uint16_t* qkv, uint16_t* o, float* lse, const AttnShape& s, cudaStream_t st);
+int flash_fwd_tc(const uint16_t* qkv, uint16_t* o, float* lse, const AttnShape& s, cudaStream_t st);
 
 // Backward: dqkv (bf16, same packing as qkv) from dO, O, lse.  Needs fp32
 // workspaces dq_acc [B*T, nh*hd] and dsum [B*nh*T].
 int flash_bwd(const uint16_t* qkv, const uint16_t* o, const uint16_t* dout, const float* lse,
               uint16_t* dqkv, float* dq_acc, float* dsum, const AttnShape& s, cudaStream_t st);
+// tcgen05/TMEM backward (attention_tc.cu; hd 128, seq_len % 128 == 0); same
+// contract as flash_bwd.
+int flash_bwd_tc(const uint16_t* qkv, const uint16_t* o, const uint16_t* dout, const float* lse,
+                 uint16_t* dqkv, float* dq_acc, float* dsum, const AttnShape& s, cudaStream_t st);
+// Shared pre/post steps of both backward kernels: zero dq_acc and compute
+// dsum = rowsum(dO * O); convert dq_acc (fp32) into the q columns of dqkv.
+int attn_bwd_prep(const uint16_t* o, const uint16_t* dout, float* dq_acc, float* dsum,
+                  const AttnShape& s, cudaStream_t st);
+int attn_bwd_finish(const float* dq_acc, uint16_t* dqkv, const AttnShape& s, cudaStream_t st);
 
 }  // namespace glt

@@ -337,7 +337,365 @@ int launch_fwd_tc(const uint16_t* qkv, uint16_t* o, float* lse, const AttnShape&
   return GLT_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Backward.  One CTA per (128-key tile, kv head, batch) loops over the GQA
+// query heads and the causal 64-query tiles ("items").  Per item, with the
+// key tile's K and V resident in smem and Q/dO double-buffered:
+//   S^T  = K . Q^T      dP^T = V . dO^T          (M=128 keys, N=64 q, K=128)
+//   compute warps (thread = key row): P^T = exp2(S^T*scale*log2e - lse),
+//     dS^T = P^T (dP^T - rowsum(dO*O)); both written bf16 to smem tiles
+//   dV  += P^T . dO     dK  += dS^T . Q          (M=128 keys, N=128 d, K=64)
+//   dQ^T = K^T . dS^T                            (M=128 d, N=64 q, K=128)
+// dV/dK accumulate in TMEM across items; dQ^T is read per item, staged in
+// smem as a [64 q][128 d] fp32 tile and added into the global fp32 dQ
+// accumulator with one TMA bulk reduce-add (no per-element atomics).
+// TMEM: S^T 64 | dP^T 64 | dV 128 | dK 128 | dQ^T 64 = 448 of 512 columns.
+// ---------------------------------------------------------------------------
+constexpr int BK_KEYS = 128;  // keys per CTA
+constexpr int BQ = 64;        // queries per item
+
+struct BwdSmem {
+  static constexpr uint32_t KV_BYTES = BK_KEYS * 128 * 2;  // [128 keys][128 d] = 2 blocks x 16 KB
+  static constexpr uint32_t QD_BYTES = BQ * 128 * 2;       // [64 q][128 d] = 2 blocks x 8 KB
+  static constexpr uint32_t T_BYTES = BK_KEYS * BQ * 2;    // [128 keys][64 q] bf16
+  static constexpr uint32_t DQ_BYTES = BQ * 128 * 4;       // [64 q][128 d] fp32
+  static constexpr uint32_t OFF_K = 0;
+  static constexpr uint32_t OFF_V = OFF_K + KV_BYTES;
+  static constexpr uint32_t OFF_Q = OFF_V + KV_BYTES;       // [2]
+  static constexpr uint32_t OFF_DO = OFF_Q + 2 * QD_BYTES;  // [2]
+  static constexpr uint32_t OFF_P = OFF_DO + 2 * QD_BYTES;
+  static constexpr uint32_t OFF_DS = OFF_P + T_BYTES;
+  static constexpr uint32_t OFF_DQ = OFF_DS + T_BYTES;
+  static constexpr uint32_t OFF_LSE = OFF_DQ + DQ_BYTES;    // [2][64] lse*log2e, [2][64] dsum
+  static constexpr uint32_t OFF_BAR = OFF_LSE + 4 * BQ * 4;
+  static constexpr uint32_t NUM_BARS = 1 + 2 + 2 + 1 + 1 + 1 + 1 + 1 + 1 + 1;
+  static constexpr uint32_t TOTAL = 1024 + OFF_BAR + NUM_BARS * 8 + 16;
+};
+
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* tm, uint32_t src, int c0,
+                                                  int c1) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(tm)),
+      "r"(src), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Bounded group barrier of the 128 compute threads on an mbarrier (count 128).
+__device__ __forceinline__ bool group_sync(uint64_t* bar, uint32_t& phase, unsigned int* err) {
+  mbar_arrive(bar);
+  const bool ok = mbar_wait(bar, phase, err);
+  phase ^= 1u;
+  return ok;
+}
+
+__global__ void __launch_bounds__(192, 1)
+    attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_k,
+                       const __grid_constant__ CUtensorMap tm_q,
+                       const __grid_constant__ CUtensorMap tm_do,
+                       const __grid_constant__ CUtensorMap tm_dq, const float* __restrict__ lse,
+                       const float* __restrict__ dsum, uint16_t* __restrict__ dqkv, AttnShape s,
+                       unsigned int* err) {
+  using L = BwdSmem;
+  constexpr int HD = 128;
+  constexpr uint32_t TMEM_COLS = 512;
+  constexpr uint32_t COL_S = 0, COL_DP = 64, COL_DV = 128, COL_DK = 256, COL_DQ = 384;
+  constexpr uint32_t ID_SDP = make_idesc(BQ, false, false);   // M=128, N=64, K-major x K-major
+  constexpr uint32_t ID_DVK = make_idesc(HD, false, true);    // M=128, N=128, A K-major, B MN-major
+  constexpr uint32_t ID_DQ = make_idesc(BQ, true, true);      // M=128, N=64,  A MN, B MN
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::OFF_BAR);
+  uint64_t* kv_full = bars;
+  uint64_t* qd_full = kv_full + 1;   // [2]
+  uint64_t* qd_empty = qd_full + 2;  // [2]
+  uint64_t* sdp_full = qd_empty + 2;
+  uint64_t* sdp_free = sdp_full + 1;
+  uint64_t* p_full = sdp_free + 1;
+  uint64_t* mm_done = p_full + 1;
+  uint64_t* dq_free = mm_done + 1;
+  uint64_t* gbar = dq_free + 1;      // compute-group barrier
+  uint64_t* drain = gbar + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  float* s_lse = reinterpret_cast<float*>(sm + L::OFF_LSE);   // [2][64]
+  float* s_dsum = s_lse + 2 * BQ;                              // [2][64]
+  __shared__ int abort_flag;
+  volatile int& s_abort = abort_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kt = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int rep = s.nh / s.nkv;
+  const int q_first = kt * (BK_KEYS / BQ);                 // first causal query tile
+  const int per_head = s.T / BQ - q_first;
+  const int n_items = rep * per_head;
+  const int row0 = b * s.T;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int i = 0; i < 2; ++i) { mbar_init(&qd_full[i], 1); mbar_init(&qd_empty[i], 1); }
+    mbar_init(sdp_full, 1);
+    mbar_init(sdp_free, 4);
+    mbar_init(p_full, 4);
+    mbar_init(mm_done, 1);
+    mbar_init(dq_free, 4);
+    mbar_init(gbar, 128);
+    mbar_init(drain, 1);
+    s_abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_do);
+    tma_prefetch_desc(&tm_dq);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t sK = smem_u32(sm + L::OFF_K), sV = smem_u32(sm + L::OFF_V);
+  const uint32_t sQ = smem_u32(sm + L::OFF_Q), sDO = smem_u32(sm + L::OFF_DO);
+  const uint32_t sP = smem_u32(sm + L::OFF_P), sDS = smem_u32(sm + L::OFF_DS);
+  const uint32_t sDQ = smem_u32(sm + L::OFF_DQ);
+
+  if (warp == 0) {
+    // ------------------------------ producer ------------------------------
+    if (lane == 0) {
+      const int kcol = (s.nh + kvh) * HD, vcol = (s.nh + s.nkv + kvh) * HD;
+      mbar_arrive_expect_tx(kv_full, 2 * L::KV_BYTES);
+      for (int c = 0; c < 2; ++c) {
+        tma_load_2d(sm + L::OFF_K + c * (BK_KEYS * 128), &tm_k, kv_full, kcol + 64 * c, row0 + kt * BK_KEYS);
+        tma_load_2d(sm + L::OFF_V + c * (BK_KEYS * 128), &tm_k, kv_full, vcol + 64 * c, row0 + kt * BK_KEYS);
+      }
+      for (int i = 0; i < n_items && !s_abort; ++i) {
+        const int st = i & 1;
+        const int h = kvh * rep + i / per_head, qt = q_first + i % per_head;
+        if (!mbar_wait(&qd_empty[st], ((i >> 1) & 1) ^ 1, err)) { s_abort = 1; break; }
+        mbar_arrive_expect_tx(&qd_full[st], 2 * L::QD_BYTES);
+        for (int c = 0; c < 2; ++c) {
+          tma_load_2d(sm + L::OFF_Q + st * L::QD_BYTES + c * (BQ * 128), &tm_q, &qd_full[st],
+                      h * HD + 64 * c, row0 + qt * BQ);
+          tma_load_2d(sm + L::OFF_DO + st * L::QD_BYTES + c * (BQ * 128), &tm_do, &qd_full[st],
+                      h * HD + 64 * c, row0 + qt * BQ);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer ----------------------------
+    if (lane == 0) {
+      bool ok = mbar_wait(kv_full, 0, err);
+      for (int i = 0; ok && i < n_items; ++i) {
+        const int st = i & 1;
+        if (!mbar_wait(&qd_full[st], (i >> 1) & 1, err) || !mbar_wait(sdp_free, (i & 1) ^ 1, err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t qb = sQ + st * L::QD_BYTES, db = sDO + st * L::QD_BYTES;
+#pragma unroll
+        for (int k = 0; k < HD / 16; ++k) {
+          umma_bf16(tmem + COL_S, desc_kmajor(sK + (k >> 2) * (BK_KEYS * 128), k & 3),
+                    desc_kmajor(qb + (k >> 2) * (BQ * 128), k & 3), ID_SDP, k > 0);
+        }
+#pragma unroll
+        for (int k = 0; k < HD / 16; ++k) {
+          umma_bf16(tmem + COL_DP, desc_kmajor(sV + (k >> 2) * (BK_KEYS * 128), k & 3),
+                    desc_kmajor(db + (k >> 2) * (BQ * 128), k & 3), ID_SDP, k > 0);
+        }
+        umma_commit(sdp_full);
+        if (!mbar_wait(p_full, i & 1, err) || !mbar_wait(dq_free, (i & 1) ^ 1, err)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < BQ / 16; ++k) {
+          umma_bf16(tmem + COL_DV, desc_kmajor(sP, k), desc_mnmajor(db, k), ID_DVK, (i > 0 || k > 0));
+          umma_bf16(tmem + COL_DK, desc_kmajor(sDS, k), desc_mnmajor(qb, k), ID_DVK, (i > 0 || k > 0));
+        }
+        // dQ^T = K^T . dS^T: A = K tile read MN-major (d contiguous, 16 KB between d blocks),
+        // B = dS^T tile read MN-major (q contiguous)
+#pragma unroll
+        for (int k = 0; k < BK_KEYS / 16; ++k) {
+          umma_bf16(tmem + COL_DQ, make_sdesc(sK + k * (UMMA_K * 128), BK_KEYS * 128, 1024),
+                    make_sdesc(sDS + k * (UMMA_K * 128), 8192, 1024), ID_DQ, k > 0);
+        }
+        umma_commit(mm_done);
+        umma_commit(&qd_empty[st]);
+      }
+      if (!ok) s_abort = 1;
+    }
+  } else {
+    // ------------------------------- compute ------------------------------
+    const int sub = warp & 3;
+    const int r = sub * 32 + lane;                  // key row (TMEM lane); for dQ^T: d index
+    const int tid = threadIdx.x - 64;               // 0..127
+    const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
+    const float sl2 = s.scale * LOG2E_F;
+    const int key = kt * BK_KEYS + r;
+    uint32_t gphase = 0;
+    bool ok = true;
+    for (int i = 0; i < n_items; ++i) {
+      const int h = kvh * rep + i / per_head, qt = q_first + i % per_head;
+      const int pb = i & 1;
+      if (tid < BQ) {
+        const int64_t li = (static_cast<int64_t>(b) * s.nh + h) * s.T + qt * BQ + tid;
+        s_lse[pb * BQ + tid] = lse[li] * LOG2E_F;
+        s_dsum[pb * BQ + tid] = dsum[li];
+      }
+      if (!group_sync(gbar, gphase, err)) { ok = false; break; }
+      if (!mbar_wait(sdp_full, i & 1, err)) { ok = false; break; }
+      tc_fence_after();
+      float sv[BQ], dp[BQ];
+      {
+        float t[32];
+        tmem_ld32(tmem + lane_off + COL_S, t);
+#pragma unroll
+        for (int c = 0; c < 32; ++c) sv[c] = t[c];
+        tmem_ld32(tmem + lane_off + COL_S + 32, t);
+#pragma unroll
+        for (int c = 0; c < 32; ++c) sv[32 + c] = t[c];
+        tmem_ld32(tmem + lane_off + COL_DP, t);
+#pragma unroll
+        for (int c = 0; c < 32; ++c) dp[c] = t[c];
+        tmem_ld32(tmem + lane_off + COL_DP + 32, t);
+#pragma unroll
+        for (int c = 0; c < 32; ++c) dp[32 + c] = t[c];
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(sdp_free);
+      const bool diag = qt * BQ < (kt + 1) * BK_KEYS;
+      const float* ls = s_lse + pb * BQ;
+      const float* dsv = s_dsum + pb * BQ;
+#pragma unroll
+      for (int c = 0; c < BQ; ++c) {
+        float p = exp2f(sv[c] * sl2 - ls[c]);
+        if (diag && key > qt * BQ + c) p = 0.f;
+        sv[c] = p;
+        dp[c] = p * (dp[c] - dsv[c]);
+      }
+      // P^T and dS^T rows -> 128-byte swizzled smem rows (the tiles of the
+      // previous item are free: its mm_done was waited below)
+#pragma unroll
+      for (int c = 0; c < BQ / 8; ++c) {
+        const uint32_t off = r * 128 + ((c ^ (r & 7)) << 4);
+        asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(sP + off),
+                     "r"(pack_bf16x2(sv[8 * c], sv[8 * c + 1])), "r"(pack_bf16x2(sv[8 * c + 2], sv[8 * c + 3])),
+                     "r"(pack_bf16x2(sv[8 * c + 4], sv[8 * c + 5])), "r"(pack_bf16x2(sv[8 * c + 6], sv[8 * c + 7]))
+                     : "memory");
+        asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(sDS + off),
+                     "r"(pack_bf16x2(dp[8 * c], dp[8 * c + 1])), "r"(pack_bf16x2(dp[8 * c + 2], dp[8 * c + 3])),
+                     "r"(pack_bf16x2(dp[8 * c + 4], dp[8 * c + 5])), "r"(pack_bf16x2(dp[8 * c + 6], dp[8 * c + 7]))
+                     : "memory");
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+      if (!mbar_wait(mm_done, i & 1, err)) { ok = false; break; }
+      tc_fence_after();
+      // dQ^T row (this thread's d) -> smem [q][d] fp32 -> TMA reduce-add into dq_acc
+      if (tid == 0) bulk_wait_read0();              // previous reduce has read the smem tile
+      if (!group_sync(gbar, gphase, err)) { ok = false; break; }
+      float* dq_s = reinterpret_cast<float*>(sm + L::OFF_DQ);
+#pragma unroll 1
+      for (int c0 = 0; c0 < BQ; c0 += 32) {
+        float t[32];
+        tmem_ld32(tmem + lane_off + COL_DQ + c0, t);
+#pragma unroll
+        for (int c = 0; c < 32; ++c) dq_s[(c0 + c) * HD + r] = t[c] * s.scale;
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_free);
+      fence_proxy_async_smem();
+      if (!group_sync(gbar, gphase, err)) { ok = false; break; }
+      if (tid == 0) {
+        tma_reduce_add_2d(&tm_dq, sDQ, h * HD, row0 + qt * BQ);
+        bulk_commit();
+      }
+    }
+    if (ok && n_items > 0) {
+      // dK (scaled) and dV rows of this CTA's keys
+      uint16_t* krow = dqkv + static_cast<int64_t>(row0 + key) * s.ld_qkv + (s.nh + kvh) * HD;
+      uint16_t* vrow = dqkv + static_cast<int64_t>(row0 + key) * s.ld_qkv + (s.nh + s.nkv + kvh) * HD;
+#pragma unroll 1
+      for (int c0 = 0; c0 < HD; c0 += 32) {
+        float t[32];
+        tmem_ld32(tmem + lane_off + COL_DV + c0, t);
+#pragma unroll
+        for (int c = 0; c < 32; c += 8) {
+          uint4 w;
+          w.x = pack_bf16x2(t[c], t[c + 1]); w.y = pack_bf16x2(t[c + 2], t[c + 3]);
+          w.z = pack_bf16x2(t[c + 4], t[c + 5]); w.w = pack_bf16x2(t[c + 6], t[c + 7]);
+          *reinterpret_cast<uint4*>(vrow + c0 + c) = w;
+        }
+        tmem_ld32(tmem + lane_off + COL_DK + c0, t);
+#pragma unroll
+        for (int c = 0; c < 32; c += 8) {
+          uint4 w;
+          w.x = pack_bf16x2(t[c] * s.scale, t[c + 1] * s.scale);
+          w.y = pack_bf16x2(t[c + 2] * s.scale, t[c + 3] * s.scale);
+          w.z = pack_bf16x2(t[c + 4] * s.scale, t[c + 5] * s.scale);
+          w.w = pack_bf16x2(t[c + 6] * s.scale, t[c + 7] * s.scale);
+          *reinterpret_cast<uint4*>(krow + c0 + c) = w;
+        }
+      }
+    }
+    if (!ok) s_abort = 1;
+    if (tid == 0) bulk_wait0();   // all reduce-adds complete before the CTA exits
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    if (s_abort) {
+      if (lane == 0) {
+        umma_commit(drain);
+        mbar_wait(drain, 0, err);
+      }
+      __syncwarp();
+    }
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
 }  // namespace
+
+int flash_bwd_tc(const uint16_t* qkv, const uint16_t* o, const uint16_t* dout, const float* lse,
+                 uint16_t* dqkv, float* dq_acc, float* dsum, const AttnShape& s, cudaStream_t st) {
+  if (s.hd != 128) return fail(GLT_EINVAL, "attention backward (tcgen05): head_dim must be 128");
+  if (s.T % BK_KEYS) return fail(GLT_EINVAL, "attention backward (tcgen05): seq_len %% 128 != 0");
+  if (s.nkv <= 0 || s.nh % s.nkv) return fail(GLT_EINVAL, "attention: nh %% nkv != 0");
+  if (s.ld_qkv % 8 || s.ld_o % 8) return fail(GLT_EINVAL, "attention: strides not 16-byte");
+  GLT_TRY(attn_bwd_prep(o, dout, dq_acc, dsum, s, st));
+  const int64_t M = static_cast<int64_t>(s.B) * s.T;
+  CUtensorMap tk, tq, tdo, tdq;
+  GLT_TRY(make_tmap_bf16(&tk, qkv, s.ld_qkv, M, s.ld_qkv, BK_KEYS));
+  GLT_TRY(make_tmap_bf16(&tq, qkv, s.ld_qkv, M, s.ld_qkv, BQ));
+  GLT_TRY(make_tmap_bf16(&tdo, dout, s.ld_o, M, s.ld_o, BQ));
+  GLT_TRY(make_tmap_f32_plain(&tdq, dq_acc, static_cast<uint64_t>(s.nh) * s.hd, M,
+                              static_cast<uint64_t>(s.nh) * s.hd, 128, BQ));
+  constexpr int smem = BwdSmem::TOTAL;
+  GLT_TRY(ensure_smem_attr(reinterpret_cast<const void*>(attn_bwd_tc_kernel), smem));
+  dim3 grid(s.T / BK_KEYS, s.nkv, s.B);
+  attn_bwd_tc_kernel<<<grid, 192, smem, st>>>(tk, tq, tdo, tdq, lse, dsum, dqkv, s,
+                                              device_error_word());
+  GLT_LAUNCH_CHECK();
+  return attn_bwd_finish(dq_acc, dqkv, s, st);
+}
 
 int flash_fwd_tc(const uint16_t* qkv, uint16_t* o, float* lse, const AttnShape& s,
                  cudaStream_t st) {

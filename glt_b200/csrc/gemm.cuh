@@ -19,6 +19,10 @@ struct Operand {
 //   dims {inner, outer}, row stride `ld` elements, box {64, box_outer}.
 int make_tmap_bf16(CUtensorMap* tm, const void* base, uint64_t inner, uint64_t outer,
                    uint64_t ld, uint32_t box_outer);
+// 2-D fp32 tensor map without swizzle (dims {inner, outer}, row stride ld
+// elements, box {box_inner, box_outer}); used for TMA reduce-add stores.
+int make_tmap_f32_plain(CUtensorMap* tm, const void* base, uint64_t inner, uint64_t outer,
+                        uint64_t ld, uint32_t box_inner, uint32_t box_outer);
 
 int num_sms();
 // Sets the dynamic-smem attribute of `func` to `bytes` once per process.

@@ -566,7 +566,11 @@ int Model::forward_layer(int l, bool use_graft, cudaStream_t st) {
   GLT_TRY(rmsnorm_fwd(xs[l], y.in_norm, xn, y.var1, M, D, cfg.rms_norm_eps, st));
   GLT_PROF(GLT_PROF_QKV, g_bf16(kmaj(xn, D), kmaj(y.wqkv, D), M, QKV, D, y.qkv, QKV, nullptr, 0, st));
   if (rope_on(l)) GLT_TRY(rope_apply(y.qkv, as, cos_t, sin_t, 0, 1, 1, st));
-  GLT_PROF(GLT_PROF_ATTN_FWD, flash_fwd(y.qkv, y.o, y.lse, as, st));
+  // tcgen05/TMEM kernel for 128-token tiles; the mma.sync kernel covers seq_len % 128 != 0
+  if (T % 128 == 0)
+    GLT_PROF(GLT_PROF_ATTN_FWD, flash_fwd_tc(y.qkv, y.o, y.lse, as, st));
+  else
+    GLT_PROF(GLT_PROF_ATTN_FWD, flash_fwd(y.qkv, y.o, y.lse, as, st));
   GLT_PROF(GLT_PROF_OPROJ, g_bf16(kmaj(y.o, AD), kmaj(y.wo, AD), M, D, AD, y.x_post, D, xs[l], D, st));
   return ffn_forward(l, y.x_post, xs[l + 1], y.var2, use_graft, st);
 }
@@ -628,7 +632,10 @@ int Model::backward_layer(int l, cudaStream_t st) {
   GLT_TRY(rmsnorm_bwd(dtmp, y.x_post, y.post_norm, y.var2, dx, dx, dy_b, M, D, cfg.rms_norm_eps, st));
   // attention: do = dx_post . Wo ; flash backward ; RoPE^T ; dxn = dqkv . Wqkv
   GLT_PROF(GLT_PROF_DO, g_bf16(kmaj(dy_b, D), mnmaj(y.wo, AD), M, AD, D, dout_b, AD, nullptr, 0, st));
-  GLT_PROF(GLT_PROF_ATTN_BWD, flash_bwd(y.qkv, y.o, dout_b, y.lse, dqkv, dq_acc, dsum, as, st));
+  if (hd == 128 && T % 128 == 0)
+    GLT_PROF(GLT_PROF_ATTN_BWD, flash_bwd_tc(y.qkv, y.o, dout_b, y.lse, dqkv, dq_acc, dsum, as, st));
+  else
+    GLT_PROF(GLT_PROF_ATTN_BWD, flash_bwd(y.qkv, y.o, dout_b, y.lse, dqkv, dq_acc, dsum, as, st));
   if (rope_on(l)) GLT_TRY(rope_apply(dqkv, as, cos_t, sin_t, 1, 1, 1, st));
   GLT_PROF(GLT_PROF_DX_QKV, g_f32(kmaj(dqkv, QKV), mnmaj(y.wqkv, D), M, D, QKV, dtmp, D, st));
   GLT_TRY(rmsnorm_bwd(dtmp, xs[l], y.in_norm, y.var1, dx, dx, nullptr, M, D, cfg.rms_norm_eps, st));

@@ -82,11 +82,14 @@ extern "C" int glt_attention_fwd(const uint16_t* qkv, int64_t ld_qkv, uint16_t* 
 extern "C" int glt_attention_bwd(const uint16_t* qkv, int64_t ld_qkv, const uint16_t* o,
                                  const uint16_t* dout, int64_t ld_o, const float* lse,
                                  uint16_t* dqkv, float* dq_acc, float* dsum, int B, int T, int nh,
-                                 int nkv, int hd, void* stream) {
+                                 int nkv, int hd, int impl, void* stream) {
   if (!qkv || !o || !dout || !lse || !dqkv || !dq_acc || !dsum)
     return glt::fail(GLT_EINVAL, "null argument");
   const AttnShape s = make_shape(B, T, nh, nkv, hd, ld_qkv, ld_o);
-  return glt::flash_bwd(qkv, o, dout, lse, dqkv, dq_acc, dsum, s, static_cast<cudaStream_t>(stream));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (impl == GLT_ATTN_TCGEN05) return glt::flash_bwd_tc(qkv, o, dout, lse, dqkv, dq_acc, dsum, s, st);
+  if (impl == GLT_ATTN_MMA_SYNC) return glt::flash_bwd(qkv, o, dout, lse, dqkv, dq_acc, dsum, s, st);
+  return glt::fail(GLT_EINVAL, "unknown attention implementation %d", impl);
 }
 
 extern "C" int glt_rope(uint16_t* qkv, int64_t ld_qkv, int B, int T, int nh, int nkv, int hd,

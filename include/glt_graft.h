@@ -162,8 +162,9 @@ GLT_API int glt_shadow_bake(uint16_t* base, int64_t base_stride, const float* gr
 /* indexed, not repeat_interleave'd); backward = attention_bwd_autograd's  */
 /* gradient (attention_autograd_impl.inc:1-39) into dqkv (same packing),   */
 /* with fp32 workspaces dq_acc [B*T, nh*hd] and dsum [B*nh*T].             */
-/* impl: GLT_ATTN_TCGEN05 (tcgen05/TMEM kernel, seq_len % 128 == 0) or      */
-/* GLT_ATTN_MMA_SYNC (seq_len % 64 == 0).  hd: 64 or 128.                   */
+/* impl: GLT_ATTN_TCGEN05 (tcgen05/TMEM kernels, seq_len % 128 == 0; the   */
+/* backward needs hd 128) or GLT_ATTN_MMA_SYNC (seq_len % 64 == 0).         */
+/* hd: 64 or 128.                                                          */
 /* RoPE: half-split rotation in place on q and k (rope_impl.inc:8-64);      */
 /* inverse = 1 applies the transpose (its backward).                        */
 /* RMSNorm: rms_norm_fwd_kernel / rms_norm_bwd_kernel                       */
@@ -177,7 +178,7 @@ GLT_API int glt_attention_fwd(const uint16_t* qkv, int64_t ld_qkv, uint16_t* o, 
 GLT_API int glt_attention_bwd(const uint16_t* qkv, int64_t ld_qkv, const uint16_t* o,
                               const uint16_t* dout, int64_t ld_o, const float* lse, uint16_t* dqkv,
                               float* dq_acc, float* dsum, int B, int T, int nh, int nkv, int hd,
-                              void* stream);
+                              int impl, void* stream);
 GLT_API int glt_rope(uint16_t* qkv, int64_t ld_qkv, int B, int T, int nh, int nkv, int hd,
                      float theta, int inverse, void* stream);
 GLT_API int glt_rmsnorm_fwd(const uint16_t* x, const uint16_t* w, uint16_t* y, float* var, int M,

@@ -70,8 +70,10 @@ def test_tcgen05_and_mma_sync_agree_on_large_scores():
     torch.testing.assert_close(l1, l2, rtol=1e-3, atol=2e-3)
 
 
-@pytest.mark.parametrize("B,T,nh,nkv,hd", [(2, 128, 4, 2, 128), (1, 256, 4, 4, 64)])
-def test_backward_matches_autograd(B, T, nh, nkv, hd):
+@pytest.mark.parametrize("impl,B,T,nh,nkv,hd", [(MMA, 2, 128, 4, 2, 128), (MMA, 1, 256, 4, 4, 64),
+                                                (TC, 2, 128, 4, 2, 128), (TC, 1, 384, 8, 2, 128),
+                                                (TC, 2, 256, 4, 4, 128)])
+def test_backward_matches_autograd(impl, B, T, nh, nkv, hd):
     qkv = make_qkv(B, T, nh, nkv, hd, seed=11)
     o, lse = fwd(qkv, B, T, nh, nkv, hd, MMA)
     g = torch.Generator(device="cuda").manual_seed(12)
@@ -80,7 +82,7 @@ def test_backward_matches_autograd(B, T, nh, nkv, hd):
     dq_acc = torch.empty(B * T, nh * hd, device="cuda")
     dsum = torch.empty(B * nh * T, device="cuda")
     _lib.check(lib.glt_attention_bwd(vp(qkv), qkv.shape[1], vp(o), vp(dout), nh * hd, vp(lse),
-                                     vp(dqkv), vp(dq_acc), vp(dsum), B, T, nh, nkv, hd,
+                                     vp(dqkv), vp(dq_acc), vp(dsum), B, T, nh, nkv, hd, impl,
                                      C.c_void_p(torch.cuda.current_stream().cuda_stream)))
     torch.cuda.synchronize()
     x = qkv.float().requires_grad_(True)

@@ -61,6 +61,12 @@ class GltStepStats(C.Structure):
         "domain_ood_energy_ratio", "total_loss", "lr", "grad_norm")]
 
 
+class GltEvalStats(C.Structure):
+    _fields_ = [("tokens", C.c_int64), ("total_nll", C.c_double), ("mean_ce", C.c_double),
+                ("ppl", C.c_double), ("logits_sum", C.c_double), ("logits_l2", C.c_double),
+                ("logits_hash", C.c_uint64), ("graft_forward_calls", C.c_int64)]
+
+
 _cfgp = C.POINTER(GltModelConfig)
 _fp = C.POINTER(C.c_void_p)
 
@@ -85,6 +91,8 @@ SIGNATURES: dict[str, tuple] = {
     "glt_model_refresh_graft": (_i32, [_vp, _vp]),
     "glt_train_step": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, C.POINTER(GltStepStats), _vp]),
     "glt_forward": (_i32, [_vp, _vp, _i32, _i32, _vp, _vp]),
+    "glt_model_eval": (_i32, [_vp, _vp, C.c_int64, _i32, _i32, C.POINTER(GltEvalStats), _vp]),
+    "glt_model_shadow_bake": (_i32, [_vp, _vp]),
     "glt_block_step": (_i32, [_vp, _vp, _vp, _f32, _i32, C.POINTER(_f32), _vp, _vp, _vp]),
     "glt_model_activation": (_i32, [_vp, _i32, _i32, C.POINTER(_vp), C.POINTER(_i64)]),
     "glt_dp_unique_id": (_i32, [_vp, _i32]),

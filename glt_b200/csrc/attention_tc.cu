@@ -2,7 +2,7 @@
 //
 // One CTA per (128-query tile, head, batch); 6 warps:
 //   warp 0      TMA producer: the Q tile once, then 64-key K/V tiles into a
-//               3-stage ring (128B swizzle, plain per-CTA loads, no multicast)
+//               3-stage ring (128B swizzle, plain per-CTA loads)
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer:
 //                 S_j = Q.K_j^T   (M=128, N=64,  K=hd; both operands K-major)
 //                 O  += P_j.V_j   (M=128, N=hd,  K=64; P K-major, V MN-major)

@@ -294,6 +294,7 @@ extern "C" int glt_model_save_checkpoint(GltModel* m, const char* path, const ch
                                          int domain_id) {
   if (!m) return glt::fail(GLT_EINVAL, "null model");
   glt::Model* mm = reinterpret_cast<glt::Model*>(m);
+  if (!mm->gw) return glt::fail(GLT_ESTATE, "graft storage was freed by the shadow bake");
   GLT_CUDA_TRY(cudaDeviceSynchronize());
   return glt_checkpoint_save(path, mm->gw, mm->graft_numel, 0, session_id, domain_id, mm->S,
                              mm->H, mm->D, mm->L);
@@ -303,6 +304,7 @@ extern "C" int glt_model_load_checkpoint(GltModel* m, const char* path, const ch
                                          int expected_domain_id) {
   if (!m) return glt::fail(GLT_EINVAL, "null model");
   glt::Model* mm = reinterpret_cast<glt::Model*>(m);
+  if (!mm->gw) return glt::fail(GLT_ESTATE, "graft storage was freed by the shadow bake");
   GLT_TRY(glt_checkpoint_load(path, mm->gw, mm->graft_numel, 0, expected_domain_id, session_id,
                               3 * mm->L, mm->S, mm->H, nullptr));
   GLT_TRY(mm->refresh_graft(nullptr));

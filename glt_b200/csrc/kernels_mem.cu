@@ -26,17 +26,6 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return t;
 }
 
-__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
-  f[0] = bf16_lo(u.x); f[1] = bf16_hi(u.x); f[2] = bf16_lo(u.y); f[3] = bf16_hi(u.y);
-  f[4] = bf16_lo(u.z); f[5] = bf16_hi(u.z); f[6] = bf16_lo(u.w); f[7] = bf16_hi(u.w);
-}
-__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
-  uint4 u;
-  u.x = pack_bf16x2(f[0], f[1]); u.y = pack_bf16x2(f[2], f[3]);
-  u.z = pack_bf16x2(f[4], f[5]); u.w = pack_bf16x2(f[6], f[7]);
-  return u;
-}
-
 // ------------------------------- RMSNorm -----------------------------------
 __global__ void __launch_bounds__(ROW_THREADS) rmsnorm_fwd_kernel(
     const uint16_t* __restrict__ x, const uint16_t* __restrict__ w, uint16_t* __restrict__ y,
@@ -281,27 +270,30 @@ __global__ void finalize_loss_kernel(DevStats* s, float lambda, int active, floa
 }
 
 __global__ void __launch_bounds__(ROW_THREADS) silence_down_prep_kernel(
-    const float* __restrict__ dx, const uint16_t* __restrict__ dd, const float* __restrict__ esq,
-    const int32_t* __restrict__ ood, const DevStats* __restrict__ stats, uint16_t* __restrict__ dy,
-    uint16_t* __restrict__ dyg, int D) {
+    const float* __restrict__ dx, const uint16_t* __restrict__ dd, int64_t ld_dd,
+    const float* __restrict__ esq, const int32_t* __restrict__ ood,
+    const DevStats* __restrict__ stats, uint16_t* __restrict__ dy, uint16_t* __restrict__ dyg,
+    int64_t ld_dyg, int D, int h0, int H) {
   const int64_t row = blockIdx.x;
   float sc = 0.f;
   if (dd && ood[row]) {
     const float norm = sqrtf(esq[row] + 1e-8f);
-    sc = stats->lambda_eff / (norm * sqrtf(static_cast<float>(D)));
+    sc = stats->lambda_eff / (norm * sqrtf(static_cast<float>(H)));
   }
   const float4* src = reinterpret_cast<const float4*>(dx + row * D);
   for (int i = threadIdx.x; i < (D >> 3); i += ROW_THREADS) {
     const float4 a = src[2 * i], b = src[2 * i + 1];
     float f[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
     reinterpret_cast<uint4*>(dy + row * D)[i] = pack8(f);
+    const int j = 8 * i - h0;  // column inside the graft window
+    if (j < 0 || j >= H) continue;
     if (dd) {
       float g[8];
-      unpack8(reinterpret_cast<const uint4*>(dd + row * D)[i], g);
+      unpack8(*reinterpret_cast<const uint4*>(dd + row * ld_dd + j), g);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) f[j] += sc * g[j];
+      for (int k = 0; k < 8; ++k) f[k] += sc * g[k];
     }
-    reinterpret_cast<uint4*>(dyg + row * D)[i] = pack8(f);
+    *reinterpret_cast<uint4*>(dyg + row * ld_dyg + j) = pack8(f);
   }
 }
 
@@ -359,12 +351,16 @@ __global__ void __launch_bounds__(ROW_THREADS) mse_grad_kernel(
 
 // ------------------------------- AdamW -------------------------------------
 __device__ __forceinline__ void write_mirror(const MirrorTargets& mt, uint16_t* const* gu,
-                                             uint16_t* const* wd, int l, int p, int s, int h,
-                                             float w) {
+                                             uint16_t* const* wd, int64_t i, int l, int p, int s,
+                                             int h, float w) {
   // Only grafted (layer, kind) pairs carry the delta in the fused weights;
   // the rest stay zero so they contribute nothing (should_graft_proj).
   if (l < mt.layer_begin || l > mt.layer_end || !mt.kinds[p]) return;
   const uint16_t b = f32_to_bf16_bits(w);
+  if (mt.plain) {
+    mt.plain[i] = b;
+    return;
+  }
   const int c = mt.f_pad + s;
   if (p < 2) {
     const int64_t row = 256 * (c >> 7) + (c & 127) + (p == 1 ? 128 : 0);
@@ -399,9 +395,9 @@ __global__ void adamw_kernel(float* __restrict__ w, const float* __restrict__ gr
     const float wo = w[i];
     const float nw = wo - a.lr * mh / (sqrtf(vh) + a.eps) - a.lr * a.wd * wo;
     w[i] = nw;
-    if (gu) {
+    if (gu || mt.plain) {
       const int64_t r = i - proj * SH;
-      write_mirror(mt, gu, wdp, static_cast<int>(proj / 3), p, static_cast<int>(r / H),
+      write_mirror(mt, gu, wdp, i, static_cast<int>(proj / 3), p, static_cast<int>(r / H),
                    static_cast<int>(r % H), nw);
     }
   }
@@ -413,8 +409,30 @@ __global__ void mirror_kernel(const float* __restrict__ w, int64_t n, int64_t SH
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t proj = i / SH;
     const int64_t r = i - proj * SH;
-    write_mirror(mt, gu, wdp, static_cast<int>(proj / 3), static_cast<int>(proj % 3),
+    write_mirror(mt, gu, wdp, i, static_cast<int>(proj / 3), static_cast<int>(proj % 3),
                  static_cast<int>(r / H), static_cast<int>(r % H), w[i]);
+  }
+}
+
+__global__ void shadow_bake_fused_kernel(const float* __restrict__ g, int64_t n, int64_t SH, int H,
+                                         int i0, int h0, MirrorTargets mt, uint16_t* const* gu,
+                                         uint16_t* const* wdp) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t proj = i / SH;
+    const int l = static_cast<int>(proj / 3), p = static_cast<int>(proj % 3);
+    if (l < mt.layer_begin || l > mt.layer_end || !mt.kinds[p]) continue;
+    const int64_t r = i - proj * SH;
+    const int c = i0 + static_cast<int>(r / H);
+    const int hh = h0 + static_cast<int>(r % H);
+    uint16_t* dst;
+    if (p < 2) {
+      const int64_t row = 256 * (c >> 7) + (c & 127) + (p == 1 ? 128 : 0);
+      dst = gu[l] + row * mt.D + hh;
+    } else {
+      dst = wdp[l] + static_cast<int64_t>(hh) * mt.ffn + c;
+    }
+    *dst = f32_to_bf16_bits(bf16_bits_to_f32(*dst) + g[i]);
   }
 }
 
@@ -548,12 +566,14 @@ int finalize_loss(DevStats* stats, float lambda_silence, int active_grafts, floa
   return GLT_OK;
 }
 
-int silence_down_prep(const float* dx, const uint16_t* delta_down, const float* esq_down,
-                      const int32_t* ood, const DevStats* stats, uint16_t* dy, uint16_t* dyg,
-                      int M, int D, cudaStream_t st) {
+int silence_down_prep(const float* dx, const uint16_t* delta_down, int64_t ld_dd,
+                      const float* esq_down, const int32_t* ood, const DevStats* stats,
+                      uint16_t* dy, uint16_t* dyg, int64_t ld_dyg, int M, int D, int h0, int H,
+                      cudaStream_t st) {
   if (M <= 0) return GLT_OK;
-  silence_down_prep_kernel<<<M, ROW_THREADS, 0, st>>>(dx, delta_down, esq_down, ood, stats, dy,
-                                                       dyg, D);
+  if ((h0 | H | ld_dd | ld_dyg) & 7) return fail(GLT_EINVAL, "silence_down_prep: window not 8-aligned");
+  silence_down_prep_kernel<<<M, ROW_THREADS, 0, st>>>(dx, delta_down, ld_dd, esq_down, ood, stats,
+                                                       dy, dyg, ld_dyg, D, h0, H);
   GLT_LAUNCH_CHECK();
   return GLT_OK;
 }
@@ -612,6 +632,16 @@ int refresh_mirror(const float* w, int L, int S, int H, const MirrorTargets& mir
   const int64_t SH = static_cast<int64_t>(S) * H;
   const int64_t n = SH * 3 * L;
   mirror_kernel<<<grid_for(n, 256), 256, 0, st>>>(w, n, SH, H, mirror, mirror.w_gu, mirror.w_d);
+  GLT_LAUNCH_CHECK();
+  return GLT_OK;
+}
+
+int shadow_bake_fused(const float* g, int L, int S, int H, int i0, int h0,
+                      const MirrorTargets& mt, cudaStream_t st) {
+  const int64_t SH = static_cast<int64_t>(S) * H;
+  const int64_t n = SH * 3 * L;
+  if (n <= 0) return GLT_OK;
+  shadow_bake_fused_kernel<<<grid_for(n, 256), 256, 0, st>>>(g, n, SH, H, i0, h0, mt, mt.w_gu, mt.w_d);
   GLT_LAUNCH_CHECK();
   return GLT_OK;
 }

@@ -59,12 +59,15 @@ int set_clip_scale(DevStats* stats, float v, cudaStream_t st);
 int finalize_loss(DevStats* stats, float lambda_silence, int active_grafts, float lm_loss_scale,
                   cudaStream_t st);
 
-// dy = bf16(dx);  dyg = bf16(dx + s_t * delta_down) with
+// dy = bf16(dx) over all D columns;  on the graft's hidden window [h0, h0+H):
+// dyg[:, j] = bf16(dx[:, h0+j] + s_t * delta_down[:, j]) with
 // s_t = ood_t * lambda_eff / (sqrt(esq_t + 1e-8) * sqrt(H))  (silence_blend_kernel,
-// src/kernels_elementwise_impl.inc:8-67).  delta_down may be null (no down graft).
-int silence_down_prep(const float* dx, const uint16_t* delta_down, const float* esq_down,
-                      const int32_t* ood, const DevStats* stats, uint16_t* dy, uint16_t* dyg,
-                      int M, int D, cudaStream_t st);
+// src/kernels_elementwise_impl.inc:8-67).  delta_down may be null (no down
+// graft).  h0 and H are multiples of 8; concat geometry is h0 = 0, H = D.
+int silence_down_prep(const float* dx, const uint16_t* delta_down, int64_t ld_dd,
+                      const float* esq_down, const int32_t* ood, const DevStats* stats,
+                      uint16_t* dy, uint16_t* dyg, int64_t ld_dyg, int M, int D, int h0, int H,
+                      cudaStream_t st);
 
 // Global L2 norm of gscale * grads -> stats->clip_scale = gscale * min(1, clip/norm)
 // (reduce_l2/calc_scale, src/kernels_elementwise_impl.inc:133-197; gscale = 1/world
@@ -72,9 +75,11 @@ int silence_down_prep(const float* dx, const uint16_t* delta_down, const float* 
 int grad_clip_scale(const float* grad, int64_t n, float clip_norm, float gscale,
                     DevStats* stats, cudaStream_t st);
 
-// Where the bf16 mirror of each graft projection lives inside the fused
-// concat weights (may be null: no mirror).
+// Where the bf16 mirror of each graft projection lives: inside the fused
+// concat weights (w_gu / w_d), or, for the overlay geometry, a plain bf16
+// [3L, S, H] copy in the delta_offset layout (`plain`).  Both may be null.
 struct MirrorTargets {
+  uint16_t* plain;   // overlay: bf16 image at the same flat index, or null
   uint16_t** w_gu;   // [L] device pointers to W_gu_cat (2F' x D, interleaved 128-blocks)
   uint16_t** w_d;    // [L] device pointers to W_d_cat (D x F')
   int f_pad;         // first graft column in the intermediate index space
@@ -99,6 +104,13 @@ int refresh_mirror(const float* w, int L, int S, int H, const MirrorTargets& mir
 // mode 0: base[i0+s, h0+h] = bf16(base + g[s,h]);  mode 1: base[h0+h, i0+s] = ...
 int shadow_bake(uint16_t* base, int64_t base_stride, const float* g, int S, int H, int i0, int h0,
                 int mode, cudaStream_t st);
+
+// Shadow bake of every enabled (layer, projection) of the graft straight into
+// the fused layer weights (W_gu interleaved 128-row gate/up blocks, W_d
+// [D, ffn]) of the overlay geometry: intermediate index i0+s, hidden index
+// h0+h; same bf16 round-to-nearest-even of base + delta as shadow_bake.
+int shadow_bake_fused(const float* g, int L, int S, int H, int i0, int h0,
+                      const MirrorTargets& mt, cudaStream_t st);
 
 // Deterministic N(0, std) init (counter-based hash + Box-Muller).
 int init_normal_bf16(uint16_t* p, int64_t n, uint64_t seed, float std, cudaStream_t st);

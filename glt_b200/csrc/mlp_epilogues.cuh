@@ -205,4 +205,246 @@ struct EpiGradGateUp {
   }
 };
 
+// ---------------------------------------------------------------------------
+// Overlay geometry (the reference's own: the graft overlays intermediate
+// columns [i0, i0+S) and hidden columns [h0, h0+H) of the base MLP,
+// layer_forward_impl.inc:21-22).  The expand deltas delta = x_h . Delta^T come
+// from their own GEMM (fp32) and are injected into the accumulators of the
+// slice columns before SwiGLU, in place of fused_inject_clone_energy_kernel's
+// bf16 read-modify-write.  i0 and S are multiples of 8, so an 8-column chunk
+// is either wholly inside the slice or wholly outside it.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void load8f(const float* p, float* v) {
+  const float4 a = *reinterpret_cast<const float4*>(p);
+  const float4 b = *reinterpret_cast<const float4*>(p + 4);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+// Expand / contract delta GEMM: C (fp32) = acc; optional bf16 copy; per-row
+// sums of squares of columns [0, split) into esq_lo and [split, N) into
+// esq_hi (the delta energies, kernels_elementwise_impl.inc:287-367).
+template <int BN>
+struct EpiDeltaF32 {
+  float* C;
+  int64_t ldc;
+  uint16_t* Cb;  // bf16 copy or null
+  int64_t ldcb;
+  int M, N, split;
+  float* esq_lo;
+  float* esq_hi;
+  __device__ __forceinline__ void operator()(const tc::EpiCtx<BN>& c) const {
+    float lo = 0.f, hi = 0.f;
+#pragma unroll 1
+    for (int j = 0; j < BN; j += 32) {
+      float v[32];
+      c.load(j, v);
+      if (c.row >= M) continue;
+#pragma unroll
+      for (int i = 0; i < 32; i += 8) {
+        const int col = c.n0 + j + i;
+        if (col >= N) continue;  // N is a multiple of 8
+        float* dst = C + static_cast<int64_t>(c.row) * ldc + col;
+        *reinterpret_cast<float4*>(dst) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+        *reinterpret_cast<float4*>(dst + 4) = make_float4(v[i + 4], v[i + 5], v[i + 6], v[i + 7]);
+        if (Cb) {
+          uint4 w;
+          w.x = pack_bf16x2(v[i], v[i + 1]); w.y = pack_bf16x2(v[i + 2], v[i + 3]);
+          w.z = pack_bf16x2(v[i + 4], v[i + 5]); w.w = pack_bf16x2(v[i + 6], v[i + 7]);
+          *reinterpret_cast<uint4*>(Cb + static_cast<int64_t>(c.row) * ldcb + col) = w;
+        }
+        float ss = 0.f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) ss += v[i + k] * v[i + k];
+        if (col < split) lo += ss; else hi += ss;
+      }
+    }
+    if (c.row < M) {
+      if (esq_lo && lo != 0.f) atomicAdd(esq_lo + c.row, lo);
+      if (esq_hi && hi != 0.f) atomicAdd(esq_hi + c.row, hi);
+    }
+  }
+};
+
+// C (bf16) = bf16(acc + inj[:, col - c0] on columns [c0, c1) [+ R]).
+// Used by the down GEMM (contract delta into hidden columns [h0, h0+H)) and
+// by dh (contract input grad into intermediate columns [i0, i0+S)).
+template <int BN>
+struct EpiBF16Inj {
+  uint16_t* C;
+  int64_t ldc;
+  const uint16_t* R;  // residual (may alias C) or null
+  int64_t ldr;
+  int M, N;
+  const float* inj;   // or null
+  int64_t ld_inj;
+  int c0, c1;
+  __device__ __forceinline__ void operator()(const tc::EpiCtx<BN>& c) const {
+#pragma unroll 1
+    for (int j = 0; j < BN; j += 32) {
+      float v[32];
+      c.load(j, v);
+      if (c.row >= M) continue;
+#pragma unroll
+      for (int i = 0; i < 32; i += 8) {
+        const int col = c.n0 + j + i;
+        if (col >= N) continue;
+        float o[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) o[k] = v[i + k];
+        if (inj && col >= c0 && col < c1) {
+          float d[8];
+          load8f(inj + static_cast<int64_t>(c.row) * ld_inj + (col - c0), d);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) o[k] += d[k];
+        }
+        if (R) {
+          float r[8];
+          unpack8(*reinterpret_cast<const uint4*>(R + static_cast<int64_t>(c.row) * ldr + col), r);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) o[k] += r[k];
+        }
+        *reinterpret_cast<uint4*>(C + static_cast<int64_t>(c.row) * ldc + col) = pack8(o);
+      }
+    }
+  }
+};
+
+// Forward gate/up + SwiGLU with the expand deltas injected on [i0, i1).
+struct EpiSwiGLUFwdOv {
+  uint16_t* h;
+  int64_t ldh;
+  int M;
+  const float* dg;  // [M, ld_inj] gate delta (column s = intermediate i0+s) or null
+  const float* du;  // up delta or null
+  int64_t ld_inj;
+  int i0, i1;
+  __device__ __forceinline__ void operator()(const tc::EpiCtx<256>& c) const {
+    const int cb = c.n0 >> 1;
+#pragma unroll 1
+    for (int j = 0; j < 128; j += 32) {
+      float g[32], u[32];
+      c.load(j, g);
+      c.load(128 + j, u);
+      if (c.row >= M) continue;
+      uint16_t* dst = h + static_cast<int64_t>(c.row) * ldh + cb + j;
+#pragma unroll
+      for (int i = 0; i < 32; i += 8) {
+        const int col = cb + j + i;
+        if (col >= i0 && col < i1) {
+          const int64_t off = static_cast<int64_t>(c.row) * ld_inj + (col - i0);
+          float d[8];
+          if (dg) {
+            load8f(dg + off, d);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) g[i + k] += d[k];
+          }
+          if (du) {
+            load8f(du + off, d);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) u[i + k] += d[k];
+          }
+        }
+        float o[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) o[k] = g[i + k] * sigmoidf_(g[i + k]) * u[i + k];
+        *reinterpret_cast<uint4*>(dst + i) = pack8(o);
+      }
+    }
+  }
+};
+
+// Backward of the overlay MLP fused into the gate/up recompute
+// (layer_recompute_impl.inc:8-91 + layer_backward_impl.inc:36-361):
+//   recompute gp/up (+ injected deltas on the slice), SwiGLU backward into
+//   dgu for every column (the base input grad uses the plain dgp/dup);
+//   on the slice also the silence-blended expand grads
+//     dys_gate = dgp + ood * lambda_eff / (norm_g sqrt(S) + 1e-8) * delta_gate
+//   (fused_silence_blend_energy_kernel, :458-560) into dys [M, 2S] (gate
+//   columns [0, S), up [S, 2S)), and h = silu(gp) up into hg for the contract
+//   weight grad.
+struct EpiSwiGLUBwdOv {
+  const uint16_t* dh;
+  int64_t lddh;
+  uint16_t* dgu;
+  int64_t ldgu;
+  const float* dg;  // gate delta or null (gate not grafted)
+  const float* du;
+  int64_t ld_inj;
+  uint16_t* dys;    // [M, lddys] or null
+  int64_t lddys;
+  uint16_t* hg;     // [M, ldhg] or null (down not grafted)
+  int64_t ldhg;
+  int M, i0, i1, S;
+  const float* esq_gate;
+  const float* esq_up;
+  const int32_t* ood;
+  const DevStats* stats;
+  __device__ __forceinline__ void operator()(const tc::EpiCtx<256>& c) const {
+    const int cb = c.n0 >> 1;
+    const bool slice = (cb + 128 > i0) && (cb < i1);
+    float sg_s = 0.f, su_s = 0.f;
+    if (slice && c.row < M && ood[c.row]) {
+      const float lam = stats->lambda_eff;
+      const float rs = sqrtf(static_cast<float>(S));
+      if (dg) sg_s = lam / (sqrtf(esq_gate[c.row] + 1e-8f) * rs + 1e-8f);
+      if (du) su_s = lam / (sqrtf(esq_up[c.row] + 1e-8f) * rs + 1e-8f);
+    }
+#pragma unroll 1
+    for (int j = 0; j < 128; j += 32) {
+      float g[32], u[32];
+      c.load(j, g);
+      c.load(128 + j, u);
+      if (c.row >= M) continue;
+      const uint16_t* dhr = dh + static_cast<int64_t>(c.row) * lddh + cb + j;
+      uint16_t* dgr = dgu + static_cast<int64_t>(c.row) * ldgu + c.n0 + j;
+#pragma unroll
+      for (int i = 0; i < 32; i += 8) {
+        const int col = cb + j + i;
+        const bool in = col >= i0 && col < i1;
+        float deg[8] = {}, deu[8] = {};
+        const int64_t off = static_cast<int64_t>(c.row) * ld_inj + (col - i0);
+        if (in && dg) {
+          load8f(dg + off, deg);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) g[i + k] += deg[k];
+        }
+        if (in && du) {
+          load8f(du + off, deu);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) u[i + k] += deu[k];
+        }
+        float d[8];
+        unpack8(*reinterpret_cast<const uint4*>(dhr + i), d);
+        float og[8], ou[8], hh[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float gp = g[i + k], up = u[i + k];
+          const float sg = sigmoidf_(gp);
+          og[k] = d[k] * up * sg * (1.f + gp * (1.f - sg));
+          ou[k] = d[k] * gp * sg;
+          hh[k] = gp * sg * up;
+        }
+        *reinterpret_cast<uint4*>(dgr + i) = pack8(og);
+        *reinterpret_cast<uint4*>(dgr + 128 + i) = pack8(ou);
+        if (in) {
+          const int s = col - i0;
+          if (dys) {
+            float bg[8], bu[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              bg[k] = og[k] + sg_s * deg[k];
+              bu[k] = ou[k] + su_s * deu[k];
+            }
+            uint16_t* dr = dys + static_cast<int64_t>(c.row) * lddys + s;
+            if (dg) *reinterpret_cast<uint4*>(dr) = pack8(bg);
+            if (du) *reinterpret_cast<uint4*>(dr + S) = pack8(bu);
+          }
+          if (hg) *reinterpret_cast<uint4*>(hg + static_cast<int64_t>(c.row) * ldhg + s) = pack8(hh);
+        }
+      }
+    }
+  }
+};
+
 }  // namespace glt

@@ -197,15 +197,6 @@ int Model::prof_collect() {
   return GLT_OK;
 }
 
-// Runs `expr` (a launch returning a status) bracketed by profiling events.
-#define GLT_PROF(kind, expr)            \
-  do {                                  \
-    const int _pb = prof_begin(kind, st); \
-    const int _ps = (expr);             \
-    prof_end(_pb, st);                  \
-    if (_ps != GLT_OK) return _ps;      \
-  } while (0)
-
 // ------------------------------ allocation ---------------------------------
 Model::~Model() {
   for (auto& e : ev_live) { cudaEventDestroy(e.a); cudaEventDestroy(e.b); }
@@ -219,24 +210,23 @@ Model::~Model() {
   if (arena) cudaFree(arena);
   if (graft_mem) cudaFree(graft_mem);
   if (pinned_stats) cudaFreeHost(pinned_stats);
+  if (eval_mem) cudaFree(eval_mem);
+  if (ev_pinned) cudaFreeHost(ev_pinned);
 }
 
 int Model::setup(const GltModelConfig& c, int batch, int seq, int k) {
   cfg = c;
   kind = k;
   GLT_TRY(config_validate(&cfg, batch, 1));
-  if (cfg.layout != GLT_LAYOUT_CONCAT)
-    return fail(GLT_EINVAL,
-                "the fused B200 training path runs the concat [base | graft] geometry; use the "
-                "glt_graft_* ops for overlay-geometry graft GEMMs");
   if (kind == GLT_MODEL_DECODER && batch % 2 != 0) return fail(GLT_EINVAL, "--batch-size must be even");
+  overlay = cfg.layout == GLT_LAYOUT_OVERLAY;
   B = batch;
   T = seq;
   M = B * T;
   D = cfg.hidden_dim;
   F = cfg.intermediate_dim;
   S = cfg.slice_dim;
-  H = D;  // concat geometry: graft spans the full hidden dimension
+  H = overlay ? D / cfg.max_domains : D;  // concat: the graft spans the full hidden dimension
   V = cfg.vocab_size;
   L = cfg.num_layers;
   nh = cfg.num_heads;
@@ -246,7 +236,21 @@ int Model::setup(const GltModelConfig& c, int batch, int seq, int k) {
   AD = nh * hd;
   F_pad = static_cast<int>(rup(F, 256));
   S_pad = static_cast<int>(rup(S, 128));
-  FF = F_pad + S_pad;
+  if (overlay) {
+    // i0 = domain_id * S, h0 = domain_id * H (layer_forward_impl.inc:21-22)
+    FF = F_pad;
+    i0 = cfg.domain_id * S;
+    h0 = cfg.domain_id * H;
+    if (S % 8 || H % 8)
+      return fail(GLT_EINVAL, "overlay geometry needs slice_dim (%d) and hidden_dim/max_domains (%d) "
+                  "to be multiples of 8", S, H);
+    if (i0 + S > F) return fail(GLT_EINVAL, "domain slice exceeds intermediate_dim");
+    if (h0 + H > D) return fail(GLT_EINVAL, "domain H-slice exceeds hidden_dim");
+  } else {
+    FF = F_pad + S_pad;
+    i0 = F_pad;
+    h0 = 0;
+  }
   if (D % 64) return fail(GLT_EINVAL, "hidden_dim must be a multiple of 64");
   if (kind == GLT_MODEL_DECODER) {
     if (T % 64) return fail(GLT_EINVAL, "seq_len must be a multiple of 64");
@@ -303,7 +307,7 @@ int Model::allocate() {
     add(reinterpret_cast<void**>(&y.x_post), b2 * M * D);
     add(reinterpret_cast<void**>(&y.x_ffn), b2 * M * D);
     add(reinterpret_cast<void**>(&y.var2), b4 * M);
-    if (enabled[3 * l + 2]) add(reinterpret_cast<void**>(&y.dd), b2 * M * D);
+    if (enabled[3 * l + 2]) add(reinterpret_cast<void**>(&y.dd), b2 * M * H);
     if (dec) {
       add(reinterpret_cast<void**>(&y.var1), b4 * M);
       add(reinterpret_cast<void**>(&y.qkv), b2 * M * QKV);
@@ -322,6 +326,11 @@ int Model::allocate() {
   add(reinterpret_cast<void**>(&dh), b2 * M * FF);
   add(reinterpret_cast<void**>(&dgu), b2 * M * 2 * FF);
   add(reinterpret_cast<void**>(&hg), b2 * M * S_pad);
+  if (overlay) {
+    add(reinterpret_cast<void**>(&gwb), b2 * static_cast<size_t>(graft_numel));
+    add(reinterpret_cast<void**>(&dlt), b4 * M * 2 * static_cast<size_t>(S));
+    add(reinterpret_cast<void**>(&dys), b2 * M * 2 * static_cast<size_t>(S));
+  }
   add(reinterpret_cast<void**>(&stats), sizeof(DevStats));
   add(reinterpret_cast<void**>(&d_enabled), sizeof(int) * 3 * L);
   add(reinterpret_cast<void**>(&d_gu_ptrs), sizeof(void*) * L);
@@ -389,6 +398,7 @@ int Model::allocate() {
 
 MirrorTargets Model::mirror() const {
   MirrorTargets mt;
+  mt.plain = overlay ? gwb : nullptr;
   mt.w_gu = d_gu_ptrs;
   mt.w_d = d_wd_ptrs;
   mt.f_pad = F_pad;
@@ -510,6 +520,7 @@ int Model::init_random(uint64_t seed, float std, float graft_std, float graft_do
     }
   }
   // graft: gate/up N(0, graft_std), down N(0, graft_down_std)
+  if (!gw) return fail(GLT_ESTATE, "graft storage was freed by the shadow bake");
   const int64_t SH = static_cast<int64_t>(S) * H;
   GLT_CUDA_TRY(cudaMemsetAsync(gw, 0, graft_numel * 4, st));
   for (int l = 0; l < L; ++l)
@@ -524,7 +535,10 @@ int Model::init_random(uint64_t seed, float std, float graft_std, float graft_do
   return GLT_OK;
 }
 
-int Model::refresh_graft(cudaStream_t st) { return refresh_mirror(gw, L, S, H, mirror(), st); }
+int Model::refresh_graft(cudaStream_t st) {
+  if (!gw) return fail(GLT_ESTATE, "graft storage was freed by the shadow bake");
+  return refresh_mirror(gw, L, S, H, mirror(), st);
+}
 
 // ------------------------------ forward ------------------------------------
 bool Model::rope_on(int l) const {
@@ -533,9 +547,13 @@ bool Model::rope_on(int l) const {
 
 int Model::ffn_forward(int l, const uint16_t* x_in, uint16_t* x_out, float* var_out,
                        bool use_graft, cudaStream_t st) {
+  if (overlay) return ffn_forward_overlay(l, x_in, x_out, var_out, use_graft, st);
   Layer& y = layers[l];
-  const bool grafted = use_graft && (enabled[3 * l] || enabled[3 * l + 1] || enabled[3 * l + 2]);
-  const int ff = grafted ? FF : F_pad;  // non-grafted layers skip the graft columns
+  const bool any = enabled[3 * l] || enabled[3 * l + 1] || enabled[3 * l + 2];
+  const bool grafted = use_graft && any;
+  // Non-grafted layers skip the graft columns; after a shadow bake they are
+  // base columns and stay in the GEMMs (without the graft-side energies).
+  const int ff = (grafted || (shadow_baked && any)) ? FF : F_pad;
   GLT_TRY(rmsnorm_fwd(x_in, y.post_norm, y.x_ffn, var_out, M, D, cfg.rms_norm_eps, st));
   // gate/up + SwiGLU (+ graft energies)
   {
@@ -579,14 +597,15 @@ int Model::forward_layer(int l, bool use_graft, cudaStream_t st) {
 // dx (fp32, grad wrt the FFN output / residual stream) -> dtmp = grad wrt x_ffn;
 // graft weight grads accumulated into `grad`.
 int Model::ffn_backward(int l, cudaStream_t st) {
+  if (overlay) return ffn_backward_overlay(l, st);
   Layer& y = layers[l];
   const bool gate = enabled[3 * l], up = enabled[3 * l + 1], down = enabled[3 * l + 2];
   const bool grafted = gate || up || down;
   const int ff = grafted ? FF : F_pad;
   const int64_t SH = static_cast<int64_t>(S) * H;
   // dy = bf16(dx); dyg = bf16(dx + silence_down)
-  GLT_TRY(silence_down_prep(dx, down ? y.dd : nullptr, y.esq + 2 * static_cast<int64_t>(M), ood,
-                            stats, dy_b, dyg_b, M, D, st));
+  GLT_TRY(silence_down_prep(dx, down ? y.dd : nullptr, D, y.esq + 2 * static_cast<int64_t>(M), ood,
+                            stats, dy_b, dyg_b, D, M, D, 0, D, st));
   // dh = [dy | dyg] . W_d   (graft columns read the silence-blended gradient)
   {
     Operand a2 = kmaj(dyg_b, D);
@@ -671,8 +690,7 @@ int Model::train_step(const int32_t* ids_in, const int32_t* ood_in, int host, in
   // LM head + cross-entropy + dlogits . E, chunked over rows
   for (int r0 = 0; r0 < M; r0 += ce_rows) {
     const int rows = std::min(ce_rows, M - r0);
-    GLT_PROF(GLT_PROF_LM_HEAD, g_bf16(kmaj(xf + static_cast<int64_t>(r0) * D, D), kmaj(lm_head, D), rows, V,
-                                      D, logits, V, nullptr, 0, st));
+    GLT_TRY(lm_head_chunk(r0, rows, st));
     GLT_PROF(GLT_PROF_CE, cross_entropy_chunk(logits, V, rows, r0, V, ids, ood, T, cfg.lm_loss_scale, stats, st));
     GLT_PROF(GLT_PROF_LM_DX, g_f32(kmaj(logits, V), mnmaj(lm_head, D), rows, D, V,
                                     dtmp + static_cast<int64_t>(r0) * D, D, st));
@@ -682,6 +700,13 @@ int Model::train_step(const int32_t* ids_in, const int32_t* ood_in, int host, in
   GLT_TRY(rmsnorm_bwd(dtmp, xs[L], final_norm, varf, nullptr, dx, nullptr, M, D, cfg.rms_norm_eps, st));
   for (int l = L - 1; l >= 0; --l) GLT_TRY(backward_layer(l, st));
   return finish_step(step, total_steps, out, st);
+}
+
+// logits[0:rows] = final-norm rows [r0, r0+rows) . lm_head^T (bf16)
+int Model::lm_head_chunk(int r0, int rows, cudaStream_t st) {
+  GLT_PROF(GLT_PROF_LM_HEAD, g_bf16(kmaj(xf + static_cast<int64_t>(r0) * D, D), kmaj(lm_head, D), rows, V,
+                                    D, logits, V, nullptr, 0, st));
+  return GLT_OK;
 }
 
 int Model::finish_step(int step, int total_steps, GltStepStats* out, cudaStream_t st) {
@@ -716,6 +741,7 @@ int Model::finish_step(int step, int total_steps, GltStepStats* out, cudaStream_
 int Model::forward_logits(const int32_t* ids_in, int host, int use_graft, uint16_t* out,
                           cudaStream_t st) {
   if (kind != GLT_MODEL_DECODER) return fail(GLT_ESTATE, "forward needs the decoder model");
+  if (use_graft && !gw) return fail(GLT_ESTATE, "graft storage was freed by the shadow bake");
   GLT_TRY(load_inputs(ids_in, nullptr, host, st));
   GLT_CUDA_TRY(cudaMemsetAsync(esq_all, 0, sizeof(float) * 3 * static_cast<size_t>(L) * M, st));
   GLT_TRY(forward_all(use_graft != 0, st));
@@ -727,6 +753,7 @@ int Model::forward_logits(const int32_t* ids_in, int host, int use_graft, uint16
 int Model::block_step(const uint16_t* x, const float* y_t, float lr, int step, float* loss,
                       uint16_t* out, float* dx_out, cudaStream_t st) {
   if (kind != GLT_MODEL_MLP_BLOCK) return fail(GLT_ESTATE, "block_step needs the MLP-block model");
+  if (!gw) return fail(GLT_ESTATE, "graft storage was freed by the shadow bake");
   GLT_CUDA_TRY(cudaMemsetAsync(stats, 0, sizeof(DevStats), st));
   GLT_CUDA_TRY(cudaMemsetAsync(grad, 0, graft_numel * 4, st));
   GLT_CUDA_TRY(cudaMemsetAsync(ood, 0, sizeof(int32_t) * M, st));
@@ -834,6 +861,7 @@ extern "C" int glt_model_graft_buffers(GltModel* m, float** weight, float** grad
                                        float** adam_v, int64_t* numel) {
   if (!m) return glt::fail(GLT_EINVAL, "null model");
   Model* mm = reinterpret_cast<Model*>(m);
+  if (!mm->gw) return glt::fail(GLT_ESTATE, "graft storage was freed by the shadow bake");
   if (weight) *weight = mm->gw;
   if (grad) *grad = mm->grad;
   if (adam_m) *adam_m = mm->adam_m;

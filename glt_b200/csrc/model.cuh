@@ -32,7 +32,13 @@ struct Layer {
   uint16_t* x_ffn = nullptr;      // [M, D] post-attention RMSNorm output
   float* var2 = nullptr;          // [M]
   float* esq = nullptr;           // [3][M] per-token sum of squares of gate/up/down deltas
-  uint16_t* dd = nullptr;         // [M, D] delta_down (bf16), for the silence gradient
+  uint16_t* dd = nullptr;         // [M, H] delta_down (bf16), for the silence gradient
+};
+
+// Running eval totals on the device (eval.cu).
+struct EvalAccum {
+  double nll, sum, sumsq;
+  uint64_t hash;
 };
 
 struct Model {
@@ -41,6 +47,11 @@ struct Model {
   int B = 0, T = 0, M = 0, D = 0, F = 0, S = 0, H = 0, V = 0, L = 0;
   int nh = 0, nkv = 0, hd = 0, QKV = 0, AD = 0;
   int F_pad = 0, S_pad = 0, FF = 0;
+  // Graft geometry: overlay (the reference's) puts the slice on intermediate
+  // columns [i0, i0+S) and hidden columns [h0, h0+H) of the base; concat
+  // appends S graft columns at i0 = F_pad with h0 = 0, H = D.
+  bool overlay = false;
+  int i0 = 0, h0 = 0;
   std::vector<int> enabled;  // [3L] should_graft_proj
   int active_grafts = 0;
   bool shadow_baked = false;
@@ -72,6 +83,9 @@ struct Model {
   uint16_t* dh = nullptr;
   uint16_t* dgu = nullptr;
   uint16_t* hg = nullptr;
+  uint16_t* gwb = nullptr;     // overlay: bf16 mirror of the graft [3L, S, H]
+  float* dlt = nullptr;        // overlay: expand deltas [M, 2S] fp32 (gate | up)
+  uint16_t* dys = nullptr;     // overlay: silence-blended expand grads [M, 2S] bf16
   uint16_t* dqkv = nullptr;
   uint16_t* dout_b = nullptr;
   float* dq_acc = nullptr;
@@ -111,6 +125,11 @@ struct Model {
   int ffn_forward(int l, const uint16_t* x_in, uint16_t* x_out, float* var_out, bool use_graft,
                   cudaStream_t st);
   int forward_layer(int l, bool use_graft, cudaStream_t st);
+  // model_overlay.cu
+  int expand_deltas(int l, bool gate, bool up, float* esq_gate, float* esq_up, cudaStream_t st);
+  int ffn_forward_overlay(int l, const uint16_t* x_in, uint16_t* x_out, float* var_out,
+                          bool use_graft, cudaStream_t st);
+  int ffn_backward_overlay(int l, cudaStream_t st);
   int ffn_backward(int l, cudaStream_t st);
   int backward_layer(int l, cudaStream_t st);
   int load_inputs(const int32_t* ids_in, const int32_t* ood_in, int host, cudaStream_t st);
@@ -123,6 +142,18 @@ struct Model {
   int block_step(const uint16_t* x, const float* y, float lr, int step, float* loss,
                  uint16_t* out, float* dx_out, cudaStream_t st);
   int activation(int which, int layer, void** ptr, int64_t* numel);
+  int lm_head_chunk(int r0, int rows, cudaStream_t st);
+
+  // eval.cu: eval-only / shadow-eval metrics and the model's own shadow bake
+  void* eval_mem = nullptr;
+  uint64_t* ev_tables = nullptr;
+  double* ev_rows = nullptr;
+  EvalAccum* ev_acc = nullptr;
+  EvalAccum* ev_pinned = nullptr;
+  int eval_alloc();
+  int eval(const int32_t* ids_in, int64_t n_seq, int host, int use_graft, GltEvalStats* out,
+           cudaStream_t st);
+  int shadow_bake_self(cudaStream_t st);
 
   // per-kind kernel timing (GLT_PROF_*)
   bool prof_on = false;
@@ -142,3 +173,14 @@ struct Model {
 };
 
 }  // namespace glt
+
+// Runs `expr` (an int status) inside a Model method with stream `st`, timed
+// under profiling kind `kind` when the model's profiling is enabled.
+#define GLT_PROF(kind, expr)            \
+  do {                                  \
+    const int _pb = prof_begin(kind, st); \
+    const int _ps = (expr);             \
+    prof_end(_pb, st);                  \
+    if (_ps != GLT_OK) return _ps;      \
+  } while (0)
+

@@ -15,8 +15,8 @@
 //   warps 2..5  epilogue: tcgen05.ld of the 128 x BN fp32 accumulator,
 //               user epilogue functor (stores / SwiGLU / residual / atomics)
 // Two TMEM accumulators (2*BN columns) let the epilogue of tile i overlap
-// the main loop of tile i+1.  No cluster multicast is used anywhere, so the
-// kernel is safe in multi-GPU jobs.
+// the main loop of tile i+1.  Every TMA load is a plain per-CTA load into
+// the CTA's own shared memory, so the kernel is safe in multi-GPU jobs.
 //
 // Every mbarrier wait is bounded (GLT_MBAR_TIMEOUT_NS of %globaltimer);
 // a timed-out wait records GLT_DEVERR_MBAR_TIMEOUT in the device error word

@@ -15,7 +15,7 @@ from dataclasses import dataclass, field, fields
 import torch
 
 from . import _lib
-from ._lib import GltModelConfig, GltStepStats, check, lib
+from ._lib import GltModelConfig, GltStepStats, GltEvalStats, check, lib
 
 LAYOUT_OVERLAY, LAYOUT_CONCAT = 0, 1
 MODEL_DECODER, MODEL_MLP_BLOCK = 0, 1
@@ -23,7 +23,8 @@ W_EMBED, W_LM_HEAD, W_FINAL_NORM, W_IN_NORM, W_Q, W_K, W_V, W_O, W_POST_NORM, W_
 # per-kind kernel timing slots (GLT_PROF_* in include/glt_graft.h)
 PROF_NAMES = ["gate_up_fwd", "down_fwd", "delta_down", "qkv", "o_proj", "attn_fwd", "dh",
               "recompute_swiglu_bwd", "wgrad_down", "wgrad_gate_up", "dx_gate_up", "do",
-              "attn_bwd", "dx_qkv", "lm_head", "lm_dx", "cross_entropy"]
+              "attn_bwd", "dx_qkv", "lm_head", "lm_dx", "cross_entropy", "delta_expand",
+              "graft_dgrad"]
 PROF_KINDS = len(PROF_NAMES)
 
 
@@ -187,6 +188,21 @@ class GraftModel:
                               C.c_void_p(logits.data_ptr()) if logits is not None else None,
                               _stream()))
         return logits
+
+    def eval(self, ids: torch.Tensor, use_graft: bool = True) -> dict:
+        """Eval-only / shadow-eval metrics over ids [num_sequences, seq_len]
+        (grafting.hip:446-713): tokens, mean_ce, ppl, logits_sum, logits_l2,
+        logits_hash, graft_forward_calls."""
+        host = int(ids.device.type == "cpu")
+        ids = ids.to(torch.int32).contiguous()
+        st = GltEvalStats()
+        check(lib.glt_model_eval(self.handle, C.c_void_p(ids.data_ptr()), ids.shape[0], host,
+                                 int(use_graft), C.byref(st), _stream()))
+        return {f: getattr(st, f) for f, _ in GltEvalStats._fields_}
+
+    def shadow_bake(self) -> None:
+        """Bake the graft into the base weights and free the graft storage."""
+        check(lib.glt_model_shadow_bake(self.handle, _stream()))
 
     def block_step(self, x: torch.Tensor, y: torch.Tensor, lr: float, step: int = 0,
                    outputs: bool = True):

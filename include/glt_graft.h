@@ -298,6 +298,37 @@ GLT_API int glt_train_step(GltModel* m, const int32_t* ids, const int32_t* ood_m
 GLT_API int glt_forward(GltModel* m, const int32_t* ids, int host_inputs, int use_graft,
                         uint16_t* logits, void* stream);
 
+/* Eval-only / shadow-eval metrics (grafting.hip:446-713): the deterministic
+ * forward over num_sequences sequences of the model's seq_len tokens
+ * (ids [num_sequences, seq_len] int32, host or device), in batches of the
+ * model's batch size (a shorter last batch is run as is).
+ *   mean_ce   mean next-token cross entropy over every position t < T-1 of
+ *             every sequence (no OOD mask), ppl = exp(mean_ce)
+ *   logits_sum / logits_l2  sum and L2 norm of all logits read as fp32
+ *   logits_hash  FNV-1a 64 over the little-endian fp32 bytes of the logits in
+ *             [sequence, position, vocab] order, chained across batches
+ *   graft_forward_calls  layers run with graft GEMMs (the reference's
+ *             g_graft_fwd_calls; 0 for a base-only or shadow eval)
+ * use_graft = 1 is the explicit-graft eval (--eval-only with a checkpoint),
+ * 0 the base model or, after glt_model_shadow_bake, the shadow model.
+ * Synchronises the stream. */
+typedef struct GltEvalStats {
+  int64_t tokens;
+  double total_nll, mean_ce, ppl, logits_sum, logits_l2;
+  uint64_t logits_hash;
+  int64_t graft_forward_calls;
+} GltEvalStats;
+GLT_API int glt_model_eval(GltModel* m, const int32_t* ids, int64_t num_sequences, int host_ids,
+                           int use_graft, GltEvalStats* out, void* stream);
+
+/* apply_graft_to_shadow for the model's own graft (shadow_bake_impl.inc:58-128):
+ * bakes the enabled projections of the grafted layer range into the base
+ * weights (bf16 round-to-nearest-even of base + delta), then frees the graft
+ * storage as --shadow-eval does before its first forward (grafting.hip:483-490).
+ * A second call fails (g_shadow_baked guard); training, graft access and
+ * use_graft = 1 forwards fail afterwards.  Synchronises the stream. */
+GLT_API int glt_model_shadow_bake(GltModel* m, void* stream);
+
 /* MLP-block step: out = x + MLP(rms_norm(x)),
  * loss = mean((out - y)^2), backward to the graft, AdamW with lr.
  * x: bf16 [M, D] device; y: fp32 [M, D] device.  Optional outputs: out (bf16),
@@ -332,7 +363,9 @@ GLT_API int glt_model_activation(GltModel* m, int which, int layer, void** ptr, 
 #define GLT_PROF_LM_HEAD 14
 #define GLT_PROF_LM_DX 15
 #define GLT_PROF_CE 16
-#define GLT_PROF_KINDS 17
+#define GLT_PROF_DELTA_EXPAND 17 /* overlay: x_h.Delta_{gate,up}^T (+ energy) */
+#define GLT_PROF_GRAFT_DGRAD 18  /* overlay: dyh.Delta_down^T, dys.Delta_gu  */
+#define GLT_PROF_KINDS 19
 GLT_API int glt_model_profile(GltModel* m, int enable);
 GLT_API int glt_model_profile_read(GltModel* m, double* ms, int64_t* launches, int reset);
 

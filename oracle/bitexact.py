@@ -279,7 +279,7 @@ def get_lr(step: int, total_steps: int, lr_peak: float, warmup: int) -> float:
 # FNV-1a 64 over little-endian fp32 logits (grafting.hip:504, 535-547)
 # ---------------------------------------------------------------------------
 def fnv1a64_f32(values: np.ndarray, h: int = 1469598103934665603) -> int:
-    data = np.ascontiguousarray(values, dtype="<f4").view(np.uint8)
+    data = np.ascontiguousarray(values, dtype="<f4").reshape(-1).view(np.uint8)
     for byte in data.tolist():
         h ^= byte
         h = (h * 1099511628211) & MASK64

@@ -93,6 +93,12 @@ SIGNATURES: dict[str, tuple] = {
     "glt_forward": (_i32, [_vp, _vp, _i32, _i32, _vp, _vp]),
     "glt_model_eval": (_i32, [_vp, _vp, C.c_int64, _i32, _i32, C.POINTER(GltEvalStats), _vp]),
     "glt_model_shadow_bake": (_i32, [_vp, _vp]),
+    "glt_model_load_safetensors": (_i32, [_vp, C.c_char_p, _vp]),
+    "glt_safetensors_tensor_info": (_i32, [C.c_char_p, C.c_char_p, C.POINTER(_i32),
+                                           C.POINTER(C.c_int64), C.POINTER(_i32)]),
+    "glt_device_memory": (_i32, [C.POINTER(C.c_int64), C.POINTER(C.c_int64)]),
+    "glt_malloc": (_i32, [C.POINTER(C.c_void_p), C.c_int64]),
+    "glt_free": (_i32, [_vp]),
     "glt_block_step": (_i32, [_vp, _vp, _vp, _f32, _i32, C.POINTER(_f32), _vp, _vp, _vp]),
     "glt_model_activation": (_i32, [_vp, _i32, _i32, C.POINTER(_vp), C.POINTER(_i64)]),
     "glt_dp_unique_id": (_i32, [_vp, _i32]),

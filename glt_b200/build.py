@@ -24,6 +24,8 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libglt_b200.so")
+CLI_SRC = os.path.join(HERE, "cli", "graft_train.cpp")
+CLI = os.path.join(HERE, "graft_train")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [
@@ -103,7 +105,25 @@ def build(force: bool = False, jobs: int | None = None, verbose_ptxas: bool = Fa
             os.remove(fp)
     if logs:
         sys.stderr.write("\n".join(logs) + "\n")
+    build_cli(force)
     return LIB
+
+
+def build_cli(force: bool = False) -> str:
+    """The graft_train command line: plain C++ over the C ABI, linked against
+    the in-tree library (found next to the binary at run time)."""
+    hdr = os.path.join(ROOT, "include", "glt_graft.h")
+    newest = max(os.path.getmtime(p) for p in (CLI_SRC, hdr, LIB))
+    if not force and os.path.exists(CLI) and os.path.getmtime(CLI) >= newest:
+        return CLI
+    cxx = os.environ.get("CXX") or shutil.which("g++") or "g++"
+    cmd = [cxx, "-O2", "-std=c++17", "-Wall", "-I" + os.path.join(ROOT, "include"), CLI_SRC,
+           "-o", CLI + ".tmp", "-L" + HERE, "-lglt_b200", "-Wl,-rpath,$ORIGIN"]
+    p = subprocess.run(cmd, capture_output=True, text=True)
+    if p.returncode != 0:
+        raise RuntimeError(f"graft_train build failed:\n{p.stdout}\n{p.stderr}")
+    os.replace(CLI + ".tmp", CLI)
+    return CLI
 
 
 def main() -> None:

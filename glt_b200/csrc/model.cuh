@@ -143,6 +143,7 @@ struct Model {
                  uint16_t* out, float* dx_out, cudaStream_t st);
   int activation(int which, int layer, void** ptr, int64_t* numel);
   int lm_head_chunk(int r0, int rows, cudaStream_t st);
+  int load_safetensors(const char* path, cudaStream_t st);  // safetensors_io.cu
 
   // eval.cu: eval-only / shadow-eval metrics and the model's own shadow bake
   void* eval_mem = nullptr;

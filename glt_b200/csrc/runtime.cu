@@ -164,6 +164,28 @@ extern "C" int glt_launch_count(uint64_t* out) {
   return GLT_OK;
 }
 
+extern "C" int glt_malloc(void** ptr, int64_t bytes) {
+  if (!ptr || bytes < 0) return fail(GLT_EINVAL, "glt_malloc: bad args");
+  *ptr = nullptr;
+  if (bytes == 0) return GLT_OK;
+  const cudaError_t e = cudaMalloc(ptr, static_cast<size_t>(bytes));
+  if (e != cudaSuccess) return fail(GLT_ENOMEM, "cudaMalloc(%lld) failed: %s", (long long)bytes, cudaGetErrorString(e));
+  return GLT_OK;
+}
+
+extern "C" int glt_free(void* ptr) {
+  if (ptr) GLT_CUDA_TRY(cudaFree(ptr));
+  return GLT_OK;
+}
+
+extern "C" int glt_device_memory(int64_t* used_bytes, int64_t* total_bytes) {
+  size_t fr = 0, tot = 0;
+  GLT_CUDA_TRY(cudaMemGetInfo(&fr, &tot));
+  if (used_bytes) *used_bytes = static_cast<int64_t>(tot - fr);
+  if (total_bytes) *total_bytes = static_cast<int64_t>(tot);
+  return GLT_OK;
+}
+
 extern "C" int glt_memcpy(void* dst, const void* src, int64_t bytes, void* stream, int sync) {
   if (bytes < 0 || (bytes > 0 && (!dst || !src))) return fail(GLT_EINVAL, "glt_memcpy: bad args");
   if (bytes == 0) return GLT_OK;

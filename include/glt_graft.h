@@ -61,8 +61,14 @@ GLT_API int glt_device_error(unsigned int* out_code);
  * synchronises the stream when sync != 0.  Lets bindings move data in and out
  * of library-owned buffers without their own CUDA runtime binding. */
 GLT_API int glt_memcpy(void* dst, const void* src, int64_t bytes, void* stream, int sync);
+/* Device allocation for bindings that have no CUDA runtime of their own. */
+GLT_API int glt_malloc(void** ptr, int64_t bytes);
+GLT_API int glt_free(void* ptr);
 /* Number of kernels this library has launched in the process so far. */
 GLT_API int glt_launch_count(uint64_t* out);
+/* Device memory in use and in total on the current device (cudaMemGetInfo);
+ * the reference samples hipMemGetInfo for peak_train_vram_mb (grafting.hip:807-821). */
+GLT_API int glt_device_memory(int64_t* used_bytes, int64_t* total_bytes);
 
 /* ------------------------------------------------------------------------ */
 /* Generic tensor-core GEMM (bf16 x bf16 -> fp32 accumulate)                */
@@ -249,6 +255,17 @@ GLT_API int glt_model_create(const GltModelConfig* cfg, int batch_size, int seq_
 GLT_API int glt_model_destroy(GltModel* m);
 /* Bytes of device memory held by the model (arena + graft buffers). */
 GLT_API int glt_model_memory(const GltModel* m, int64_t* arena_bytes, int64_t* graft_bytes);
+
+/* load_base_model_safetensors (src/model_io_impl.inc:57-190): path is one
+ * .safetensors file or a directory of shards (read in sorted order); HF
+ * tensor names; BF16/F16/F32 converted to bf16 (RNE); lm_head.weight absent
+ * means tied (the model must be created with tie_embeddings = 1, and with 0
+ * when it is present); lm_head stored [D, V] is transposed. */
+GLT_API int glt_model_load_safetensors(GltModel* m, const char* path, void* stream);
+/* Looks a tensor up by name in a safetensors file or directory: found = 0/1,
+ * ndim and up to 8 dims of its shape.  Host only (no device work). */
+GLT_API int glt_safetensors_tensor_info(const char* path, const char* name, int* found,
+                                        int64_t* shape, int* ndim);
 
 /* Seeded N(0, std) base init (norm weights 1), graft gate/up N(0, graft_std),
  * graft down N(0, graft_down_std); Adam state zeroed. */

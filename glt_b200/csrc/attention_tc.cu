@@ -224,19 +224,25 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_free[sb]);
-      // scale + causal mask + tile max
-      float mt = -INFINITY;
-      const bool diag = (j + 1) * AK > qt * AQ;
+      // causal mask (diagonal tiles only) + tile max of the raw scores; the
+      // scale is positive, so it is applied to the max and folded into the
+      // exponent's FFMA below
+      float mr = -INFINITY;
+      if ((j + 1) * AK > qt * AQ) {
+        const int lim = qrow - j * AK;  // keys i <= lim are visible
 #pragma unroll
-      for (int i = 0; i < AK; ++i) {
-        float v = sv[i] * sl2;
-        if (diag && j * AK + i > qrow) v = -INFINITY;
-        sv[i] = v;
-        mt = fmaxf(mt, v);
+        for (int i = 0; i < AK; ++i) {
+          if (i > lim) sv[i] = -INFINITY;
+          mr = fmaxf(mr, sv[i]);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < AK; ++i) mr = fmaxf(mr, sv[i]);
       }
+      const float mt = mr * sl2;
       const bool need = mt > m_run + RESCALE_THRESHOLD;   // includes the first tile
       const float m_new = need ? fmaxf(m_run, mt) : m_run;
-      const float alpha = (m_run == -INFINITY) ? 0.f : exp2f(m_run - m_new);
+      const float alpha = (m_run == -INFINITY) ? 0.f : ex2_approx(m_run - m_new);
       // P buffer sb is free once the PV product of tile j-2 is done
       if (j >= 2 && !mbar_wait(&p_free[sb], ((j - 2) >> 1) & 1, err)) { s_abort = 1; break; }
       if (__any_sync(0xffffffffu, need) && j > 0) {
@@ -261,16 +267,17 @@ __global__ void __launch_bounds__(192, 1)
       // probabilities -> bf16 P row (128 bytes, swizzled 16-byte chunks)
       float ls = 0.f;
       const uint32_t prow = sP + sb * L::P_BYTES + r * 128;
+      const float neg_m = -m_run;
 #pragma unroll
       for (int c = 0; c < AK / 8; ++c) {
         float p[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          p[i] = exp2f(sv[c * 8 + i] - m_run);
+          p[i] = ex2_approx(fmaf(sv[c * 8 + i], sl2, neg_m));
           ls += p[i];
         }
-        const uint32_t w0 = pack_bf16x2(p[0], p[1]), w1 = pack_bf16x2(p[2], p[3]);
-        const uint32_t w2 = pack_bf16x2(p[4], p[5]), w3 = pack_bf16x2(p[6], p[7]);
+        const uint32_t w0 = pack_bf16x2_rn(p[0], p[1]), w1 = pack_bf16x2_rn(p[2], p[3]);
+        const uint32_t w2 = pack_bf16x2_rn(p[4], p[5]), w3 = pack_bf16x2_rn(p[6], p[7]);
         asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(prow + ((c ^ (r & 7)) << 4)),
                      "r"(w0), "r"(w1), "r"(w2), "r"(w3)
                      : "memory");
@@ -293,10 +300,10 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
         for (int i = 0; i < 32; i += 8) {
           uint4 w;
-          w.x = pack_bf16x2(ov[i] * inv, ov[i + 1] * inv);
-          w.y = pack_bf16x2(ov[i + 2] * inv, ov[i + 3] * inv);
-          w.z = pack_bf16x2(ov[i + 4] * inv, ov[i + 5] * inv);
-          w.w = pack_bf16x2(ov[i + 6] * inv, ov[i + 7] * inv);
+          w.x = pack_bf16x2_rn(ov[i] * inv, ov[i + 1] * inv);
+          w.y = pack_bf16x2_rn(ov[i + 2] * inv, ov[i + 3] * inv);
+          w.z = pack_bf16x2_rn(ov[i + 4] * inv, ov[i + 5] * inv);
+          w.w = pack_bf16x2_rn(ov[i + 6] * inv, ov[i + 7] * inv);
           *reinterpret_cast<uint4*>(orow + c + i) = w;
         }
       }
@@ -580,10 +587,15 @@ __global__ void __launch_bounds__(192, 1)
       const float* dsv = s_dsum + pb * BQ;
 #pragma unroll
       for (int c = 0; c < BQ; ++c) {
-        float p = exp2f(sv[c] * sl2 - ls[c]);
-        if (diag && key > qt * BQ + c) p = 0.f;
+        const float p = ex2_approx(fmaf(sv[c], sl2, -ls[c]));
         sv[c] = p;
         dp[c] = p * (dp[c] - dsv[c]);
+      }
+      if (diag) {  // causal: query qt*BQ + c sees this key only if key <= query
+        const int lim = key - qt * BQ;
+#pragma unroll
+        for (int c = 0; c < BQ; ++c)
+          if (c < lim) { sv[c] = 0.f; dp[c] = 0.f; }
       }
       // P^T and dS^T rows -> 128-byte swizzled smem rows (the tiles of the
       // previous item are free: its mm_done was waited below)
@@ -591,12 +603,12 @@ __global__ void __launch_bounds__(192, 1)
       for (int c = 0; c < BQ / 8; ++c) {
         const uint32_t off = r * 128 + ((c ^ (r & 7)) << 4);
         asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(sP + off),
-                     "r"(pack_bf16x2(sv[8 * c], sv[8 * c + 1])), "r"(pack_bf16x2(sv[8 * c + 2], sv[8 * c + 3])),
-                     "r"(pack_bf16x2(sv[8 * c + 4], sv[8 * c + 5])), "r"(pack_bf16x2(sv[8 * c + 6], sv[8 * c + 7]))
+                     "r"(pack_bf16x2_rn(sv[8 * c], sv[8 * c + 1])), "r"(pack_bf16x2_rn(sv[8 * c + 2], sv[8 * c + 3])),
+                     "r"(pack_bf16x2_rn(sv[8 * c + 4], sv[8 * c + 5])), "r"(pack_bf16x2_rn(sv[8 * c + 6], sv[8 * c + 7]))
                      : "memory");
         asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(sDS + off),
-                     "r"(pack_bf16x2(dp[8 * c], dp[8 * c + 1])), "r"(pack_bf16x2(dp[8 * c + 2], dp[8 * c + 3])),
-                     "r"(pack_bf16x2(dp[8 * c + 4], dp[8 * c + 5])), "r"(pack_bf16x2(dp[8 * c + 6], dp[8 * c + 7]))
+                     "r"(pack_bf16x2_rn(dp[8 * c], dp[8 * c + 1])), "r"(pack_bf16x2_rn(dp[8 * c + 2], dp[8 * c + 3])),
+                     "r"(pack_bf16x2_rn(dp[8 * c + 4], dp[8 * c + 5])), "r"(pack_bf16x2_rn(dp[8 * c + 6], dp[8 * c + 7]))
                      : "memory");
       }
       fence_proxy_async_smem();

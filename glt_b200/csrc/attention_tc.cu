@@ -353,10 +353,16 @@ int launch_fwd_tc(const uint16_t* qkv, uint16_t* o, float* lse, const AttnShape&
 //     dS^T = P^T (dP^T - rowsum(dO*O)); both written bf16 to smem tiles
 //   dV  += P^T . dO     dK  += dS^T . Q          (M=128 keys, N=128 d, K=64)
 //   dQ^T = K^T . dS^T                            (M=128 d, N=64 q, K=128)
-// dV/dK accumulate in TMEM across items; dQ^T is read per item, staged in
-// smem as a [64 q][128 d] fp32 tile and added into the global fp32 dQ
-// accumulator with one TMA bulk reduce-add (no per-element atomics).
-// TMEM: S^T 64 | dP^T 64 | dV 128 | dK 128 | dQ^T 64 = 448 of 512 columns.
+// Pipeline: the MMA thread issues S/dP of item i+1 before dV/dK/dQ of item
+// i, so the compute warps' exponentials for item i+1 overlap the tensor
+// core's work on item i.  S/dP are double-buffered in TMEM; dQ^T of item i
+// lands in the S^T columns of its own buffer (consumed by then), and the
+// buffer is released once the compute warps have read dQ^T out.  Each
+// compute warp stages its 32 d-columns of dQ as a [64 q][32 d] fp32 tile and
+// adds it into the global fp32 dQ accumulator with its own TMA bulk
+// reduce-add, so no barrier spans the compute warps.
+// TMEM: buffer b (b = 0, 1): S^T / dQ^T [128b, 128b+64), dP^T [128b+64,
+// 128b+128); dV [256, 384); dK [384, 512).
 // ---------------------------------------------------------------------------
 constexpr int BK_KEYS = 128;  // keys per CTA
 constexpr int BQ = 64;        // queries per item
@@ -365,17 +371,17 @@ struct BwdSmem {
   static constexpr uint32_t KV_BYTES = BK_KEYS * 128 * 2;  // [128 keys][128 d] = 2 blocks x 16 KB
   static constexpr uint32_t QD_BYTES = BQ * 128 * 2;       // [64 q][128 d] = 2 blocks x 8 KB
   static constexpr uint32_t T_BYTES = BK_KEYS * BQ * 2;    // [128 keys][64 q] bf16
-  static constexpr uint32_t DQ_BYTES = BQ * 128 * 4;       // [64 q][128 d] fp32
+  static constexpr uint32_t DQW_BYTES = BQ * 32 * 4;       // per compute warp: [64 q][32 d] fp32
   static constexpr uint32_t OFF_K = 0;
   static constexpr uint32_t OFF_V = OFF_K + KV_BYTES;
   static constexpr uint32_t OFF_Q = OFF_V + KV_BYTES;       // [2]
   static constexpr uint32_t OFF_DO = OFF_Q + 2 * QD_BYTES;  // [2]
   static constexpr uint32_t OFF_P = OFF_DO + 2 * QD_BYTES;
   static constexpr uint32_t OFF_DS = OFF_P + T_BYTES;
-  static constexpr uint32_t OFF_DQ = OFF_DS + T_BYTES;
-  static constexpr uint32_t OFF_LSE = OFF_DQ + DQ_BYTES;    // [2][64] lse*log2e, [2][64] dsum
-  static constexpr uint32_t OFF_BAR = OFF_LSE + 4 * BQ * 4;
-  static constexpr uint32_t NUM_BARS = 1 + 2 + 2 + 1 + 1 + 1 + 1 + 1 + 1 + 1;
+  static constexpr uint32_t OFF_DQ = OFF_DS + T_BYTES;      // [4 warps]
+  static constexpr uint32_t OFF_LSE = OFF_DQ + 4 * DQW_BYTES;  // [4 warps][lse 64 | dsum 64]
+  static constexpr uint32_t OFF_BAR = OFF_LSE + 4 * 2 * BQ * 4;
+  static constexpr uint32_t NUM_BARS = 1 + 2 + 2 + 2 + 2 + 1 + 1 + 1;
   static constexpr uint32_t TOTAL = 1024 + OFF_BAR + NUM_BARS * 8 + 16;
 };
 
@@ -393,14 +399,6 @@ __device__ __forceinline__ void bulk_wait_read0() {
 }
 __device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
-// Bounded group barrier of the 128 compute threads on an mbarrier (count 128).
-__device__ __forceinline__ bool group_sync(uint64_t* bar, uint32_t& phase, unsigned int* err) {
-  mbar_arrive(bar);
-  const bool ok = mbar_wait(bar, phase, err);
-  phase ^= 1u;
-  return ok;
-}
-
 __global__ void __launch_bounds__(192, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_k,
                        const __grid_constant__ CUtensorMap tm_q,
@@ -411,7 +409,7 @@ __global__ void __launch_bounds__(192, 1)
   using L = BwdSmem;
   constexpr int HD = 128;
   constexpr uint32_t TMEM_COLS = 512;
-  constexpr uint32_t COL_S = 0, COL_DP = 64, COL_DV = 128, COL_DK = 256, COL_DQ = 384;
+  constexpr uint32_t COL_DV = 256, COL_DK = 384;
   constexpr uint32_t ID_SDP = make_idesc(BQ, false, false);   // M=128, N=64, K-major x K-major
   constexpr uint32_t ID_DVK = make_idesc(HD, false, true);    // M=128, N=128, A K-major, B MN-major
   constexpr uint32_t ID_DQ = make_idesc(BQ, true, true);      // M=128, N=64,  A MN, B MN
@@ -420,18 +418,14 @@ __global__ void __launch_bounds__(192, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::OFF_BAR);
   uint64_t* kv_full = bars;
-  uint64_t* qd_full = kv_full + 1;   // [2]
-  uint64_t* qd_empty = qd_full + 2;  // [2]
-  uint64_t* sdp_full = qd_empty + 2;
-  uint64_t* sdp_free = sdp_full + 1;
-  uint64_t* p_full = sdp_free + 1;
+  uint64_t* qd_full = kv_full + 1;    // [2]
+  uint64_t* qd_empty = qd_full + 2;   // [2]
+  uint64_t* sdp_full = qd_empty + 2;  // [2] per TMEM buffer
+  uint64_t* sdp_free = sdp_full + 2;  // [2] per TMEM buffer (dQ^T read out)
+  uint64_t* p_full = sdp_free + 2;
   uint64_t* mm_done = p_full + 1;
-  uint64_t* dq_free = mm_done + 1;
-  uint64_t* gbar = dq_free + 1;      // compute-group barrier
-  uint64_t* drain = gbar + 1;
+  uint64_t* drain = mm_done + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
-  float* s_lse = reinterpret_cast<float*>(sm + L::OFF_LSE);   // [2][64]
-  float* s_dsum = s_lse + 2 * BQ;                              // [2][64]
   __shared__ int abort_flag;
   volatile int& s_abort = abort_flag;
 
@@ -445,13 +439,14 @@ __global__ void __launch_bounds__(192, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    for (int i = 0; i < 2; ++i) { mbar_init(&qd_full[i], 1); mbar_init(&qd_empty[i], 1); }
-    mbar_init(sdp_full, 1);
-    mbar_init(sdp_free, 4);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&qd_full[i], 1);
+      mbar_init(&qd_empty[i], 1);
+      mbar_init(&sdp_full[i], 1);
+      mbar_init(&sdp_free[i], 4);
+    }
     mbar_init(p_full, 4);
     mbar_init(mm_done, 1);
-    mbar_init(dq_free, 4);
-    mbar_init(gbar, 128);
     mbar_init(drain, 1);
     s_abort = 0;
     fence_mbar_init();
@@ -473,7 +468,6 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t sK = smem_u32(sm + L::OFF_K), sV = smem_u32(sm + L::OFF_V);
   const uint32_t sQ = smem_u32(sm + L::OFF_Q), sDO = smem_u32(sm + L::OFF_DO);
   const uint32_t sP = smem_u32(sm + L::OFF_P), sDS = smem_u32(sm + L::OFF_DS);
-  const uint32_t sDQ = smem_u32(sm + L::OFF_DQ);
 
   if (warp == 0) {
     // ------------------------------ producer ------------------------------
@@ -500,43 +494,45 @@ __global__ void __launch_bounds__(192, 1)
   } else if (warp == 1) {
     // ------------------------------ MMA issuer ----------------------------
     if (lane == 0) {
-      bool ok = mbar_wait(kv_full, 0, err);
-      for (int i = 0; ok && i < n_items; ++i) {
-        const int st = i & 1;
-        if (!mbar_wait(&qd_full[st], (i >> 1) & 1, err) || !mbar_wait(sdp_free, (i & 1) ^ 1, err)) {
-          ok = false;
-          break;
-        }
+      // S^T(j), dP^T(j) into TMEM buffer j & 1 (both operands K-major)
+      auto issue_sdp = [&](int j) -> bool {
+        const int st = j & 1, bf = j & 1;
+        if (!mbar_wait(&qd_full[st], (j >> 1) & 1, err)) return false;
+        if (!mbar_wait(&sdp_free[bf], ((j >> 1) & 1) ^ 1, err)) return false;
         tc_fence_after();
         const uint32_t qb = sQ + st * L::QD_BYTES, db = sDO + st * L::QD_BYTES;
+        const uint32_t col = 128u * bf;
 #pragma unroll
-        for (int k = 0; k < HD / 16; ++k) {
-          umma_bf16(tmem + COL_S, desc_kmajor(sK + (k >> 2) * (BK_KEYS * 128), k & 3),
+        for (int k = 0; k < HD / 16; ++k)
+          umma_bf16(tmem + col, desc_kmajor(sK + (k >> 2) * (BK_KEYS * 128), k & 3),
                     desc_kmajor(qb + (k >> 2) * (BQ * 128), k & 3), ID_SDP, k > 0);
-        }
 #pragma unroll
-        for (int k = 0; k < HD / 16; ++k) {
-          umma_bf16(tmem + COL_DP, desc_kmajor(sV + (k >> 2) * (BK_KEYS * 128), k & 3),
+        for (int k = 0; k < HD / 16; ++k)
+          umma_bf16(tmem + col + 64, desc_kmajor(sV + (k >> 2) * (BK_KEYS * 128), k & 3),
                     desc_kmajor(db + (k >> 2) * (BQ * 128), k & 3), ID_SDP, k > 0);
-        }
-        umma_commit(sdp_full);
-        if (!mbar_wait(p_full, i & 1, err) || !mbar_wait(dq_free, (i & 1) ^ 1, err)) {
-          ok = false;
-          break;
-        }
+        umma_commit(&sdp_full[bf]);
+        return true;
+      };
+      bool ok = mbar_wait(kv_full, 0, err);
+      if (ok && n_items > 0) { tc_fence_after(); ok = issue_sdp(0); }
+      for (int i = 0; ok && i < n_items; ++i) {
+        if (i + 1 < n_items && !issue_sdp(i + 1)) { ok = false; break; }
+        const int st = i & 1;
+        if (!mbar_wait(p_full, i & 1, err)) { ok = false; break; }
         tc_fence_after();
+        const uint32_t qb = sQ + st * L::QD_BYTES, db = sDO + st * L::QD_BYTES;
 #pragma unroll
         for (int k = 0; k < BQ / 16; ++k) {
           umma_bf16(tmem + COL_DV, desc_kmajor(sP, k), desc_mnmajor(db, k), ID_DVK, (i > 0 || k > 0));
           umma_bf16(tmem + COL_DK, desc_kmajor(sDS, k), desc_mnmajor(qb, k), ID_DVK, (i > 0 || k > 0));
         }
-        // dQ^T = K^T . dS^T: A = K tile read MN-major (d contiguous, 16 KB between d blocks),
+        // dQ^T = K^T . dS^T into the (consumed) S^T columns of buffer i & 1:
+        // A = K tile read MN-major (d contiguous, 16 KB between d blocks),
         // B = dS^T tile read MN-major (q contiguous)
 #pragma unroll
-        for (int k = 0; k < BK_KEYS / 16; ++k) {
-          umma_bf16(tmem + COL_DQ, make_sdesc(sK + k * (UMMA_K * 128), BK_KEYS * 128, 1024),
+        for (int k = 0; k < BK_KEYS / 16; ++k)
+          umma_bf16(tmem + 128u * (i & 1), make_sdesc(sK + k * (UMMA_K * 128), BK_KEYS * 128, 1024),
                     make_sdesc(sDS + k * (UMMA_K * 128), 8192, 1024), ID_DQ, k > 0);
-        }
         umma_commit(mm_done);
         umma_commit(&qd_empty[st]);
       }
@@ -546,100 +542,119 @@ __global__ void __launch_bounds__(192, 1)
     // ------------------------------- compute ------------------------------
     const int sub = warp & 3;
     const int r = sub * 32 + lane;                  // key row (TMEM lane); for dQ^T: d index
-    const int tid = threadIdx.x - 64;               // 0..127
     const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
     const float sl2 = s.scale * LOG2E_F;
     const int key = kt * BK_KEYS + r;
-    uint32_t gphase = 0;
-    bool ok = true;
-    for (int i = 0; i < n_items; ++i) {
+    float* w_ls = reinterpret_cast<float*>(sm + L::OFF_LSE) + sub * 2 * BQ;  // this warp's lse | dsum
+    float* w_dq = reinterpret_cast<float*>(sm + L::OFF_DQ + sub * L::DQW_BYTES);
+    const uint32_t sDQW = smem_u32(w_dq);
+    // lse / dsum of item i, prefetched one item ahead (lane holds q = lane, 32 + lane)
+    auto lse_index = [&](int i, int q) -> int64_t {
       const int h = kvh * rep + i / per_head, qt = q_first + i % per_head;
-      const int pb = i & 1;
-      if (tid < BQ) {
-        const int64_t li = (static_cast<int64_t>(b) * s.nh + h) * s.T + qt * BQ + tid;
-        s_lse[pb * BQ + tid] = lse[li] * LOG2E_F;
-        s_dsum[pb * BQ + tid] = dsum[li];
-      }
-      if (!group_sync(gbar, gphase, err)) { ok = false; break; }
-      if (!mbar_wait(sdp_full, i & 1, err)) { ok = false; break; }
+      return (static_cast<int64_t>(b) * s.nh + h) * s.T + qt * BQ + q;
+    };
+    float pl0 = 0.f, pl1 = 0.f, pd0 = 0.f, pd1 = 0.f;
+    if (n_items > 0) {
+      pl0 = lse[lse_index(0, lane)];
+      pl1 = lse[lse_index(0, 32 + lane)];
+      pd0 = dsum[lse_index(0, lane)];
+      pd1 = dsum[lse_index(0, 32 + lane)];
+    }
+    // dQ of item j: TMEM -> this warp's [64 q][32 d] tile -> TMA reduce-add
+    auto flush_dq = [&](int j) -> bool {
+      if (!mbar_wait(mm_done, j & 1, err)) return false;
       tc_fence_after();
-      float sv[BQ], dp[BQ];
-      {
-        float t[32];
-        tmem_ld32(tmem + lane_off + COL_S, t);
-#pragma unroll
-        for (int c = 0; c < 32; ++c) sv[c] = t[c];
-        tmem_ld32(tmem + lane_off + COL_S + 32, t);
-#pragma unroll
-        for (int c = 0; c < 32; ++c) sv[32 + c] = t[c];
-        tmem_ld32(tmem + lane_off + COL_DP, t);
-#pragma unroll
-        for (int c = 0; c < 32; ++c) dp[c] = t[c];
-        tmem_ld32(tmem + lane_off + COL_DP + 32, t);
-#pragma unroll
-        for (int c = 0; c < 32; ++c) dp[32 + c] = t[c];
-      }
+      float t0[32], t1[32];
+      tmem_ld32(tmem + lane_off + 128u * (j & 1), t0);
+      tmem_ld32(tmem + lane_off + 128u * (j & 1) + 32, t1);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(sdp_free);
-      const bool diag = qt * BQ < (kt + 1) * BK_KEYS;
-      const float* ls = s_lse + pb * BQ;
-      const float* dsv = s_dsum + pb * BQ;
-#pragma unroll
-      for (int c = 0; c < BQ; ++c) {
-        const float p = ex2_approx(fmaf(sv[c], sl2, -ls[c]));
-        sv[c] = p;
-        dp[c] = p * (dp[c] - dsv[c]);
+      if (lane == 0) {
+        mbar_arrive(&sdp_free[j & 1]);
+        bulk_wait_read0();                          // this warp's previous reduce has read its tile
       }
-      if (diag) {  // causal: query qt*BQ + c sees this key only if key <= query
-        const int lim = key - qt * BQ;
+      __syncwarp();
 #pragma unroll
-        for (int c = 0; c < BQ; ++c)
-          if (c < lim) { sv[c] = 0.f; dp[c] = 0.f; }
+      for (int q = 0; q < 32; ++q) {
+        w_dq[q * 32 + lane] = t0[q] * s.scale;
+        w_dq[(32 + q) * 32 + lane] = t1[q] * s.scale;
       }
-      // P^T and dS^T rows -> 128-byte swizzled smem rows (the tiles of the
-      // previous item are free: its mm_done was waited below)
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        const int h = kvh * rep + j / per_head, qt = q_first + j % per_head;
+        tma_reduce_add_2d(&tm_dq, sDQW, h * HD + sub * 32, row0 + qt * BQ);
+        bulk_commit();
+      }
+      return true;
+    };
+    bool ok = true;
+    for (int i = 0; i < n_items; ++i) {
+      const int qt = q_first + i % per_head;
+      // this item's lse*log2e and dsum -> warp-private smem; prefetch the next item's
+      w_ls[lane] = pl0 * LOG2E_F;
+      w_ls[32 + lane] = pl1 * LOG2E_F;
+      w_ls[BQ + lane] = pd0;
+      w_ls[BQ + 32 + lane] = pd1;
+      __syncwarp();
+      if (i + 1 < n_items) {
+        pl0 = lse[lse_index(i + 1, lane)];
+        pl1 = lse[lse_index(i + 1, 32 + lane)];
+        pd0 = dsum[lse_index(i + 1, lane)];
+        pd1 = dsum[lse_index(i + 1, 32 + lane)];
+      }
+      if (!mbar_wait(&sdp_full[i & 1], (i >> 1) & 1, err)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t pw[BQ / 2], dw[BQ / 2];   // P^T and dS^T rows, packed bf16 pairs
+      {
+        const uint32_t col = 128u * (i & 1);
+        float sv[32], dv[32];
+        const bool diag = qt * BQ < (kt + 1) * BK_KEYS;
+        const int lim = key - qt * BQ;  // causal: query qt*BQ + c sees this key iff c >= lim
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          tmem_ld32(tmem + lane_off + col + 32 * half, sv);
+          tmem_ld32(tmem + lane_off + col + 64 + 32 * half, dv);
+#pragma unroll
+          for (int c = 0; c < 32; c += 2) {
+            const int q = 32 * half + c;
+            const float4 l2 = *reinterpret_cast<const float4*>(w_ls + (q & ~3));
+            const float4 d2 = *reinterpret_cast<const float4*>(w_ls + BQ + (q & ~3));
+            const float la = (q & 3) == 0 ? l2.x : l2.z, lb = (q & 3) == 0 ? l2.y : l2.w;
+            const float da = (q & 3) == 0 ? d2.x : d2.z, db = (q & 3) == 0 ? d2.y : d2.w;
+            float p0 = ex2_approx(fmaf(sv[c], sl2, -la));
+            float p1 = ex2_approx(fmaf(sv[c + 1], sl2, -lb));
+            if (diag) {
+              if (q < lim) p0 = 0.f;
+              if (q + 1 < lim) p1 = 0.f;
+            }
+            pw[q >> 1] = pack_bf16x2_rn(p0, p1);
+            dw[q >> 1] = pack_bf16x2_rn(p0 * (dv[c] - da), p1 * (dv[c + 1] - db));
+          }
+        }
+      }
+      // S^T/dP^T are in registers; dQ of the previous item frees its buffer
+      if (i > 0 && !flush_dq(i - 1)) { ok = false; break; }
+      // P^T and dS^T rows -> 128-byte swizzled smem rows (the previous item's
+      // tiles are free: its mm_done was waited in flush_dq)
 #pragma unroll
       for (int c = 0; c < BQ / 8; ++c) {
         const uint32_t off = r * 128 + ((c ^ (r & 7)) << 4);
-        asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(sP + off),
-                     "r"(pack_bf16x2_rn(sv[8 * c], sv[8 * c + 1])), "r"(pack_bf16x2_rn(sv[8 * c + 2], sv[8 * c + 3])),
-                     "r"(pack_bf16x2_rn(sv[8 * c + 4], sv[8 * c + 5])), "r"(pack_bf16x2_rn(sv[8 * c + 6], sv[8 * c + 7]))
+        asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(sP + off), "r"(pw[4 * c]),
+                     "r"(pw[4 * c + 1]), "r"(pw[4 * c + 2]), "r"(pw[4 * c + 3])
                      : "memory");
-        asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(sDS + off),
-                     "r"(pack_bf16x2_rn(dp[8 * c], dp[8 * c + 1])), "r"(pack_bf16x2_rn(dp[8 * c + 2], dp[8 * c + 3])),
-                     "r"(pack_bf16x2_rn(dp[8 * c + 4], dp[8 * c + 5])), "r"(pack_bf16x2_rn(dp[8 * c + 6], dp[8 * c + 7]))
+        asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(sDS + off), "r"(dw[4 * c]),
+                     "r"(dw[4 * c + 1]), "r"(dw[4 * c + 2]), "r"(dw[4 * c + 3])
                      : "memory");
       }
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
-      if (!mbar_wait(mm_done, i & 1, err)) { ok = false; break; }
-      tc_fence_after();
-      // dQ^T row (this thread's d) -> smem [q][d] fp32 -> TMA reduce-add into dq_acc
-      if (tid == 0) bulk_wait_read0();              // previous reduce has read the smem tile
-      if (!group_sync(gbar, gphase, err)) { ok = false; break; }
-      float* dq_s = reinterpret_cast<float*>(sm + L::OFF_DQ);
-#pragma unroll 1
-      for (int c0 = 0; c0 < BQ; c0 += 32) {
-        float t[32];
-        tmem_ld32(tmem + lane_off + COL_DQ + c0, t);
-#pragma unroll
-        for (int c = 0; c < 32; ++c) dq_s[(c0 + c) * HD + r] = t[c] * s.scale;
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(dq_free);
-      fence_proxy_async_smem();
-      if (!group_sync(gbar, gphase, err)) { ok = false; break; }
-      if (tid == 0) {
-        tma_reduce_add_2d(&tm_dq, sDQ, h * HD, row0 + qt * BQ);
-        bulk_commit();
-      }
     }
+    if (ok && n_items > 0) ok = flush_dq(n_items - 1);
     if (ok && n_items > 0) {
-      // dK (scaled) and dV rows of this CTA's keys
+      // dK (scaled) and dV rows of this CTA's keys (mm_done of the last item was waited)
       uint16_t* krow = dqkv + static_cast<int64_t>(row0 + key) * s.ld_qkv + (s.nh + kvh) * HD;
       uint16_t* vrow = dqkv + static_cast<int64_t>(row0 + key) * s.ld_qkv + (s.nh + s.nkv + kvh) * HD;
 #pragma unroll 1
@@ -649,24 +664,24 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
         for (int c = 0; c < 32; c += 8) {
           uint4 w;
-          w.x = pack_bf16x2(t[c], t[c + 1]); w.y = pack_bf16x2(t[c + 2], t[c + 3]);
-          w.z = pack_bf16x2(t[c + 4], t[c + 5]); w.w = pack_bf16x2(t[c + 6], t[c + 7]);
+          w.x = pack_bf16x2_rn(t[c], t[c + 1]); w.y = pack_bf16x2_rn(t[c + 2], t[c + 3]);
+          w.z = pack_bf16x2_rn(t[c + 4], t[c + 5]); w.w = pack_bf16x2_rn(t[c + 6], t[c + 7]);
           *reinterpret_cast<uint4*>(vrow + c0 + c) = w;
         }
         tmem_ld32(tmem + lane_off + COL_DK + c0, t);
 #pragma unroll
         for (int c = 0; c < 32; c += 8) {
           uint4 w;
-          w.x = pack_bf16x2(t[c] * s.scale, t[c + 1] * s.scale);
-          w.y = pack_bf16x2(t[c + 2] * s.scale, t[c + 3] * s.scale);
-          w.z = pack_bf16x2(t[c + 4] * s.scale, t[c + 5] * s.scale);
-          w.w = pack_bf16x2(t[c + 6] * s.scale, t[c + 7] * s.scale);
+          w.x = pack_bf16x2_rn(t[c] * s.scale, t[c + 1] * s.scale);
+          w.y = pack_bf16x2_rn(t[c + 2] * s.scale, t[c + 3] * s.scale);
+          w.z = pack_bf16x2_rn(t[c + 4] * s.scale, t[c + 5] * s.scale);
+          w.w = pack_bf16x2_rn(t[c + 6] * s.scale, t[c + 7] * s.scale);
           *reinterpret_cast<uint4*>(krow + c0 + c) = w;
         }
       }
     }
     if (!ok) s_abort = 1;
-    if (tid == 0) bulk_wait0();   // all reduce-adds complete before the CTA exits
+    if (lane == 0) bulk_wait0();   // this warp's reduce-adds complete before the CTA exits
   }
 
   tc_fence_before();
@@ -699,7 +714,7 @@ int flash_bwd_tc(const uint16_t* qkv, const uint16_t* o, const uint16_t* dout, c
   GLT_TRY(make_tmap_bf16(&tq, qkv, s.ld_qkv, M, s.ld_qkv, BQ));
   GLT_TRY(make_tmap_bf16(&tdo, dout, s.ld_o, M, s.ld_o, BQ));
   GLT_TRY(make_tmap_f32_plain(&tdq, dq_acc, static_cast<uint64_t>(s.nh) * s.hd, M,
-                              static_cast<uint64_t>(s.nh) * s.hd, 128, BQ));
+                              static_cast<uint64_t>(s.nh) * s.hd, 32, BQ));
   constexpr int smem = BwdSmem::TOTAL;
   GLT_TRY(ensure_smem_attr(reinterpret_cast<const void*>(attn_bwd_tc_kernel), smem));
   dim3 grid(s.T / BK_KEYS, s.nkv, s.B);

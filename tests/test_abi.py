@@ -100,3 +100,14 @@ def test_model_create_reports_errors_without_throwing():
     h = C.c_void_p()
     st = _lib.lib.glt_model_create(C.byref(c.to_c()), 16, 512, 7, C.byref(h))
     assert st == 1 and "unknown model kind" in _lib.last_error()
+
+
+def test_profile_kinds_match_header():
+    # glt_model_profile_read writes GLT_PROF_KINDS entries into each buffer;
+    # the Python mirror must size them the same or the call overruns them.
+    text = open(HEADER).read()
+    kinds = int(re.search(r"#define GLT_PROF_KINDS (\d+)", text).group(1))
+    assert G.PROF_KINDS == kinds
+    idx = {int(v): k.lower() for k, v in re.findall(r"#define GLT_PROF_(\w+) (\d+)", text) if k != "KINDS"}
+    assert len(idx) == kinds
+    assert idx[0] == "gate_up_fwd" and idx[12] == "attn_bwd" and idx[16] == "ce"

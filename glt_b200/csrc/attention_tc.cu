@@ -1,18 +1,26 @@
 // Causal GQA flash-attention forward on the 5th-generation tensor cores.
 //
-// One CTA per (128-query tile, head, batch); 6 warps:
-//   warp 0      TMA producer: the Q tile once, then 64-key K/V tiles into a
-//               3-stage ring (128B swizzle, plain per-CTA loads)
+// One CTA per (128-query tile, head, batch), two CTAs resident per SM so that
+// one CTA's barrier round trips, prologue and epilogue overlap the other's
+// tensor-core work; 6 warps:
+//   warp 0      TMA producer: the Q tile once, then 64-key K and V tiles into
+//               two 2-stage rings (128B swizzle, plain per-CTA loads).  A K
+//               stage is released as soon as its S product completes, a V
+//               stage after its PV product.
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer:
-//                 S_j = Q.K_j^T   (M=128, N=64,  K=hd; both operands K-major)
-//                 O  += P_j.V_j   (M=128, N=hd,  K=64; P K-major, V MN-major)
+//                 S_j = Q.K_j^T   (M=128, N=64,  K=hd; A, B from smem, K-major)
+//                 O  += P_j.V_j   (M=128, N=hd,  K=64; A = P from TMEM,
+//                                  B = V from smem, MN-major)
 //               S_{j+1} is issued before O += P_j.V_j so the softmax of tile j
 //               overlaps the next QK^T.
 //   warps 2..5  softmax: thread i owns query row i (= TMEM lane i); reads its
-//               S row with tcgen05.ld, keeps the running max / sum, writes the
-//               bf16 probabilities into a 128B-swizzled smem tile that is the
-//               K-major A operand of the PV product, and writes the output.
-// TMEM: two S buffers (64 columns each) + O (hd columns).
+//               S row with tcgen05.ld, keeps the running max / sum, and writes
+//               the bf16 probabilities back over the first 32 columns of the
+//               same S buffer with tcgen05.st, where the PV product reads them
+//               as its A operand (no shared-memory round trip for P).
+// TMEM (256 columns): S/P buffers 0 and 1 (64 columns each) + O (hd columns).
+// An S/P buffer is reused for S_{j+2} only after the PV product that read P_j
+// from it has completed (its commit), so no tensor-core ordering is assumed.
 // The O rescale of online softmax is conditional: the running max used for
 // the exponentials only moves when a row's max grows by more than 2^8, so the
 // O read-modify-write in TMEM (which must wait for the previous PV product)
@@ -34,33 +42,44 @@ using namespace tc;
 
 constexpr int AQ = 128;      // query rows per CTA
 constexpr int AK = 64;       // keys per tile
-constexpr int KV_STAGES = 3;
+constexpr int K_STAGES = 2;
+constexpr int V_STAGES = 2;
 constexpr float LOG2E_F = 1.4426950408889634f;
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
       "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
       "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
-      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
-      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
-      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
-      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
-      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
-      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
-      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
-      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
-      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
-      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
-      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+      "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]),
+      "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]),
+      "r"(v[29]), "r"(v[30]), "r"(v[31])
       : "memory");
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  uint32_t u[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(v[i]);
+  tmem_st32(taddr, u);
 }
 __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+// D (TMEM) (+)= A (TMEM) . B (smem descriptor), kind::f16, one CTA.  A is
+// M=128 lanes x K=16 bf16, two elements per 32-bit column (8 columns).
+__device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
 
 template <int HD>
@@ -68,23 +87,26 @@ struct FwdSmem {
   static constexpr uint32_t Q_BYTES = AQ * HD * 2;          // HD/64 blocks of [128 x 128B]
   static constexpr uint32_t K_BYTES = AK * HD * 2;          // HD/64 blocks of [64 x 128B]
   static constexpr uint32_t V_BYTES = AK * HD * 2;          // HD/64 chunks of [64 x 128B]
-  static constexpr uint32_t P_BYTES = AQ * AK * 2;          // [128 x 128B]
   static constexpr uint32_t OFF_Q = 0;
   static constexpr uint32_t OFF_K = OFF_Q + Q_BYTES;
-  static constexpr uint32_t OFF_V = OFF_K + KV_STAGES * K_BYTES;
-  static constexpr uint32_t OFF_P = OFF_V + KV_STAGES * V_BYTES;
-  static constexpr uint32_t OFF_BAR = OFF_P + 2 * P_BYTES;
-  static constexpr uint32_t NUM_BARS = 1 + 2 * KV_STAGES + 2 + 2 + 2 + 2 + 1;
+  static constexpr uint32_t OFF_V = OFF_K + K_STAGES * K_BYTES;
+  static constexpr uint32_t OFF_BAR = OFF_V + V_STAGES * V_BYTES;
+  static constexpr uint32_t NUM_BARS = 1 + 2 * K_STAGES + 2 * V_STAGES + 2 + 2 + 2 + 1;
   static constexpr uint32_t TOTAL = 1024 + OFF_BAR + NUM_BARS * 8 + 16;
 };
+// two CTAs per SM (228 KB of shared memory per SM, 1 KB reserved per CTA)
+static_assert(2 * (FwdSmem<128>::TOTAL + 1024) <= 233472, "attention forward: two CTAs do not fit");
+
+constexpr int FWD_THREADS = 192;   // producer, MMA, 4 softmax warps
 
 template <int HD>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(FWD_THREADS, 2)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
                        const __grid_constant__ CUtensorMap tm_kv, uint16_t* __restrict__ o,
                        float* __restrict__ lse, AttnShape s, unsigned int* err) {
   using L = FwdSmem<HD>;
-  constexpr uint32_t TMEM_COLS = 256;   // S0 | S1 | O (HD <= 128)
+  constexpr uint32_t TMEM_COLS = 256;   // S/P 0 | S/P 1 | O (HD <= 128)
+  constexpr uint32_t COL_O = 2 * AK;
   constexpr uint32_t ID_S = make_idesc(AK, false, false);
   constexpr uint32_t ID_PV = make_idesc(HD, false, true);
   extern __shared__ uint8_t smem_raw[];
@@ -92,19 +114,22 @@ __global__ void __launch_bounds__(192, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::OFF_BAR);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = q_full + 1;
-  uint64_t* kv_empty = kv_full + KV_STAGES;
-  uint64_t* s_full = kv_empty + KV_STAGES;  // [2]
-  uint64_t* s_free = s_full + 2;            // [2]
-  uint64_t* p_full = s_free + 2;            // [2]
-  uint64_t* p_free = p_full + 2;            // [2]  (= PV product done)
+  uint64_t* k_full = q_full + 1;
+  uint64_t* k_empty = k_full + K_STAGES;
+  uint64_t* v_full = k_empty + K_STAGES;
+  uint64_t* v_empty = v_full + V_STAGES;
+  uint64_t* s_full = v_empty + V_STAGES;    // [2]  S_j in buffer j & 1
+  uint64_t* p_full = s_full + 2;            // [2]  P_j written over it
+  uint64_t* p_free = p_full + 2;            // [2]  PV_j done: buffer reusable, O quiescent
   uint64_t* drain = p_free + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   __shared__ int abort_flag;
   volatile int& s_abort = abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qt = gridDim.x - 1 - blockIdx.x;   // heaviest tiles first
+  // x = query tile, heaviest first within each (head, batch): CTAs that run
+  // together share one head's K/V in L2
+  const int qt = gridDim.x - 1 - blockIdx.x;
   const int h = blockIdx.y, b = blockIdx.z;
   const int kvh = h / (s.nh / s.nkv);
   const int n_kv = (qt * AQ + AQ) / AK;        // causal: keys < (qt+1)*128
@@ -112,10 +137,10 @@ __global__ void __launch_bounds__(192, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < KV_STAGES; ++i) { mbar_init(&kv_full[i], 1); mbar_init(&kv_empty[i], 1); }
+    for (int i = 0; i < K_STAGES; ++i) { mbar_init(&k_full[i], 1); mbar_init(&k_empty[i], 1); }
+    for (int i = 0; i < V_STAGES; ++i) { mbar_init(&v_full[i], 1); mbar_init(&v_empty[i], 1); }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 4);
       mbar_init(&p_full[i], 4);
       mbar_init(&p_free[i], 1);
     }
@@ -138,7 +163,6 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t sQ = smem_u32(sm + L::OFF_Q);
   const uint32_t sK = smem_u32(sm + L::OFF_K);
   const uint32_t sV = smem_u32(sm + L::OFF_V);
-  const uint32_t sP = smem_u32(sm + L::OFF_P);
 
   if (warp == 0) {
     // ------------------------------ producer ------------------------------
@@ -149,27 +173,31 @@ __global__ void __launch_bounds__(192, 1)
       for (int c = 0; c < HD / 64; ++c)
         tma_load_2d(sm + L::OFF_Q + c * (AQ * 128), &tm_q, q_full, qcol + 64 * c, row_base + qt * AQ);
       for (int j = 0; j < n_kv && !s_abort; ++j) {
-        const int st = j % KV_STAGES;
-        if (!mbar_wait(&kv_empty[st], ((j / KV_STAGES) & 1) ^ 1, err)) { s_abort = 1; break; }
-        mbar_arrive_expect_tx(&kv_full[st], L::K_BYTES + L::V_BYTES);
-        uint8_t* kb = sm + L::OFF_K + st * L::K_BYTES;
-        uint8_t* vb = sm + L::OFF_V + st * L::V_BYTES;
+        const int ks = j % K_STAGES, vs = j % V_STAGES;
+        if (!mbar_wait(&k_empty[ks], ((j / K_STAGES) & 1) ^ 1, err)) { s_abort = 1; break; }
+        mbar_arrive_expect_tx(&k_full[ks], L::K_BYTES);
+        uint8_t* kb = sm + L::OFF_K + ks * L::K_BYTES;
 #pragma unroll
-        for (int c = 0; c < HD / 64; ++c) {
-          tma_load_2d(kb + c * (AK * 128), &tm_kv, &kv_full[st], kcol + 64 * c, row_base + j * AK);
-          tma_load_2d(vb + c * (AK * 128), &tm_kv, &kv_full[st], vcol + 64 * c, row_base + j * AK);
-        }
+        for (int c = 0; c < HD / 64; ++c)
+          tma_load_2d(kb + c * (AK * 128), &tm_kv, &k_full[ks], kcol + 64 * c, row_base + j * AK);
+        if (!mbar_wait(&v_empty[vs], ((j / V_STAGES) & 1) ^ 1, err)) { s_abort = 1; break; }
+        mbar_arrive_expect_tx(&v_full[vs], L::V_BYTES);
+        uint8_t* vb = sm + L::OFF_V + vs * L::V_BYTES;
+#pragma unroll
+        for (int c = 0; c < HD / 64; ++c)
+          tma_load_2d(vb + c * (AK * 128), &tm_kv, &v_full[vs], vcol + 64 * c, row_base + j * AK);
       }
     }
   } else if (warp == 1) {
     // ------------------------------ MMA issuer ----------------------------
     if (lane == 0) {
       auto issue_s = [&](int j) -> bool {
-        const int st = j % KV_STAGES, sb = j & 1;
-        if (!mbar_wait(&kv_full[st], (j / KV_STAGES) & 1, err)) return false;
-        if (!mbar_wait(&s_free[sb], ((j >> 1) & 1) ^ 1, err)) return false;
+        const int ks = j % K_STAGES, sb = j & 1;
+        if (!mbar_wait(&k_full[ks], (j / K_STAGES) & 1, err)) return false;
+        // buffer sb last held P_{j-2}: wait until PV_{j-2} has read it
+        if (!mbar_wait(&p_free[sb], ((j >> 1) & 1) ^ 1, err)) return false;
         tc_fence_after();
-        const uint32_t kb = sK + st * L::K_BYTES;
+        const uint32_t kb = sK + ks * L::K_BYTES;
 #pragma unroll
         for (int k = 0; k < HD / 16; ++k) {
           const uint64_t ad = desc_kmajor(sQ + (k >> 2) * (AQ * 128), k & 3);
@@ -177,25 +205,24 @@ __global__ void __launch_bounds__(192, 1)
           umma_bf16(tmem + sb * AK, ad, bd, ID_S, k > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[sb]);
+        umma_commit(&k_empty[ks]);
         return true;
       };
       bool ok = mbar_wait(q_full, 0, err);
       if (ok) { tc_fence_after(); ok = issue_s(0); }
       for (int j = 0; ok && j < n_kv; ++j) {
         if (j + 1 < n_kv && !issue_s(j + 1)) { ok = false; break; }
-        const int sb = j & 1, st = j % KV_STAGES;
+        const int sb = j & 1, vs = j % V_STAGES;
+        if (!mbar_wait(&v_full[vs], (j / V_STAGES) & 1, err)) { ok = false; break; }
         if (!mbar_wait(&p_full[sb], (j >> 1) & 1, err)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t vb = sV + st * L::V_BYTES;
-        const uint32_t pb = sP + sb * L::P_BYTES;
+        const uint32_t vb = sV + vs * L::V_BYTES;
 #pragma unroll
-        for (int k = 0; k < AK / 16; ++k) {
-          const uint64_t ad = desc_kmajor(pb, k);
-          const uint64_t bd = desc_mnmajor(vb, k);
-          umma_bf16(tmem + 2 * AK, ad, bd, ID_PV, (j > 0 || k > 0) ? 1u : 0u);
-        }
+        for (int k = 0; k < AK / 16; ++k)
+          umma_bf16_ts(tmem + COL_O, tmem + sb * AK + 8 * k, desc_mnmajor(vb, k), ID_PV,
+                       (j > 0 || k > 0) ? 1u : 0u);
         umma_commit(&p_free[sb]);
-        umma_commit(&kv_empty[st]);
+        umma_commit(&v_empty[vs]);
       }
       if (!ok) s_abort = 1;
     }
@@ -221,30 +248,22 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
         for (int i = 0; i < 32; ++i) sv[32 + i] = t[i];
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_free[sb]);
-      // causal mask (diagonal tiles only) + tile max of the raw scores; the
-      // scale is positive, so it is applied to the max and folded into the
-      // exponent's FFMA below
-      float mr = -INFINITY;
+      // causal mask (diagonal tiles only) + max of the raw scores (four
+      // independent chains); the scale is positive, so it is applied to the
+      // max and folded into the exponent's FFMA below
       if ((j + 1) * AK > qt * AQ) {
         const int lim = qrow - j * AK;  // keys i <= lim are visible
 #pragma unroll
-        for (int i = 0; i < AK; ++i) {
+        for (int i = 0; i < AK; ++i)
           if (i > lim) sv[i] = -INFINITY;
-          mr = fmaxf(mr, sv[i]);
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < AK; ++i) mr = fmaxf(mr, sv[i]);
       }
-      const float mt = mr * sl2;
+      float m4[4] = {sv[0], sv[1], sv[2], sv[3]};
+#pragma unroll
+      for (int i = 4; i < AK; ++i) m4[i & 3] = fmaxf(m4[i & 3], sv[i]);
+      const float mt = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * sl2;
       const bool need = mt > m_run + RESCALE_THRESHOLD;   // includes the first tile
       const float m_new = need ? fmaxf(m_run, mt) : m_run;
       const float alpha = (m_run == -INFINITY) ? 0.f : ex2_approx(m_run - m_new);
-      // P buffer sb is free once the PV product of tile j-2 is done
-      if (j >= 2 && !mbar_wait(&p_free[sb], ((j - 2) >> 1) & 1, err)) { s_abort = 1; break; }
       if (__any_sync(0xffffffffu, need) && j > 0) {
         // O (TMEM) must be quiescent: wait for the PV product of tile j-1
         if (!mbar_wait(&p_free[(j - 1) & 1], ((j - 1) >> 1) & 1, err)) { s_abort = 1; break; }
@@ -253,10 +272,10 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll 1
         for (int c = 0; c < HD; c += 32) {
           float ov[32];
-          tmem_ld32(tmem + lane_off + 2 * AK + c, ov);
+          tmem_ld32(tmem + lane_off + COL_O + c, ov);
 #pragma unroll
           for (int i = 0; i < 32; ++i) ov[i] *= f;
-          tmem_st32(tmem + lane_off + 2 * AK + c, ov);
+          tmem_st32(tmem + lane_off + COL_O + c, ov);
         }
         tmem_wait_st();
       }
@@ -264,26 +283,21 @@ __global__ void __launch_bounds__(192, 1)
         l_run *= alpha;
         m_run = m_new;
       }
-      // probabilities -> bf16 P row (128 bytes, swizzled 16-byte chunks)
-      float ls = 0.f;
-      const uint32_t prow = sP + sb * L::P_BYTES + r * 128;
+      // probabilities -> 32 packed bf16 pairs over columns [0, 32) of this S buffer
+      float ls4[4] = {0.f, 0.f, 0.f, 0.f};
+      uint32_t pw[AK / 2];
       const float neg_m = -m_run;
 #pragma unroll
-      for (int c = 0; c < AK / 8; ++c) {
-        float p[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          p[i] = ex2_approx(fmaf(sv[c * 8 + i], sl2, neg_m));
-          ls += p[i];
-        }
-        const uint32_t w0 = pack_bf16x2_rn(p[0], p[1]), w1 = pack_bf16x2_rn(p[2], p[3]);
-        const uint32_t w2 = pack_bf16x2_rn(p[4], p[5]), w3 = pack_bf16x2_rn(p[6], p[7]);
-        asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(prow + ((c ^ (r & 7)) << 4)),
-                     "r"(w0), "r"(w1), "r"(w2), "r"(w3)
-                     : "memory");
+      for (int i = 0; i < AK; i += 2) {
+        const float p0 = ex2_approx(fmaf(sv[i], sl2, neg_m));
+        const float p1 = ex2_approx(fmaf(sv[i + 1], sl2, neg_m));
+        ls4[i & 3] += p0;
+        ls4[(i + 1) & 3] += p1;
+        pw[i >> 1] = pack_bf16x2_rn(p0, p1);
       }
-      l_run += ls;
-      fence_proxy_async_smem();   // generic-proxy smem writes -> visible to the tensor core
+      l_run += (ls4[0] + ls4[1]) + (ls4[2] + ls4[3]);
+      tmem_st32(tmem + lane_off + sb * AK, pw);
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[sb]);
@@ -296,7 +310,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll 1
       for (int c = 0; c < HD; c += 32) {
         float ov[32];
-        tmem_ld32(tmem + lane_off + 2 * AK + c, ov);
+        tmem_ld32(tmem + lane_off + COL_O + c, ov);
 #pragma unroll
         for (int i = 0; i < 32; i += 8) {
           uint4 w;
@@ -338,8 +352,14 @@ int launch_fwd_tc(const uint16_t* qkv, uint16_t* o, float* lse, const AttnShape&
   auto k = attn_fwd_tc_kernel<HD>;
   constexpr int smem = FwdSmem<HD>::TOTAL;
   GLT_TRY(ensure_smem_attr(reinterpret_cast<const void*>(k), smem));
+  static bool carveout_set = false;   // two CTAs per SM need the full shared-memory carveout
+  if (!carveout_set) {
+    GLT_CUDA_TRY(cudaFuncSetAttribute(reinterpret_cast<const void*>(k),
+                                      cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+    carveout_set = true;
+  }
   dim3 grid(s.T / AQ, s.nh, s.B);
-  k<<<grid, 192, smem, st>>>(tq, tkv, o, lse, s, device_error_word());
+  k<<<grid, FWD_THREADS, smem, st>>>(tq, tkv, o, lse, s, device_error_word());
   GLT_LAUNCH_CHECK();
   return GLT_OK;
 }
@@ -357,33 +377,42 @@ int launch_fwd_tc(const uint16_t* qkv, uint16_t* o, float* lse, const AttnShape&
 // i, so the compute warps' exponentials for item i+1 overlap the tensor
 // core's work on item i.  S/dP are double-buffered in TMEM; dQ^T of item i
 // lands in the S^T columns of its own buffer (consumed by then), and the
-// buffer is released once the compute warps have read dQ^T out.  Each
-// compute warp stages its 32 d-columns of dQ as a [64 q][32 d] fp32 tile and
-// adds it into the global fp32 dQ accumulator with its own TMA bulk
-// reduce-add, so no barrier spans the compute warps.
+// buffer is released once the compute warps have read dQ^T out.
+// Eight compute warps, two per TMEM lane quarter: warp (quarter, half) owns
+// key rows [32 quarter, +32) and query columns [32 half, +32) of each item
+// (the backward has no reduction over queries, so the halves never talk).
+// Each stages its [32 q][32 d] block of dQ and adds it into the global fp32
+// dQ accumulator with its own TMA bulk reduce-add.
 // TMEM: buffer b (b = 0, 1): S^T / dQ^T [128b, 128b+64), dP^T [128b+64,
 // 128b+128); dV [256, 384); dK [384, 512).
 // ---------------------------------------------------------------------------
 constexpr int BK_KEYS = 128;  // keys per CTA
 constexpr int BQ = 64;        // queries per item
+// Q/dO ring depth.  A stage is released only when all five products of its
+// item are done, so with two stages the load of item i+2 starts when item i
+// finishes and its latency lands on every item; three stages hide it.
+#ifndef GLT_ATTN_QD_STAGES
+#define GLT_ATTN_QD_STAGES 3
+#endif
+constexpr int QD_STAGES = GLT_ATTN_QD_STAGES;
 
 struct BwdSmem {
   static constexpr uint32_t KV_BYTES = BK_KEYS * 128 * 2;  // [128 keys][128 d] = 2 blocks x 16 KB
   static constexpr uint32_t QD_BYTES = BQ * 128 * 2;       // [64 q][128 d] = 2 blocks x 8 KB
   static constexpr uint32_t T_BYTES = BK_KEYS * BQ * 2;    // [128 keys][64 q] bf16
-  static constexpr uint32_t DQW_BYTES = BQ * 32 * 4;       // per compute warp: [64 q][32 d] fp32
+  static constexpr uint32_t DQW_BYTES = 32 * 32 * 4;       // per compute warp: [32 q][32 d] fp32
   static constexpr uint32_t OFF_K = 0;
   static constexpr uint32_t OFF_V = OFF_K + KV_BYTES;
-  static constexpr uint32_t OFF_Q = OFF_V + KV_BYTES;       // [2]
-  static constexpr uint32_t OFF_DO = OFF_Q + 2 * QD_BYTES;  // [2]
-  static constexpr uint32_t OFF_P = OFF_DO + 2 * QD_BYTES;
+  static constexpr uint32_t OFF_Q = OFF_V + KV_BYTES;                // [QD_STAGES]
+  static constexpr uint32_t OFF_DO = OFF_Q + QD_STAGES * QD_BYTES;   // [QD_STAGES]
+  static constexpr uint32_t OFF_P = OFF_DO + QD_STAGES * QD_BYTES;
   static constexpr uint32_t OFF_DS = OFF_P + T_BYTES;
-  static constexpr uint32_t OFF_DQ = OFF_DS + T_BYTES;      // [4 warps]
-  static constexpr uint32_t OFF_LSE = OFF_DQ + 4 * DQW_BYTES;  // [4 warps][lse 64 | dsum 64]
-  static constexpr uint32_t OFF_BAR = OFF_LSE + 4 * 2 * BQ * 4;
-  static constexpr uint32_t NUM_BARS = 1 + 2 + 2 + 2 + 2 + 1 + 1 + 1;
+  static constexpr uint32_t OFF_DQ = OFF_DS + T_BYTES;      // [8 warps]
+  static constexpr uint32_t OFF_BAR = OFF_DQ + 8 * DQW_BYTES;
+  static constexpr uint32_t NUM_BARS = 1 + 2 * QD_STAGES + 2 + 2 + 1 + 1 + 1;
   static constexpr uint32_t TOTAL = 1024 + OFF_BAR + NUM_BARS * 8 + 16;
 };
+static_assert(BwdSmem::TOTAL <= 232448, "attention backward: shared memory over 227 KB");
 
 __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* tm, uint32_t src, int c0,
                                                   int c1) {
@@ -399,7 +428,9 @@ __device__ __forceinline__ void bulk_wait_read0() {
 }
 __device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
-__global__ void __launch_bounds__(192, 1)
+constexpr int BWD_THREADS = 320;   // producer, MMA, 8 compute warps
+
+__global__ void __launch_bounds__(BWD_THREADS, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_k,
                        const __grid_constant__ CUtensorMap tm_q,
                        const __grid_constant__ CUtensorMap tm_do,
@@ -418,9 +449,9 @@ __global__ void __launch_bounds__(192, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::OFF_BAR);
   uint64_t* kv_full = bars;
-  uint64_t* qd_full = kv_full + 1;    // [2]
-  uint64_t* qd_empty = qd_full + 2;   // [2]
-  uint64_t* sdp_full = qd_empty + 2;  // [2] per TMEM buffer
+  uint64_t* qd_full = kv_full + 1;            // [QD_STAGES]
+  uint64_t* qd_empty = qd_full + QD_STAGES;   // [QD_STAGES]
+  uint64_t* sdp_full = qd_empty + QD_STAGES;  // [2] per TMEM buffer
   uint64_t* sdp_free = sdp_full + 2;  // [2] per TMEM buffer (dQ^T read out)
   uint64_t* p_full = sdp_free + 2;
   uint64_t* mm_done = p_full + 1;
@@ -430,6 +461,8 @@ __global__ void __launch_bounds__(192, 1)
   volatile int& s_abort = abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // x = key tile, heaviest (kt = 0) first within each (kv head, batch): CTAs
+  // that run together share that group's Q and dO in L2
   const int kt = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int rep = s.nh / s.nkv;
   const int q_first = kt * (BK_KEYS / BQ);                 // first causal query tile
@@ -439,13 +472,15 @@ __global__ void __launch_bounds__(192, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < QD_STAGES; ++i) {
       mbar_init(&qd_full[i], 1);
       mbar_init(&qd_empty[i], 1);
-      mbar_init(&sdp_full[i], 1);
-      mbar_init(&sdp_free[i], 4);
     }
-    mbar_init(p_full, 4);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sdp_full[i], 1);
+      mbar_init(&sdp_free[i], 8);
+    }
+    mbar_init(p_full, 8);
     mbar_init(mm_done, 1);
     mbar_init(drain, 1);
     s_abort = 0;
@@ -479,9 +514,9 @@ __global__ void __launch_bounds__(192, 1)
         tma_load_2d(sm + L::OFF_V + c * (BK_KEYS * 128), &tm_k, kv_full, vcol + 64 * c, row0 + kt * BK_KEYS);
       }
       for (int i = 0; i < n_items && !s_abort; ++i) {
-        const int st = i & 1;
+        const int st = i % QD_STAGES;
         const int h = kvh * rep + i / per_head, qt = q_first + i % per_head;
-        if (!mbar_wait(&qd_empty[st], ((i >> 1) & 1) ^ 1, err)) { s_abort = 1; break; }
+        if (!mbar_wait(&qd_empty[st], ((i / QD_STAGES) & 1) ^ 1, err)) { s_abort = 1; break; }
         mbar_arrive_expect_tx(&qd_full[st], 2 * L::QD_BYTES);
         for (int c = 0; c < 2; ++c) {
           tma_load_2d(sm + L::OFF_Q + st * L::QD_BYTES + c * (BQ * 128), &tm_q, &qd_full[st],
@@ -496,8 +531,8 @@ __global__ void __launch_bounds__(192, 1)
     if (lane == 0) {
       // S^T(j), dP^T(j) into TMEM buffer j & 1 (both operands K-major)
       auto issue_sdp = [&](int j) -> bool {
-        const int st = j & 1, bf = j & 1;
-        if (!mbar_wait(&qd_full[st], (j >> 1) & 1, err)) return false;
+        const int st = j % QD_STAGES, bf = j & 1;
+        if (!mbar_wait(&qd_full[st], (j / QD_STAGES) & 1, err)) return false;
         if (!mbar_wait(&sdp_free[bf], ((j >> 1) & 1) ^ 1, err)) return false;
         tc_fence_after();
         const uint32_t qb = sQ + st * L::QD_BYTES, db = sDO + st * L::QD_BYTES;
@@ -517,7 +552,7 @@ __global__ void __launch_bounds__(192, 1)
       if (ok && n_items > 0) { tc_fence_after(); ok = issue_sdp(0); }
       for (int i = 0; ok && i < n_items; ++i) {
         if (i + 1 < n_items && !issue_sdp(i + 1)) { ok = false; break; }
-        const int st = i & 1;
+        const int st = i % QD_STAGES;
         if (!mbar_wait(p_full, i & 1, err)) { ok = false; break; }
         tc_fence_after();
         const uint32_t qb = sQ + st * L::QD_BYTES, db = sDO + st * L::QD_BYTES;
@@ -540,33 +575,31 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     // ------------------------------- compute ------------------------------
-    const int sub = warp & 3;
+    const int sub = warp & 3;                       // TMEM lane quarter
+    const int half = (warp - 2) >> 2;               // query columns [32 half, 32 half + 32)
     const int r = sub * 32 + lane;                  // key row (TMEM lane); for dQ^T: d index
     const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
     const float sl2 = s.scale * LOG2E_F;
     const int key = kt * BK_KEYS + r;
-    float* w_ls = reinterpret_cast<float*>(sm + L::OFF_LSE) + sub * 2 * BQ;  // this warp's lse | dsum
-    float* w_dq = reinterpret_cast<float*>(sm + L::OFF_DQ + sub * L::DQW_BYTES);
+    float* w_dq = reinterpret_cast<float*>(sm + L::OFF_DQ + (warp - 2) * L::DQW_BYTES);
     const uint32_t sDQW = smem_u32(w_dq);
-    // lse / dsum of item i, prefetched one item ahead (lane holds q = lane, 32 + lane)
-    auto lse_index = [&](int i, int q) -> int64_t {
+    // lse / dsum of item i for query 32 half + lane (held by that lane and
+    // broadcast by shuffle), prefetched one item ahead
+    auto lse_index = [&](int i) -> int64_t {
       const int h = kvh * rep + i / per_head, qt = q_first + i % per_head;
-      return (static_cast<int64_t>(b) * s.nh + h) * s.T + qt * BQ + q;
+      return (static_cast<int64_t>(b) * s.nh + h) * s.T + qt * BQ + 32 * half + lane;
     };
-    float pl0 = 0.f, pl1 = 0.f, pd0 = 0.f, pd1 = 0.f;
+    float pl = 0.f, pd = 0.f;
     if (n_items > 0) {
-      pl0 = lse[lse_index(0, lane)];
-      pl1 = lse[lse_index(0, 32 + lane)];
-      pd0 = dsum[lse_index(0, lane)];
-      pd1 = dsum[lse_index(0, 32 + lane)];
+      pl = lse[lse_index(0)];
+      pd = dsum[lse_index(0)];
     }
-    // dQ of item j: TMEM -> this warp's [64 q][32 d] tile -> TMA reduce-add
+    // dQ of item j: TMEM -> this warp's [32 q][32 d] tile -> TMA reduce-add
     auto flush_dq = [&](int j) -> bool {
       if (!mbar_wait(mm_done, j & 1, err)) return false;
       tc_fence_after();
-      float t0[32], t1[32];
-      tmem_ld32(tmem + lane_off + 128u * (j & 1), t0);
-      tmem_ld32(tmem + lane_off + 128u * (j & 1) + 32, t1);
+      float t[32];
+      tmem_ld32(tmem + lane_off + 128u * (j & 1) + 32 * half, t);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
@@ -575,15 +608,12 @@ __global__ void __launch_bounds__(192, 1)
       }
       __syncwarp();
 #pragma unroll
-      for (int q = 0; q < 32; ++q) {
-        w_dq[q * 32 + lane] = t0[q] * s.scale;
-        w_dq[(32 + q) * 32 + lane] = t1[q] * s.scale;
-      }
+      for (int q = 0; q < 32; ++q) w_dq[q * 32 + lane] = t[q] * s.scale;
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
         const int h = kvh * rep + j / per_head, qt = q_first + j % per_head;
-        tma_reduce_add_2d(&tm_dq, sDQW, h * HD + sub * 32, row0 + qt * BQ);
+        tma_reduce_add_2d(&tm_dq, sDQW, h * HD + sub * 32, row0 + qt * BQ + 32 * half);
         bulk_commit();
       }
       return true;
@@ -591,55 +621,53 @@ __global__ void __launch_bounds__(192, 1)
     bool ok = true;
     for (int i = 0; i < n_items; ++i) {
       const int qt = q_first + i % per_head;
-      // this item's lse*log2e and dsum -> warp-private smem; prefetch the next item's
-      w_ls[lane] = pl0 * LOG2E_F;
-      w_ls[32 + lane] = pl1 * LOG2E_F;
-      w_ls[BQ + lane] = pd0;
-      w_ls[BQ + 32 + lane] = pd1;
-      __syncwarp();
+      // this item's lse*log2e and dsum; prefetch the next item's
+      const float cl = pl * LOG2E_F, cd = pd;
       if (i + 1 < n_items) {
-        pl0 = lse[lse_index(i + 1, lane)];
-        pl1 = lse[lse_index(i + 1, 32 + lane)];
-        pd0 = dsum[lse_index(i + 1, lane)];
-        pd1 = dsum[lse_index(i + 1, 32 + lane)];
+        pl = lse[lse_index(i + 1)];
+        pd = dsum[lse_index(i + 1)];
       }
       if (!mbar_wait(&sdp_full[i & 1], (i >> 1) & 1, err)) { ok = false; break; }
       tc_fence_after();
-      uint32_t pw[BQ / 2], dw[BQ / 2];   // P^T and dS^T rows, packed bf16 pairs
+      uint32_t pw[16], dw[16];   // P^T and dS^T row segments, packed bf16 pairs
       {
-        const uint32_t col = 128u * (i & 1);
+        const uint32_t col = 128u * (i & 1) + 32 * half;
         float sv[32], dv[32];
+        tmem_ld32(tmem + lane_off + col, sv);
+        tmem_ld32(tmem + lane_off + col + 64, dv);
         const bool diag = qt * BQ < (kt + 1) * BK_KEYS;
-        const int lim = key - qt * BQ;  // causal: query qt*BQ + c sees this key iff c >= lim
+        // causal: query qt*BQ + 32 half + c sees this key iff c >= lim
+        const int lim = key - qt * BQ - 32 * half;
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          tmem_ld32(tmem + lane_off + col + 32 * half, sv);
-          tmem_ld32(tmem + lane_off + col + 64 + 32 * half, dv);
-#pragma unroll
-          for (int c = 0; c < 32; c += 2) {
-            const int q = 32 * half + c;
-            const float4 l2 = *reinterpret_cast<const float4*>(w_ls + (q & ~3));
-            const float4 d2 = *reinterpret_cast<const float4*>(w_ls + BQ + (q & ~3));
-            const float la = (q & 3) == 0 ? l2.x : l2.z, lb = (q & 3) == 0 ? l2.y : l2.w;
-            const float da = (q & 3) == 0 ? d2.x : d2.z, db = (q & 3) == 0 ? d2.y : d2.w;
-            float p0 = ex2_approx(fmaf(sv[c], sl2, -la));
-            float p1 = ex2_approx(fmaf(sv[c + 1], sl2, -lb));
-            if (diag) {
-              if (q < lim) p0 = 0.f;
-              if (q + 1 < lim) p1 = 0.f;
-            }
-            pw[q >> 1] = pack_bf16x2_rn(p0, p1);
-            dw[q >> 1] = pack_bf16x2_rn(p0 * (dv[c] - da), p1 * (dv[c + 1] - db));
+        for (int c = 0; c < 32; c += 4) {
+          const float4 l4 = make_float4(__shfl_sync(0xffffffffu, cl, c), __shfl_sync(0xffffffffu, cl, c + 1),
+                                        __shfl_sync(0xffffffffu, cl, c + 2), __shfl_sync(0xffffffffu, cl, c + 3));
+          const float4 d4 = make_float4(__shfl_sync(0xffffffffu, cd, c), __shfl_sync(0xffffffffu, cd, c + 1),
+                                        __shfl_sync(0xffffffffu, cd, c + 2), __shfl_sync(0xffffffffu, cd, c + 3));
+          float p0 = ex2_approx(fmaf(sv[c], sl2, -l4.x));
+          float p1 = ex2_approx(fmaf(sv[c + 1], sl2, -l4.y));
+          float p2 = ex2_approx(fmaf(sv[c + 2], sl2, -l4.z));
+          float p3 = ex2_approx(fmaf(sv[c + 3], sl2, -l4.w));
+          if (diag) {
+            if (c < lim) p0 = 0.f;
+            if (c + 1 < lim) p1 = 0.f;
+            if (c + 2 < lim) p2 = 0.f;
+            if (c + 3 < lim) p3 = 0.f;
           }
+          pw[c >> 1] = pack_bf16x2_rn(p0, p1);
+          pw[(c >> 1) + 1] = pack_bf16x2_rn(p2, p3);
+          dw[c >> 1] = pack_bf16x2_rn(p0 * (dv[c] - d4.x), p1 * (dv[c + 1] - d4.y));
+          dw[(c >> 1) + 1] = pack_bf16x2_rn(p2 * (dv[c + 2] - d4.z), p3 * (dv[c + 3] - d4.w));
         }
       }
       // S^T/dP^T are in registers; dQ of the previous item frees its buffer
       if (i > 0 && !flush_dq(i - 1)) { ok = false; break; }
-      // P^T and dS^T rows -> 128-byte swizzled smem rows (the previous item's
-      // tiles are free: its mm_done was waited in flush_dq)
+      // P^T and dS^T row segments -> 128-byte swizzled smem rows (16-byte
+      // chunks 4 half .. 4 half + 3; the previous item's tiles are free: its
+      // mm_done was waited in flush_dq)
 #pragma unroll
-      for (int c = 0; c < BQ / 8; ++c) {
-        const uint32_t off = r * 128 + ((c ^ (r & 7)) << 4);
+      for (int c = 0; c < 4; ++c) {
+        const uint32_t off = r * 128 + (((4 * half + c) ^ (r & 7)) << 4);
         asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(sP + off), "r"(pw[4 * c]),
                      "r"(pw[4 * c + 1]), "r"(pw[4 * c + 2]), "r"(pw[4 * c + 3])
                      : "memory");
@@ -654,11 +682,12 @@ __global__ void __launch_bounds__(192, 1)
     }
     if (ok && n_items > 0) ok = flush_dq(n_items - 1);
     if (ok && n_items > 0) {
-      // dK (scaled) and dV rows of this CTA's keys (mm_done of the last item was waited)
+      // dK (scaled) and dV of this CTA's keys, d columns [64 half, 64 half + 64)
+      // (mm_done of the last item was waited)
       uint16_t* krow = dqkv + static_cast<int64_t>(row0 + key) * s.ld_qkv + (s.nh + kvh) * HD;
       uint16_t* vrow = dqkv + static_cast<int64_t>(row0 + key) * s.ld_qkv + (s.nh + s.nkv + kvh) * HD;
 #pragma unroll 1
-      for (int c0 = 0; c0 < HD; c0 += 32) {
+      for (int c0 = 64 * half; c0 < 64 * half + 64; c0 += 32) {
         float t[32];
         tmem_ld32(tmem + lane_off + COL_DV + c0, t);
 #pragma unroll
@@ -714,11 +743,11 @@ int flash_bwd_tc(const uint16_t* qkv, const uint16_t* o, const uint16_t* dout, c
   GLT_TRY(make_tmap_bf16(&tq, qkv, s.ld_qkv, M, s.ld_qkv, BQ));
   GLT_TRY(make_tmap_bf16(&tdo, dout, s.ld_o, M, s.ld_o, BQ));
   GLT_TRY(make_tmap_f32_plain(&tdq, dq_acc, static_cast<uint64_t>(s.nh) * s.hd, M,
-                              static_cast<uint64_t>(s.nh) * s.hd, 32, BQ));
+                              static_cast<uint64_t>(s.nh) * s.hd, 32, 32));
   constexpr int smem = BwdSmem::TOTAL;
   GLT_TRY(ensure_smem_attr(reinterpret_cast<const void*>(attn_bwd_tc_kernel), smem));
   dim3 grid(s.T / BK_KEYS, s.nkv, s.B);
-  attn_bwd_tc_kernel<<<grid, 192, smem, st>>>(tk, tq, tdo, tdq, lse, dsum, dqkv, s,
+  attn_bwd_tc_kernel<<<grid, BWD_THREADS, smem, st>>>(tk, tq, tdo, tdq, lse, dsum, dqkv, s,
                                               device_error_word());
   GLT_LAUNCH_CHECK();
   return attn_bwd_finish(dq_acc, dqkv, s, st);

@@ -403,12 +403,112 @@ __global__ void adamw_kernel(float* __restrict__ w, const float* __restrict__ gr
   }
 }
 
+// Vectorized AdamW: four consecutive elements per thread (S*H and H are
+// multiples of 4, so a vector stays inside one row of one projection).  The
+// bf16 image goes out as one 8-byte store: at the same flat index (overlay),
+// or into the interleaved gate/up rows of the concat weights, where h is
+// contiguous.  The down projection's image is transposed (h-major rows of
+// W_d_cat); with skip_down set it is left to mirror_down_kernel, which stages
+// that transpose through shared memory.
+__global__ void adamw_vec_kernel(float* __restrict__ w, const float* __restrict__ grad,
+                                 float* __restrict__ m, float* __restrict__ v, int64_t n,
+                                 int64_t SH, int H, AdamArgs a, const DevStats* __restrict__ stats,
+                                 MirrorTargets mt, uint16_t* const* gu, uint16_t* const* wdp,
+                                 int skip_down) {
+  const float cs = stats ? stats->clip_scale : 1.f;
+  const int64_t nvec = n >> 2;
+  for (int64_t q = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; q < nvec;
+       q += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t i = q << 2;
+    const int64_t proj = i / SH;
+    const int p = static_cast<int>(proj % 3);
+    if ((p == 0 && !a.en0) || (p == 1 && !a.en1) || (p == 2 && !a.en2)) continue;
+    const float4 g4 = *reinterpret_cast<const float4*>(grad + i);
+    const float gv[4] = {g4.x * cs, g4.y * cs, g4.z * cs, g4.w * cs};
+    float4 m4 = *reinterpret_cast<const float4*>(m + i);
+    float4 v4 = *reinterpret_cast<const float4*>(v + i);
+    float4 w4 = *reinterpret_cast<const float4*>(w + i);
+    float* mp = reinterpret_cast<float*>(&m4);
+    float* vp = reinterpret_cast<float*>(&v4);
+    float* wp = reinterpret_cast<float*>(&w4);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      mp[k] = a.b1 * mp[k] + (1.f - a.b1) * gv[k];
+      vp[k] = a.b2 * vp[k] + (1.f - a.b2) * gv[k] * gv[k];
+      const float mh = mp[k] * a.c1, vh = vp[k] * a.c2;
+      wp[k] = wp[k] - a.lr * mh / (sqrtf(vh) + a.eps) - a.lr * a.wd * wp[k];
+    }
+    *reinterpret_cast<float4*>(m + i) = m4;
+    *reinterpret_cast<float4*>(v + i) = v4;
+    *reinterpret_cast<float4*>(w + i) = w4;
+    if (!gu && !mt.plain) continue;
+    const int l = static_cast<int>(proj / 3);
+    if (l < mt.layer_begin || l > mt.layer_end || !mt.kinds[p]) continue;
+    uint2 b;
+    b.x = static_cast<uint32_t>(f32_to_bf16_bits(wp[0])) |
+          (static_cast<uint32_t>(f32_to_bf16_bits(wp[1])) << 16);
+    b.y = static_cast<uint32_t>(f32_to_bf16_bits(wp[2])) |
+          (static_cast<uint32_t>(f32_to_bf16_bits(wp[3])) << 16);
+    if (mt.plain) {
+      *reinterpret_cast<uint2*>(mt.plain + i) = b;
+      continue;
+    }
+    const int64_t r = i - proj * SH;
+    const int s = static_cast<int>(r / H), h = static_cast<int>(r % H);
+    if (p < 2) {
+      const int c = mt.f_pad + s;
+      const int64_t row = 256 * (c >> 7) + (c & 127) + (p == 1 ? 128 : 0);
+      *reinterpret_cast<uint2*>(gu[l] + row * mt.D + h) = b;
+    } else if (!skip_down) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) write_mirror(mt, gu, wdp, i + k, l, 2, s, h + k, wp[k]);
+    }
+  }
+}
+
+// bf16 image of the down projections' graft, [S, H] fp32 -> W_d_cat[h][f_pad + s]
+// for every grafted layer.  Tile of 64 s x 32 h per CTA: read 128-byte rows
+// along h, transpose in shared memory, write 128-byte rows along s.
+constexpr int MD_S = 64, MD_H = 32;
+__global__ void __launch_bounds__(256) mirror_down_kernel(const float* __restrict__ w, int S, int H,
+                                                          MirrorTargets mt,
+                                                          uint16_t* const* __restrict__ wdp) {
+  __shared__ float tile[MD_S][MD_H + 1];
+  const int l = mt.layer_begin + blockIdx.z;
+  const int s0 = blockIdx.y * MD_S, h0 = blockIdx.x * MD_H;
+  const int64_t base = (static_cast<int64_t>(l) * 3 + 2) * S * static_cast<int64_t>(H);
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;   // 8 warps
+#pragma unroll
+  for (int k = 0; k < MD_S / 8; ++k) {
+    const int s = s0 + ty + 8 * k, h = h0 + tx;
+    tile[ty + 8 * k][tx] = (s < S && h < H) ? w[base + static_cast<int64_t>(s) * H + h] : 0.f;
+  }
+  __syncthreads();
+  uint16_t* dst = wdp[l];
+#pragma unroll
+  for (int k = 0; k < MD_H / 8; ++k) {
+    const int hh = ty + 8 * k, h = h0 + hh;
+    const int s = s0 + 2 * tx;
+    if (h >= H || s >= S) continue;
+    uint16_t* p = dst + static_cast<int64_t>(h) * mt.ffn + mt.f_pad + s;
+    const uint16_t lo = f32_to_bf16_bits(tile[2 * tx][hh]);
+    if (s + 1 < S) {
+      const uint16_t hi = f32_to_bf16_bits(tile[2 * tx + 1][hh]);
+      *reinterpret_cast<uint32_t*>(p) = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+    } else {
+      *p = lo;
+    }
+  }
+}
+
 __global__ void mirror_kernel(const float* __restrict__ w, int64_t n, int64_t SH, int H,
-                              MirrorTargets mt, uint16_t* const* gu, uint16_t* const* wdp) {
+                              MirrorTargets mt, uint16_t* const* gu, uint16_t* const* wdp,
+                              int skip_down) {
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t proj = i / SH;
     const int64_t r = i - proj * SH;
+    if (skip_down && proj % 3 == 2) continue;
     write_mirror(mt, gu, wdp, i, static_cast<int>(proj / 3), static_cast<int>(proj % 3),
                  static_cast<int>(r / H), static_cast<int>(r % H), w[i]);
   }
@@ -437,15 +537,49 @@ __global__ void shadow_bake_fused_kernel(const float* __restrict__ g, int64_t n,
 }
 
 // ------------------------------- bake --------------------------------------
-__global__ void shadow_bake_kernel(uint16_t* base, int64_t stride, const float* __restrict__ g,
-                                   int S, int H, int i0, int h0, int mode) {
-  const int s = blockIdx.x;
-  if (s >= S) return;
-  for (int h = threadIdx.x; h < H; h += blockDim.x) {
-    const float d = g[static_cast<int64_t>(s) * H + h];
-    const int64_t idx = (mode == 0) ? static_cast<int64_t>(i0 + s) * stride + (h0 + h)
-                                    : static_cast<int64_t>(h0 + h) * stride + (i0 + s);
-    base[idx] = f32_to_bf16_bits(bf16_bits_to_f32(base[idx]) + d);
+// base += graft, one 64 x 64 (s, h) tile per CTA.  The graft tile is read
+// along h and kept in shared memory; the base is then updated along its own
+// rows (h for expand, s for contract, where the tile is read transposed) two
+// bf16 at a time, so both sides stay coalesced.  Each element is still
+// bf16(f32(base) + graft) with round-to-nearest-even, as in the reference.
+constexpr int BAKE_T = 64;
+__device__ __forceinline__ void bake_pair(uint16_t* base, int64_t idx, bool two, float d0, float d1) {
+  if (two && (idx & 1) == 0) {
+    uint32_t* p = reinterpret_cast<uint32_t*>(base + idx);
+    const uint32_t w = *p;
+    const uint16_t lo = f32_to_bf16_bits(bf16_bits_to_f32(static_cast<uint16_t>(w & 0xFFFFu)) + d0);
+    const uint16_t hi = f32_to_bf16_bits(bf16_bits_to_f32(static_cast<uint16_t>(w >> 16)) + d1);
+    *p = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+  } else {
+    base[idx] = f32_to_bf16_bits(bf16_bits_to_f32(base[idx]) + d0);
+    if (two) base[idx + 1] = f32_to_bf16_bits(bf16_bits_to_f32(base[idx + 1]) + d1);
+  }
+}
+
+__global__ void __launch_bounds__(256) shadow_bake_kernel(uint16_t* base, int64_t stride,
+                                                          const float* __restrict__ g, int S, int H,
+                                                          int i0, int h0, int mode) {
+  __shared__ float tile[BAKE_T][BAKE_T + 1];   // [s][h]
+  const int s0 = blockIdx.y * BAKE_T, hb = blockIdx.x * BAKE_T;
+  for (int k = threadIdx.x; k < BAKE_T * BAKE_T; k += blockDim.x) {
+    const int ts = k / BAKE_T, th = k % BAKE_T;
+    const int s = s0 + ts, h = hb + th;
+    tile[ts][th] = (s < S && h < H) ? g[static_cast<int64_t>(s) * H + h] : 0.f;
+  }
+  __syncthreads();
+  for (int k = threadIdx.x; k < BAKE_T * BAKE_T / 2; k += blockDim.x) {
+    const int row = k / (BAKE_T / 2), col = 2 * (k % (BAKE_T / 2));
+    if (mode == 0) {   // base row i0 + s, columns h0 + h, h0 + h + 1
+      const int s = s0 + row, h = hb + col;
+      if (s >= S || h >= H) continue;
+      bake_pair(base, static_cast<int64_t>(i0 + s) * stride + h0 + h, h + 1 < H, tile[row][col],
+                tile[row][col + 1]);
+    } else {           // base row h0 + h, columns i0 + s, i0 + s + 1
+      const int h = hb + row, s = s0 + col;
+      if (h >= H || s >= S) continue;
+      bake_pair(base, static_cast<int64_t>(h0 + h) * stride + i0 + s, s + 1 < S, tile[col][row],
+                tile[col + 1][row]);
+    }
   }
 }
 
@@ -620,9 +754,29 @@ int adamw_step(float* w, const float* grad, float* m, float* v, int L, int S, in
   const int64_t n = SH * 3 * L;
   MirrorTargets mt{};
   if (mirror) mt = *mirror;
-  adamw_kernel<<<grid_for(n, 256), 256, 0, st>>>(w, grad, m, v, n, SH, H, a, stats, mt,
-                                                  mirror ? mirror->w_gu : nullptr,
-                                                  mirror ? mirror->w_d : nullptr);
+  uint16_t* const* gu = mirror ? mirror->w_gu : nullptr;
+  uint16_t* const* wdp = mirror ? mirror->w_d : nullptr;
+  if (SH % 4 != 0 || H % 4 != 0) {   // shapes the vector kernel cannot take
+    adamw_kernel<<<grid_for(n, 256), 256, 0, st>>>(w, grad, m, v, n, SH, H, a, stats, mt, gu, wdp);
+    GLT_LAUNCH_CHECK();
+    return GLT_OK;
+  }
+  const bool tiled_down = gu != nullptr && !mt.plain && kinds[2] && mt.kinds[2];
+  adamw_vec_kernel<<<grid_for(n / 4, 256), 256, 0, st>>>(w, grad, m, v, n, SH, H, a, stats, mt, gu,
+                                                          wdp, tiled_down ? 1 : 0);
+  GLT_LAUNCH_CHECK();
+  if (tiled_down) GLT_TRY(mirror_down(w, L, S, H, mt, st));
+  return GLT_OK;
+}
+
+int mirror_down(const float* w, int L, int S, int H, const MirrorTargets& mirror, cudaStream_t st) {
+  MirrorTargets mt = mirror;   // grafted layers, clamped to the model's
+  if (mt.layer_begin < 0) mt.layer_begin = 0;
+  if (mt.layer_end > L - 1) mt.layer_end = L - 1;
+  const int layers = mt.layer_end - mt.layer_begin + 1;
+  if (layers <= 0 || S <= 0 || H <= 0 || !mt.w_d || !mt.kinds[2]) return GLT_OK;
+  dim3 grid((H + MD_H - 1) / MD_H, (S + MD_S - 1) / MD_S, layers);
+  mirror_down_kernel<<<grid, 256, 0, st>>>(w, S, H, mt, mt.w_d);
   GLT_LAUNCH_CHECK();
   return GLT_OK;
 }
@@ -631,8 +785,11 @@ int refresh_mirror(const float* w, int L, int S, int H, const MirrorTargets& mir
                    cudaStream_t st) {
   const int64_t SH = static_cast<int64_t>(S) * H;
   const int64_t n = SH * 3 * L;
-  mirror_kernel<<<grid_for(n, 256), 256, 0, st>>>(w, n, SH, H, mirror, mirror.w_gu, mirror.w_d);
+  const bool tiled_down = mirror.w_d != nullptr && !mirror.plain && mirror.kinds[2];
+  mirror_kernel<<<grid_for(n, 256), 256, 0, st>>>(w, n, SH, H, mirror, mirror.w_gu, mirror.w_d,
+                                                   tiled_down ? 1 : 0);
   GLT_LAUNCH_CHECK();
+  if (tiled_down) GLT_TRY(mirror_down(w, L, S, H, mirror, st));
   return GLT_OK;
 }
 
@@ -649,7 +806,8 @@ int shadow_bake_fused(const float* g, int L, int S, int H, int i0, int h0,
 int shadow_bake(uint16_t* base, int64_t base_stride, const float* g, int S, int H, int i0, int h0,
                 int mode, cudaStream_t st) {
   if (S <= 0 || H <= 0) return GLT_OK;
-  shadow_bake_kernel<<<S, 256, 0, st>>>(base, base_stride, g, S, H, i0, h0, mode);
+  dim3 grid((H + BAKE_T - 1) / BAKE_T, (S + BAKE_T - 1) / BAKE_T);
+  shadow_bake_kernel<<<grid, 256, 0, st>>>(base, base_stride, g, S, H, i0, h0, mode);
   GLT_LAUNCH_CHECK();
   return GLT_OK;
 }

@@ -92,6 +92,9 @@ struct MirrorTargets {
 // Fused AdamW over all 3L projections with the clip scale read on the device;
 // disabled projection kinds are skipped (kernels_optimizer_impl.inc:11-77).
 // Also refreshes the bf16 mirror inside the concat weights.
+// bf16 image of the grafted down projections in W_d_cat (a shared-memory
+// staged transpose of the [S, H] fp32 graft).
+int mirror_down(const float* w, int L, int S, int H, const MirrorTargets& mt, cudaStream_t st);
 int adamw_step(float* w, const float* grad, float* m, float* v, int L, int S, int H, float lr,
                float beta1, float beta2, float eps, float wd, int step, const int* kinds_enabled,
                const DevStats* stats, const MirrorTargets* mirror, cudaStream_t st);

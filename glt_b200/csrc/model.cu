@@ -554,7 +554,7 @@ int Model::ffn_forward(int l, const uint16_t* x_in, uint16_t* x_out, float* var_
   // Non-grafted layers skip the graft columns; after a shadow bake they are
   // base columns and stay in the GEMMs (without the graft-side energies).
   const int ff = (grafted || (shadow_baked && any)) ? FF : F_pad;
-  GLT_TRY(rmsnorm_fwd(x_in, y.post_norm, y.x_ffn, var_out, M, D, cfg.rms_norm_eps, st));
+  GLT_PROF(GLT_PROF_RMSNORM, rmsnorm_fwd(x_in, y.post_norm, y.x_ffn, var_out, M, D, cfg.rms_norm_eps, st));
   // gate/up + SwiGLU (+ graft energies)
   {
     EpiSwiGLUFwd e{h, FF, M, F_pad, F_pad + S,
@@ -581,9 +581,9 @@ int Model::ffn_forward(int l, const uint16_t* x_in, uint16_t* x_out, float* var_
 int Model::forward_layer(int l, bool use_graft, cudaStream_t st) {
   Layer& y = layers[l];
   AttnShape as{B, T, nh, nkv, hd, QKV, AD, 1.0f / sqrtf(static_cast<float>(hd))};
-  GLT_TRY(rmsnorm_fwd(xs[l], y.in_norm, xn, y.var1, M, D, cfg.rms_norm_eps, st));
+  GLT_PROF(GLT_PROF_RMSNORM, rmsnorm_fwd(xs[l], y.in_norm, xn, y.var1, M, D, cfg.rms_norm_eps, st));
   GLT_PROF(GLT_PROF_QKV, g_bf16(kmaj(xn, D), kmaj(y.wqkv, D), M, QKV, D, y.qkv, QKV, nullptr, 0, st));
-  if (rope_on(l)) GLT_TRY(rope_apply(y.qkv, as, cos_t, sin_t, 0, 1, 1, st));
+  if (rope_on(l)) GLT_PROF(GLT_PROF_ROPE, rope_apply(y.qkv, as, cos_t, sin_t, 0, 1, 1, st));
   // tcgen05/TMEM kernel for 128-token tiles; the mma.sync kernel covers seq_len % 128 != 0
   if (T % 128 == 0)
     GLT_PROF(GLT_PROF_ATTN_FWD, flash_fwd_tc(y.qkv, y.o, y.lse, as, st));
@@ -648,16 +648,16 @@ int Model::backward_layer(int l, cudaStream_t st) {
     GLT_TRY(dp_allreduce_layer(l));
   }
   // post-attention RMSNorm backward + residual: dx = grad wrt x_post
-  GLT_TRY(rmsnorm_bwd(dtmp, y.x_post, y.post_norm, y.var2, dx, dx, dy_b, M, D, cfg.rms_norm_eps, st));
+  GLT_PROF(GLT_PROF_RMSNORM, rmsnorm_bwd(dtmp, y.x_post, y.post_norm, y.var2, dx, dx, dy_b, M, D, cfg.rms_norm_eps, st));
   // attention: do = dx_post . Wo ; flash backward ; RoPE^T ; dxn = dqkv . Wqkv
   GLT_PROF(GLT_PROF_DO, g_bf16(kmaj(dy_b, D), mnmaj(y.wo, AD), M, AD, D, dout_b, AD, nullptr, 0, st));
   if (hd == 128 && T % 128 == 0)
     GLT_PROF(GLT_PROF_ATTN_BWD, flash_bwd_tc(y.qkv, y.o, dout_b, y.lse, dqkv, dq_acc, dsum, as, st));
   else
     GLT_PROF(GLT_PROF_ATTN_BWD, flash_bwd(y.qkv, y.o, dout_b, y.lse, dqkv, dq_acc, dsum, as, st));
-  if (rope_on(l)) GLT_TRY(rope_apply(dqkv, as, cos_t, sin_t, 1, 1, 1, st));
+  if (rope_on(l)) GLT_PROF(GLT_PROF_ROPE, rope_apply(dqkv, as, cos_t, sin_t, 1, 1, 1, st));
   GLT_PROF(GLT_PROF_DX_QKV, g_f32(kmaj(dqkv, QKV), mnmaj(y.wqkv, D), M, D, QKV, dtmp, D, st));
-  GLT_TRY(rmsnorm_bwd(dtmp, xs[l], y.in_norm, y.var1, dx, dx, nullptr, M, D, cfg.rms_norm_eps, st));
+  GLT_PROF(GLT_PROF_RMSNORM, rmsnorm_bwd(dtmp, xs[l], y.in_norm, y.var1, dx, dx, nullptr, M, D, cfg.rms_norm_eps, st));
   return GLT_OK;
 }
 
@@ -673,7 +673,7 @@ int Model::load_inputs(const int32_t* ids_in, const int32_t* ood_in, int host, c
 int Model::forward_all(bool use_graft, cudaStream_t st) {
   GLT_TRY(embedding_fwd(ids, embed, xs[0], M, D, V, st));
   for (int l = 0; l < L; ++l) GLT_TRY(forward_layer(l, use_graft, st));
-  GLT_TRY(rmsnorm_fwd(xs[L], final_norm, xf, varf, M, D, cfg.rms_norm_eps, st));
+  GLT_PROF(GLT_PROF_RMSNORM, rmsnorm_fwd(xs[L], final_norm, xf, varf, M, D, cfg.rms_norm_eps, st));
   return GLT_OK;
 }
 
@@ -697,7 +697,7 @@ int Model::train_step(const int32_t* ids_in, const int32_t* ood_in, int host, in
   }
   GLT_TRY(silence_stats(esq_all, d_enabled, L, M, S, H, ood, stats, st));
   GLT_TRY(finalize_loss(stats, cfg.lambda_silence, active_grafts, cfg.lm_loss_scale, st));
-  GLT_TRY(rmsnorm_bwd(dtmp, xs[L], final_norm, varf, nullptr, dx, nullptr, M, D, cfg.rms_norm_eps, st));
+  GLT_PROF(GLT_PROF_RMSNORM, rmsnorm_bwd(dtmp, xs[L], final_norm, varf, nullptr, dx, nullptr, M, D, cfg.rms_norm_eps, st));
   for (int l = L - 1; l >= 0; --l) GLT_TRY(backward_layer(l, st));
   return finish_step(step, total_steps, out, st);
 }
@@ -715,12 +715,12 @@ int Model::finish_step(int step, int total_steps, GltStepStats* out, cudaStream_
     GLT_CUDA_TRY(cudaStreamWaitEvent(st, comm_done, 0));
   }
   // DP: the all-reduce summed the ranks' grads; 1/world turns the sum into the mean.
-  GLT_TRY(grad_clip_scale(grad, graft_numel, cfg.gradient_clip_norm, 1.0f / dp_world, stats, st));
+  GLT_PROF(GLT_PROF_ADAMW, grad_clip_scale(grad, graft_numel, cfg.gradient_clip_norm, 1.0f / dp_world, stats, st));
   const float lr = get_lr(&cfg, step, total_steps);
   last_lr = lr;
   const int kinds[3] = {cfg.graft_proj_gate, cfg.graft_proj_up, cfg.graft_proj_down};
   MirrorTargets mt = mirror();
-  GLT_TRY(adamw_step(gw, grad, adam_m, adam_v, L, S, H, lr, cfg.adam_beta1, cfg.adam_beta2,
+  GLT_PROF(GLT_PROF_ADAMW, adamw_step(gw, grad, adam_m, adam_v, L, S, H, lr, cfg.adam_beta1, cfg.adam_beta2,
                      cfg.adam_eps, cfg.adam_weight_decay, step, kinds, stats, &mt, st));
   if (out) {
     GLT_CUDA_TRY(cudaMemcpyAsync(pinned_stats, stats, sizeof(DevStats), cudaMemcpyDeviceToHost, st));
@@ -768,7 +768,7 @@ int Model::block_step(const uint16_t* x, const float* y_t, float lr, int step, f
   const int kinds[3] = {cfg.graft_proj_gate, cfg.graft_proj_up, cfg.graft_proj_down};
   MirrorTargets mt = mirror();
   GLT_TRY(set_clip_scale(stats, 1.0f, st));
-  GLT_TRY(adamw_step(gw, grad, adam_m, adam_v, L, S, H, lr, cfg.adam_beta1, cfg.adam_beta2,
+  GLT_PROF(GLT_PROF_ADAMW, adamw_step(gw, grad, adam_m, adam_v, L, S, H, lr, cfg.adam_beta1, cfg.adam_beta2,
                      cfg.adam_eps, cfg.adam_weight_decay, step, kinds, stats, &mt, st));
   if (loss) {
     GLT_CUDA_TRY(cudaMemcpyAsync(pinned_stats, stats, sizeof(DevStats), cudaMemcpyDeviceToHost, st));
@@ -790,6 +790,8 @@ int Model::activation(int which, int layer, void** ptr, int64_t* numel) {
     case 4: if (!y) break; *ptr = y->x_ffn; *numel = static_cast<int64_t>(M) * D; return GLT_OK;
     case 5: if (!y) break; *ptr = y->esq; *numel = static_cast<int64_t>(M) * 3; return GLT_OK;
     case 6: if (!dec) break; *ptr = xf; *numel = static_cast<int64_t>(M) * D; return GLT_OK;
+    case 7: if (!y || overlay) break; *ptr = y->w_gu; *numel = 2 * static_cast<int64_t>(FF) * D; return GLT_OK;
+    case 8: if (!y || overlay) break; *ptr = y->w_d; *numel = static_cast<int64_t>(D) * FF; return GLT_OK;
     default: break;
   }
   return fail(GLT_EINVAL, "activation %d unavailable for layer %d", which, layer);

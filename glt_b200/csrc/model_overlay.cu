@@ -61,7 +61,7 @@ int Model::ffn_forward_overlay(int l, const uint16_t* x_in, uint16_t* x_out, flo
   const bool g = use_graft && enabled[3 * l], u = use_graft && enabled[3 * l + 1];
   const bool d = use_graft && enabled[3 * l + 2];
   const int64_t SH = static_cast<int64_t>(S) * H;
-  GLT_TRY(rmsnorm_fwd(x_in, y.post_norm, y.x_ffn, var_out, M, D, cfg.rms_norm_eps, st));
+  GLT_PROF(GLT_PROF_RMSNORM, rmsnorm_fwd(x_in, y.post_norm, y.x_ffn, var_out, M, D, cfg.rms_norm_eps, st));
   if (g || u) GLT_PROF(GLT_PROF_DELTA_EXPAND, expand_deltas(l, g, u, y.esq, y.esq + M, st));
   {
     EpiSwiGLUFwdOv e{h, FF, M, g ? dlt : nullptr, u ? dlt + S : nullptr, 2 * static_cast<int64_t>(S),

@@ -24,7 +24,7 @@ W_EMBED, W_LM_HEAD, W_FINAL_NORM, W_IN_NORM, W_Q, W_K, W_V, W_O, W_POST_NORM, W_
 PROF_NAMES = ["gate_up_fwd", "down_fwd", "delta_down", "qkv", "o_proj", "attn_fwd", "dh",
               "recompute_swiglu_bwd", "wgrad_down", "wgrad_gate_up", "dx_gate_up", "do",
               "attn_bwd", "dx_qkv", "lm_head", "lm_dx", "cross_entropy", "delta_expand",
-              "graft_dgrad"]
+              "graft_dgrad", "rmsnorm", "rope", "adamw"]
 PROF_KINDS = len(PROF_NAMES)
 
 

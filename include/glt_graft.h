@@ -160,6 +160,24 @@ GLT_API int glt_shadow_bake(uint16_t* base, int64_t base_stride, const float* gr
 /* (declared after GltModelConfig below) */
 
 /* ------------------------------------------------------------------------ */
+/* SwiGLU as stand-alone ops (the fused training step computes both inside  */
+/* its GEMM epilogues).  bf16 = uint16 bit patterns; fp32 gradients.        */
+/* glt_swiglu_fwd replaces fused_silu_product_strided_kernel                */
+/*   (kernels_elementwise_impl.inc:411-448): out[r, c] =                    */
+/*   bf16(silu(gate_pre[r, c]) * up[r, c]) over rows x width, each operand  */
+/*   with its own row stride (elements).  width and strides multiples of 8, */
+/*   pointers 16-byte aligned, else GLT_EINVAL.                             */
+/* glt_swiglu_bwd replaces fused_gate_up_bwd_kernel                         */
+/*   (kernels_elementwise_impl.inc:80-124): with sg = sigmoid(gp),          */
+/*   grad_gate_pre = grad_h * up * sg * (1 + gp * (1 - sg)),                */
+/*   grad_up = grad_h * gp * sg, over n contiguous elements (n % 8 == 0).   */
+/* ------------------------------------------------------------------------ */
+GLT_API int glt_swiglu_fwd(const uint16_t* gate_pre, const uint16_t* up, uint16_t* out, int rows,
+                           int width, int64_t gate_ld, int64_t up_ld, int64_t out_ld, void* stream);
+GLT_API int glt_swiglu_bwd(float* grad_gate_pre, float* grad_up, const float* grad_h,
+                           const uint16_t* up, const uint16_t* gate_pre, int64_t n, void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* Layer kernels for callers that run their own layer loop.                 */
 /* qkv: packed rows [q heads | k heads | v heads] of B*T tokens (ld_qkv     */
 /* elements per row), bf16; o / dout: [B*T, nh*hd] rows with ld_o; lse:     */
@@ -230,6 +248,18 @@ GLT_API int glt_config_validate(const GltModelConfig* cfg, int batch_size, int m
 GLT_API float glt_get_lr(const GltModelConfig* cfg, int step, int total_steps);
 /* Flat offset of projection p of layer l in [3L,S,H] (src/graft_ops_impl.inc:5-7). */
 GLT_API int64_t glt_delta_offset(int layer, int proj, int slice_dim, int h_slice_dim);
+/* glt_adamw_all replaces execute_adamw_all + adamw_fused_kernel             */
+/* (kernels_optimizer_impl.inc:11-77): one AdamW step over the flat          */
+/* [3L, S, H] graft (weights, grads, adam_m, adam_v fp32, 16-byte aligned), */
+/* bias corrections 1/(1-beta^(step+1)), decoupled weight decay, projection */
+/* kinds disabled in cfg skipped entirely.  weights_bf16 (nullable, 8-byte  */
+/* aligned) receives the RNE bf16 image at the same flat index.  grad_scale */
+/* (nullable device pointer) multiplies every gradient (the clip scale).    */
+/* Hyper-parameters come from cfg (adam_beta1/2, adam_eps,                  */
+/* adam_weight_decay); S * H must be a multiple of 4.                       */
+GLT_API int glt_adamw_all(float* weights, uint16_t* weights_bf16, const float* grads,
+                          float* adam_m, float* adam_v, const float* grad_scale,
+                          const GltModelConfig* cfg, int step, float lr, void* stream);
 
 /* apply_graft_to_shadow (src/shadow_bake_impl.inc:58-128); see glt_shadow_bake. */
 GLT_API int glt_apply_graft_to_shadow(const GltModelConfig* cfg, uint16_t* const* gate,
@@ -355,7 +385,11 @@ GLT_API int glt_block_step(GltModel* m, const uint16_t* x, const float* y, float
 
 /* Saved activations for tests: which = 0 residual input of layer, 1 qkv,
  * 2 attention output, 3 x_post_attn, 4 x_ffn, 5 per-token energy sums
- * [3][M] fp32 (sum of squares of the gate/up/down deltas), 6 final hidden. */
+ * [3][M] fp32 (sum of squares of the gate/up/down deltas), 6 final hidden;
+ * concat geometry only: 7 the layer's fused gate/up weights [2F' x D] bf16
+ * (intermediate column c at row 256*(c/128) + c%128, +128 for up; graft
+ * column s at c = F_pad + s, F_pad = F rounded up to 256), 8 its fused down
+ * weights [D x F'] bf16 (F' = F_pad + S rounded up to 128). */
 GLT_API int glt_model_activation(GltModel* m, int which, int layer, void** ptr, int64_t* numel);
 
 /* Per-kind kernel timing: CUDA events recorded on the launching stream around
@@ -382,7 +416,10 @@ GLT_API int glt_model_activation(GltModel* m, int which, int layer, void** ptr, 
 #define GLT_PROF_CE 16
 #define GLT_PROF_DELTA_EXPAND 17 /* overlay: x_h.Delta_{gate,up}^T (+ energy) */
 #define GLT_PROF_GRAFT_DGRAD 18  /* overlay: dyh.Delta_down^T, dys.Delta_gu  */
-#define GLT_PROF_KINDS 19
+#define GLT_PROF_RMSNORM 19      /* RMSNorm forward and backward            */
+#define GLT_PROF_ROPE 20         /* RoPE on q/k and its transpose on dq/dk  */
+#define GLT_PROF_ADAMW 21        /* grad clip norm + AdamW + bf16 image     */
+#define GLT_PROF_KINDS 22
 GLT_API int glt_model_profile(GltModel* m, int enable);
 GLT_API int glt_model_profile_read(GltModel* m, double* ms, int64_t* launches, int reset);
 

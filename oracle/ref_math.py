@@ -491,3 +491,19 @@ def init_weights(cfg: GraftConfig, seed: int = 0, std: float = 0.02):
     embed = rn(V, D) if V > 0 else None
     lm_head = embed if cfg.tie_embeddings else (rn(V, D) if V > 0 else None)
     return dict(embed=embed, lm_head=lm_head, final_norm=torch.ones(D), layers=layers)
+
+
+def silu_product(gate_pre: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """fused_silu_product_strided_kernel (kernels_elementwise_impl.inc:411-448):
+    bf16(gp * sigmoid(gp) * up) from bf16 operands, fp32 math."""
+    g, u = gate_pre.float(), up.float()
+    return (g * torch.sigmoid(g) * u).to(torch.bfloat16)
+
+
+def gate_up_backward(grad_h: torch.Tensor, up: torch.Tensor, gate_pre: torch.Tensor):
+    """fused_gate_up_bwd_kernel (kernels_elementwise_impl.inc:80-124):
+    sg = sigmoid(gp); grad_gate_pre = gi * up * sg * (1 + gp * (1 - sg));
+    grad_up = gi * gp * sg (fp32 outputs)."""
+    g, u, gi = gate_pre.float(), up.float(), grad_h.float()
+    sg = torch.sigmoid(g)
+    return gi * u * (sg * (1 + g * (1 - sg))), gi * (g * sg)

@@ -85,6 +85,7 @@ SIGNATURES: dict[str, tuple] = {
     "glt_adamw_all": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _f32, _vp]),
     "glt_swiglu_fwd": (_i32, [_vp, _vp, _vp, _i32, _i32, _i64, _i64, _i64, _vp]),
     "glt_swiglu_bwd": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _vp]),
+    "glt_stack_grafts": (_i32, [C.POINTER(_vp), _i32, _i32, _i32, _i32, _vp, _vp]),
     "glt_model_create": (_i32, [_cfgp, _i32, _i32, _i32, C.POINTER(_vp)]),
     "glt_model_destroy": (_i32, [_vp]),
     "glt_model_memory": (_i32, [_vp, C.POINTER(_i64), C.POINTER(_i64)]),

@@ -6,6 +6,9 @@
 //                    kernels_elementwise_impl.inc:411-448)
 //   glt_swiglu_bwd  grad_gate_pre = gi * up * silu'(gp), grad_up = gi * silu(gp)
 //                   (fused_gate_up_bwd_kernel, kernels_elementwise_impl.inc:80-124)
+//   glt_stack_grafts  N sibling grafts -> one block-diagonal overlay graft
+//                   (the explicit-injection stack of
+//                    tests/test6_stack_vs_bake_f32.cpp, as one graft)
 //   glt_adamw_all   AdamW over every projection of the flat [3L, S, H] graft,
 //                   skipping disabled projection kinds, optional bf16 image at
 //                   the same flat index (adamw_fused_kernel + execute_adamw_all,
@@ -116,6 +119,33 @@ __global__ void adamw_flat_kernel(float* __restrict__ w, uint16_t* __restrict__ 
   }
 }
 
+constexpr int MAX_STACK = 8;
+struct StackSrc {
+  const float* g[MAX_STACK];
+};
+
+// out[p, r, c] of a [3L, n*S, n*H] graft = g_d[p, r - dS, c - dH] when row r
+// and column c fall in the same domain d, else 0 (block-diagonal stack).
+__global__ void stack_grafts_kernel(StackSrc src, int n, int64_t projs, int S, int H,
+                                    float* __restrict__ out) {
+  const int64_t W = static_cast<int64_t>(n) * H;          // output row width
+  const int64_t nvec = projs * n * S * (W >> 2);          // 4 floats per vector (H % 4 == 0)
+  for (int64_t q = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; q < nvec;
+       q += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t e = q << 2;
+    const int64_t row = e / W;                             // p * n*S + r
+    const int c = static_cast<int>(e - row * W);
+    const int64_t p = row / (static_cast<int64_t>(n) * S);
+    const int r = static_cast<int>(row - p * n * S);
+    const int dr = r / S, dc = c / H;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (dr == dc)
+      v = *reinterpret_cast<const float4*>(src.g[dr] + (p * S + (r - dr * S)) * static_cast<int64_t>(H) +
+                                           (c - dc * H));
+    *reinterpret_cast<float4*>(out + e) = v;
+  }
+}
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // Grid for a grid-stride loop over n units: at most 16 CTAs per SM.
@@ -197,6 +227,28 @@ extern "C" int glt_adamw_all(float* weights, uint16_t* weights_bf16, const float
   a.en[2] = cfg->graft_proj_down;
   glt::adamw_flat_kernel<<<glt::ew_grid(n / 4, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       weights, weights_bf16, grads, adam_m, adam_v, grad_scale, n, SH, a);
+  GLT_LAUNCH_CHECK();
+  return GLT_OK;
+}
+
+extern "C" int glt_stack_grafts(const float* const* grafts, int n, int num_layers, int S, int H,
+                                float* out, void* stream) {
+  if (!grafts || !out) return glt::fail(GLT_EINVAL, "null argument");
+  if (n < 1 || n > glt::MAX_STACK)
+    return glt::fail(GLT_EINVAL, "stack of %d grafts: between 1 and %d supported", n, glt::MAX_STACK);
+  if (num_layers <= 0 || S <= 0 || H <= 0) return glt::fail(GLT_EINVAL, "empty graft");
+  if (H % 4) return glt::fail(GLT_EINVAL, "stack: h_slice_dim must be a multiple of 4");
+  glt::StackSrc src{};
+  for (int d = 0; d < n; ++d) {
+    if (!grafts[d]) return glt::fail(GLT_EINVAL, "stack: graft %d is null", d);
+    if (!glt::aligned16(grafts[d])) return glt::fail(GLT_EINVAL, "stack: graft %d not 16-byte aligned", d);
+    src.g[d] = grafts[d];
+  }
+  if (!glt::aligned16(out)) return glt::fail(GLT_EINVAL, "stack: output not 16-byte aligned");
+  const int64_t projs = 3 * static_cast<int64_t>(num_layers);
+  const int64_t nvec = projs * n * S * (static_cast<int64_t>(n) * H / 4);
+  glt::stack_grafts_kernel<<<glt::ew_grid(nvec, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      src, n, projs, S, H, out);
   GLT_LAUNCH_CHECK();
   return GLT_OK;
 }

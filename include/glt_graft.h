@@ -248,6 +248,18 @@ GLT_API int glt_config_validate(const GltModelConfig* cfg, int batch_size, int m
 GLT_API float glt_get_lr(const GltModelConfig* cfg, int step, int total_steps);
 /* Flat offset of projection p of layer l in [3L,S,H] (src/graft_ops_impl.inc:5-7). */
 GLT_API int64_t glt_delta_offset(int layer, int proj, int slice_dim, int h_slice_dim);
+/* glt_stack_grafts: a stack of n sibling grafts of the overlay geometry     */
+/* (domains 0..n-1 of one session, each a flat [3L, S, H] fp32 device       */
+/* buffer, H = hidden / max_domains) -> one [3L, n*S, n*H] graft whose       */
+/* projections are block-diagonal: domain d at rows [dS, (d+1)S) and columns */
+/* [dH, (d+1)H), zeros elsewhere.  Loaded as the graft of a model with       */
+/* slice_dim n*S, max_domains 1 and domain_id 0, it injects every domain's   */
+/* delta into the reference's slice for that domain -- the explicit stack of */
+/* tests/test6_stack_vs_bake_f32.cpp -- and glt_model_shadow_bake bakes all  */
+/* n at once (zero blocks leave the bf16 base bits unchanged).  grafts is a  */
+/* host array of n (<= 8) device pointers; out is device memory; H % 4 == 0. */
+GLT_API int glt_stack_grafts(const float* const* grafts, int n, int num_layers, int S, int H,
+                             float* out, void* stream);
 /* glt_adamw_all replaces execute_adamw_all + adamw_fused_kernel             */
 /* (kernels_optimizer_impl.inc:11-77): one AdamW step over the flat          */
 /* [3L, S, H] graft (weights, grads, adam_m, adam_v fp32, 16-byte aligned), */

@@ -507,3 +507,65 @@ def gate_up_backward(grad_h: torch.Tensor, up: torch.Tensor, gate_pre: torch.Ten
     g, u, gi = gate_pre.float(), up.float(), grad_h.float()
     sg = torch.sigmoid(g)
     return gi * u * (sg * (1 + g * (1 - sg))), gi * (g * sg)
+
+
+# ---------------------------------------------------------------------------
+# Graft stacks: sibling grafts of several domains active at once
+# ---------------------------------------------------------------------------
+def mlp_forward_stack(x_ffn: torch.Tensor, lw, deltas: list, cfg: GraftConfig, l: int):
+    """MLP forward with the grafts of domains 0..N-1 injected explicitly, each
+    into its own overlay slice (i0 = d*S, h0 = d*H): path A of
+    tests/test6_stack_vs_bake_f32.cpp:66-163 (gate and up deltas added to the
+    pre-activations, silu(gate)*up, base down GEMM, down deltas added to the
+    output), extended from two domains to N and from one MLP to a layer."""
+    S, H = cfg.slice_dim, cfg.hidden_dim // cfg.max_domains
+    wg, wu, wd = lw["wg"], lw["wu"], lw["wd"]
+    gp = x_ffn @ wg.t()
+    up = x_ffn @ wu.t()
+    for d, delta in enumerate(deltas):
+        i0, h0 = d * S, d * H
+        x_h = x_ffn[:, h0:h0 + H]
+        if cfg.should_graft_proj(l, PROJ_GATE):
+            gp[:, i0:i0 + S] += x_h @ delta_view_at(delta, cfg, l, PROJ_GATE, S, H).t()
+        if cfg.should_graft_proj(l, PROJ_UP):
+            up[:, i0:i0 + S] += x_h @ delta_view_at(delta, cfg, l, PROJ_UP, S, H).t()
+    h = torch.nn.functional.silu(gp) * up
+    ffn = h @ wd.t()
+    for d, delta in enumerate(deltas):
+        i0, h0 = d * S, d * H
+        if cfg.should_graft_proj(l, PROJ_DOWN):
+            ffn[:, h0:h0 + H] += h[:, i0:i0 + S] @ delta_view_at(delta, cfg, l, PROJ_DOWN, S, H)
+    return ffn
+
+
+def delta_view_at(delta: torch.Tensor, cfg: GraftConfig, l: int, p: int, S: int, H: int):
+    """[S, H] view of projection (l, p) of a flat [3L, S, H] graft (delta_offset)."""
+    off = (l * 3 + p) * S * H
+    return delta.view(-1)[off:off + S * H].view(S, H)
+
+
+def model_forward_stack(ids, weights, deltas: list, cfg: GraftConfig):
+    """forward_model (grafting.hip:224-271) with a stack of N domain grafts,
+    each injected explicitly (mlp_forward_stack).  Returns logits [B, T, V]."""
+    x = weights["embed"][ids.long()]
+    B, T, D = x.shape
+    for l in range(cfg.num_layers):
+        lw = weights["layers"][l]
+        x_post = attention_block(x, lw, cfg, l)
+        x_ffn, _ = rms_norm(x_post, lw["post_norm"], cfg.rms_norm_eps)
+        x = x_post + mlp_forward_stack(x_ffn.reshape(B * T, D), lw, deltas, cfg, l).view(B, T, D)
+    xn, _ = rms_norm(x, weights["final_norm"], cfg.rms_norm_eps)
+    return xn @ weights["lm_head"].t()
+
+
+def stack_grafts(deltas: list, num_layers: int, S: int, H: int) -> torch.Tensor:
+    """N sibling grafts [3L, S, H] -> one [3L, N*S, N*H] graft whose
+    projection blocks are block-diagonal (domain d at rows [dS, (d+1)S) and
+    columns [dH, (d+1)H)).  As one overlay graft at i0 = h0 = 0 it computes
+    exactly the N explicit injections (the off-diagonal zeros add nothing)
+    and bakes to the same base (bf16(base + 0) == base)."""
+    N = len(deltas)
+    out = torch.zeros(3 * num_layers, N * S, N * H, dtype=torch.float32)
+    for d, delta in enumerate(deltas):
+        out[:, d * S:(d + 1) * S, d * H:(d + 1) * H] = delta.view(3 * num_layers, S, H)
+    return out.view(-1)

@@ -177,3 +177,35 @@ def test_mlp_block_step_runs_config1_shapes():
     assert float(r["grad"][:2 * S * H].abs().max()) == 0.0
     assert float(r["grad"][2 * S * H:].abs().max()) > 0.0
     assert math.isfinite(r["loss"])
+
+
+def test_stack_as_block_diagonal_graft_equals_explicit_and_baked():
+    """N sibling grafts injected one by one (test6_stack_vs_bake_f32.cpp path A),
+    the same grafts as one block-diagonal overlay graft, and the fp32 base with
+    all of them baked in (path B) give the same logits (test6 tolerance 1e-4)."""
+    from tests.parity import make_decoder_weights
+    N, S = 4, 8
+    rc = rm.GraftConfig(hidden_dim=64, intermediate_dim=96, slice_dim=S, max_domains=N, vocab_size=64,
+                        num_layers=2, num_heads=4, num_kv_heads=2, rope_theta=10000.0,
+                        graft_layer_start=0, graft_layer_end=1, graft_proj_gate=1, graft_proj_up=1,
+                        graft_proj_down=1, layout="overlay", tie_embeddings=True).finalize()
+    H = rc.hidden_dim // N
+    w = make_decoder_weights(rc, 3, 0.05)
+    g = torch.Generator().manual_seed(7)
+    deltas = [torch.randn(3 * rc.num_layers * S * H, generator=g) * 0.05 for _ in range(N)]
+    ids = torch.randint(0, rc.vocab_size, (2, 16), generator=g, dtype=torch.int32)
+    explicit = rm.model_forward_stack(ids, w, deltas, rc)
+    rs = rm.GraftConfig(**{**rc.__dict__, "slice_dim": N * S, "max_domains": 1, "domain_id": 0}).finalize()
+    stacked, _, _, _ = rm.model_forward(ids, w, rm.stack_grafts(deltas, rc.num_layers, S, H), rs)
+    torch.testing.assert_close(stacked, explicit, rtol=1e-5, atol=1e-5)
+    wb = {**w, "layers": []}
+    for l, lw in enumerate(w["layers"]):
+        lb = {k: v.clone() for k, v in lw.items()}
+        for d, delta in enumerate(deltas):
+            i0, h0 = d * S, d * H
+            lb["wg"][i0:i0 + S, h0:h0 + H] += rm.delta_view_at(delta, rc, l, 0, S, H)
+            lb["wu"][i0:i0 + S, h0:h0 + H] += rm.delta_view_at(delta, rc, l, 1, S, H)
+            lb["wd"][h0:h0 + H, i0:i0 + S] += rm.delta_view_at(delta, rc, l, 2, S, H).t()
+        wb["layers"].append(lb)
+    baked, _, _, _ = rm.model_forward(ids, wb, None, rc)
+    torch.testing.assert_close(baked, explicit, rtol=1e-4, atol=1e-4)

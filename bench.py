@@ -46,9 +46,14 @@ WORKLOADS = {
                      "14q/2kv hd64, vocab 151936, 8x1024 tokens/GPU"),
 }
 METRIC = "graft-train tokens/s at Llama-3-8B shape, 1-8 B200; MLP GEMM % of bf16 peak"
-# ncu DRAM traffic (bytes read + written) of one gate/up GEMM launch at the
-# config-3 shape; filled from profiles/ once captured, else None.
-GATE_UP_TRAFFIC_BYTES = None
+# ncu DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one
+# gate/up GEMM launch at the config-3 layer shape (M = 32768 tokens, K = 4096,
+# N = 2F' = 30720): 2,329,381,376 B read + 996,020,480 B written, captured on
+# the identical launch of `python -m glt_b200.mlp_bench --tokens 32768 --slice
+# 1024` (the full training step is too large for a capture under the
+# profiling rules); algorithmic bytes are 1.53 GB (x 268 MB + W_gu 252 MB
+# read, h 1007 MB written).
+GATE_UP_TRAFFIC_BYTES = 2329381376 + 996020480
 
 
 def peaks():

@@ -39,7 +39,8 @@ int ensure_smem_attr(const void* func, int bytes);
 template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi>
 int launch_gemm(const Operand& A, const Operand& B, int M, int N, int K, const Epi& epi,
                 cudaStream_t stream, int k_splits = 1, const Operand* A2 = nullptr,
-                int a2_n_tile = INT_MAX, int group_m = 32) {
+                int a2_n_tile = INT_MAX, int group_m = 32, const int* m_dev = nullptr,
+                int m_off = 0) {
   using namespace tc;
   if (M <= 0 || N <= 0 || K <= 0) return GLT_OK;
   if (A.mn_major != A_MN || B.mn_major != B_MN)
@@ -73,6 +74,8 @@ int launch_gemm(const Operand& A, const Operand& B, int M, int N, int K, const E
   shape.k_splits = k_splits < 1 ? 1 : k_splits;
   shape.a2_n_tile = A2 ? a2_n_tile : INT_MAX;
   shape.group_m = group_m;
+  shape.m_dev = m_dev;
+  shape.m_off = m_off;
   shape.err = device_error_word();
   if (!shape.err) return fail(GLT_ECUDA, "device error word unavailable");
   auto kern = tc_gemm_kernel<BN, STAGES, A_MN, B_MN, Epi>;
@@ -143,6 +146,40 @@ struct EpiF32 {
 #pragma unroll
         for (int i = 0; i < 32; ++i)
           if (col0 + i < N) dst[i] = alpha * v[i] + (beta != 0.f ? beta * dst[i] : 0.f);
+      }
+    }
+  }
+};
+
+// C[rows[row]] (fp32) = acc for the first *n - off rows (row scatter; used
+// with a device-side row count, so rows past it in the last tile are skipped).
+template <int BN>
+struct EpiF32Rows {
+  float* C;
+  int64_t ldc;
+  const int* rows;   // row map of this launch (already offset)
+  const int* n;      // device row count
+  int off;
+  int N;
+  __device__ __forceinline__ void operator()(const tc::EpiCtx<BN>& c) const {
+    // every lane takes part in the (warp-collective) TMEM loads; only live
+    // rows store
+    const bool live = c.row < *n - off;
+    float* base = live ? C + static_cast<int64_t>(rows[c.row]) * ldc : nullptr;
+#pragma unroll 1
+    for (int j = 0; j < BN; j += 32) {
+      const int col0 = c.n0 + j;   // the same for the whole warp
+      if (col0 >= N) break;
+      float v[32];
+      c.load(j, v);
+      if (!live) continue;
+      float* dst = base + col0;
+      if (col0 + 32 <= N) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 4)
+          *reinterpret_cast<float4*>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+      } else {
+        for (int i = 0; i < 32 && col0 + i < N; ++i) dst[i] = v[i];
       }
     }
   }

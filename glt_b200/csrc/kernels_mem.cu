@@ -150,11 +150,14 @@ constexpr int CE_THREADS = 512;
 
 __global__ void __launch_bounds__(CE_THREADS) cross_entropy_kernel(
     uint16_t* __restrict__ logits, int64_t ld, int row0, int V, const int32_t* __restrict__ ids,
-    const int32_t* __restrict__ ood, int T, float scale, DevStats* stats) {
+    const int32_t* __restrict__ ood, int T, float scale, DevStats* stats,
+    const int* __restrict__ row_map, const int* __restrict__ n_rows) {
   __shared__ float red_m[32], red_s[32];
   __shared__ float s_lab;
   const int r = blockIdx.x;
-  const int t = row0 + r;
+  // with a row map, logits row r is token row_map[row0 + r] (live by construction)
+  if (row_map && row0 + r >= *n_rows) return;
+  const int t = row_map ? row_map[row0 + r] : row0 + r;
   const int pos = t % T;
   uint4* row = reinterpret_cast<uint4*>(logits + static_cast<int64_t>(r) * ld);
   const int nv = V >> 3;
@@ -224,6 +227,56 @@ __global__ void __launch_bounds__(CE_THREADS) cross_entropy_kernel(
       f[j] = p * coef;
     }
     row[i] = pack8(f);
+  }
+}
+
+// --------------------------- LM-head rows ---------------------------------
+// Token rows whose next-token label counts in the LM loss (position t < T-1
+// and ood[t+1] == 0, the mask of cross_entropy_kernel), in order; one CTA,
+// chunks of 1024 rows with a ballot + warp-sum scan.
+constexpr int LIVE_THREADS = 1024;
+__global__ void __launch_bounds__(LIVE_THREADS) live_rows_kernel(const int32_t* __restrict__ ood,
+                                                                 int M, int T, int* __restrict__ rows,
+                                                                 int* __restrict__ n_rows) {
+  __shared__ int warp_off[LIVE_THREADS / 32];
+  __shared__ int s_total;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  int base = 0;
+  for (int c0 = 0; c0 < M; c0 += LIVE_THREADS) {
+    const int t = c0 + threadIdx.x;
+    const bool live = t < M && (t % T) < T - 1 && ood[t + 1] == 0;
+    const unsigned bal = __ballot_sync(0xffffffffu, live);
+    if (lane == 0) warp_off[w] = __popc(bal);
+    __syncthreads();
+    if (w == 0) {
+      const int v = warp_off[lane];
+      int incl = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += n;
+      }
+      warp_off[lane] = incl - v;
+      if (lane == 31) s_total = incl;
+    }
+    __syncthreads();
+    if (live) rows[base + warp_off[w] + __popc(bal & ((1u << lane) - 1u))] = t;
+    base += s_total;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *n_rows = base;
+}
+
+// dst[i] = src[rows[i]] for i < *n_rows, rows of D bf16 (16-byte vectors).
+__global__ void gather_rows_kernel(const uint16_t* __restrict__ src, uint16_t* __restrict__ dst,
+                                   const int* __restrict__ rows, const int* __restrict__ n_rows,
+                                   int M, int D) {
+  const int n = *n_rows;
+  const int nv = D >> 3;
+  for (int i = blockIdx.x; i < M && i < n; i += gridDim.x) {
+    const uint4* s = reinterpret_cast<const uint4*>(src + static_cast<int64_t>(rows[i]) * D);
+    uint4* d = reinterpret_cast<uint4*>(dst + static_cast<int64_t>(i) * D);
+    for (int v = threadIdx.x; v < nv; v += blockDim.x) d[v] = s[v];
   }
 }
 
@@ -676,11 +729,28 @@ int count_tokens(const int32_t* ood, int B, int T, DevStats* stats, cudaStream_t
 
 int cross_entropy_chunk(uint16_t* logits, int64_t ld, int rows, int row0, int V,
                         const int32_t* ids, const int32_t* ood, int T, float scale,
-                        DevStats* stats, cudaStream_t st) {
+                        DevStats* stats, cudaStream_t st, const int* row_map,
+                        const int* n_rows) {
   if (V % 8) return fail(GLT_EINVAL, "cross_entropy: V %% 8 != 0");
   if (rows <= 0) return GLT_OK;
   cross_entropy_kernel<<<rows, CE_THREADS, 0, st>>>(logits, ld, row0, V, ids, ood, T, scale,
-                                                     stats);
+                                                     stats, row_map, n_rows);
+  GLT_LAUNCH_CHECK();
+  return GLT_OK;
+}
+
+int live_rows(const int32_t* ood, int M, int T, int* rows, int* n_rows, cudaStream_t st) {
+  if (M <= 0) return GLT_OK;
+  live_rows_kernel<<<1, LIVE_THREADS, 0, st>>>(ood, M, T, rows, n_rows);
+  GLT_LAUNCH_CHECK();
+  return GLT_OK;
+}
+
+int gather_rows(const uint16_t* src, uint16_t* dst, const int* rows, const int* n_rows, int M, int D,
+                cudaStream_t st) {
+  if (M <= 0) return GLT_OK;
+  if (D % 8) return fail(GLT_EINVAL, "gather_rows: D %% 8 != 0");
+  gather_rows_kernel<<<grid_for(M, 1), 256, 0, st>>>(src, dst, rows, n_rows, M, D);
   GLT_LAUNCH_CHECK();
   return GLT_OK;
 }

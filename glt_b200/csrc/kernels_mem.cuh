@@ -45,7 +45,14 @@ int count_tokens(const int32_t* ood, int B, int T, DevStats* stats, cudaStream_t
 // dlogits = (softmax - onehot) * mask * scale / in_count  (grafting.hip:1027-1135).
 int cross_entropy_chunk(uint16_t* logits, int64_t ld, int rows, int row0, int V,
                         const int32_t* ids, const int32_t* ood, int T, float scale,
-                        DevStats* stats, cudaStream_t st);
+                        DevStats* stats, cudaStream_t st,
+                        const int* row_map = nullptr, const int* n_rows = nullptr);
+// Rows whose next-token label counts in the LM loss (t % T < T-1 and
+// ood[t+1] == 0), in order, into rows[0, *n_rows) (one CTA).
+int live_rows(const int32_t* ood, int M, int T, int* rows, int* n_rows, cudaStream_t st);
+// dst[i] = src[rows[i]] for i < *n_rows (bf16 rows of D).
+int gather_rows(const uint16_t* src, uint16_t* dst, const int* rows, const int* n_rows, int M, int D,
+                cudaStream_t st);
 
 // Silence bookkeeping.  esq holds per-token sum of squares of each grafted
 // projection's delta output, laid out [L][3][M].

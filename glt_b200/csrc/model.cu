@@ -347,6 +347,8 @@ int Model::allocate() {
     add(reinterpret_cast<void**>(&varf), b4 * M);
     ce_rows = std::min(M, 8192);
     add(reinterpret_cast<void**>(&logits), b2 * static_cast<size_t>(ce_rows) * V);
+    add(reinterpret_cast<void**>(&lm_rows), b4 * M);
+    add(reinterpret_cast<void**>(&n_lm_rows), b4);
     add(reinterpret_cast<void**>(&cos_t), b4 * T * (hd / 2));
     add(reinterpret_cast<void**>(&sin_t), b4 * T * (hd / 2));
   } else {
@@ -687,19 +689,55 @@ int Model::train_step(const int32_t* ids_in, const int32_t* ood_in, int host, in
   GLT_CUDA_TRY(cudaMemsetAsync(esq_all, 0, sizeof(float) * 3 * static_cast<size_t>(L) * M, st));
   GLT_TRY(count_tokens(ood, B, T, stats, st));
   GLT_TRY(forward_all(true, st));
-  // LM head + cross-entropy + dlogits . E, chunked over rows
+  // LM head + cross-entropy + dlogits . E over the rows that carry LM loss
+  // only: a position whose label is OOD (or that has no label) contributes
+  // nothing to the loss, and its logit gradient is zero (cross_entropy's
+  // mask), so its logits are never computed.  The live rows are compacted on
+  // the device (the final-norm rows gathered into xn, free after the
+  // forward); the two GEMMs read the row count from device memory, and the
+  // dx GEMM scatters back into the zeroed dtmp.  Same values as computing
+  // every row; about half the LM-head work in the reference's batch layout.
+  GLT_TRY(live_rows(ood, M, T, lm_rows, n_lm_rows, st));
+  GLT_TRY(gather_rows(xf, xn, lm_rows, n_lm_rows, M, D, st));
+  GLT_CUDA_TRY(cudaMemsetAsync(dtmp, 0, sizeof(float) * static_cast<size_t>(M) * D, st));
   for (int r0 = 0; r0 < M; r0 += ce_rows) {
     const int rows = std::min(ce_rows, M - r0);
-    GLT_TRY(lm_head_chunk(r0, rows, st));
-    GLT_PROF(GLT_PROF_CE, cross_entropy_chunk(logits, V, rows, r0, V, ids, ood, T, cfg.lm_loss_scale, stats, st));
-    GLT_PROF(GLT_PROF_LM_DX, g_f32(kmaj(logits, V), mnmaj(lm_head, D), rows, D, V,
-                                    dtmp + static_cast<int64_t>(r0) * D, D, st));
+    GLT_TRY(lm_head_live_chunk(r0, rows, st));
+    GLT_PROF(GLT_PROF_CE, cross_entropy_chunk(logits, V, rows, r0, V, ids, ood, T, cfg.lm_loss_scale,
+                                              stats, st, lm_rows, n_lm_rows));
+    if (D >= 1024) {
+      EpiF32Rows<256> e{dtmp, D, lm_rows + r0, n_lm_rows, r0, D};
+      GLT_PROF(GLT_PROF_LM_DX, (launch_gemm<256, 4, false, true>(kmaj(logits, V), mnmaj(lm_head, D), rows, D, V,
+                                                                   e, st, 1, nullptr, INT_MAX, 32, n_lm_rows, r0)));
+    } else {
+      EpiF32Rows<128> e{dtmp, D, lm_rows + r0, n_lm_rows, r0, D};
+      GLT_PROF(GLT_PROF_LM_DX, (launch_gemm<128, 6, false, true>(kmaj(logits, V), mnmaj(lm_head, D), rows, D, V,
+                                                                   e, st, 1, nullptr, INT_MAX, 32, n_lm_rows, r0)));
+    }
   }
   GLT_TRY(silence_stats(esq_all, d_enabled, L, M, S, H, ood, stats, st));
   GLT_TRY(finalize_loss(stats, cfg.lambda_silence, active_grafts, cfg.lm_loss_scale, st));
   GLT_PROF(GLT_PROF_RMSNORM, rmsnorm_bwd(dtmp, xs[L], final_norm, varf, nullptr, dx, nullptr, M, D, cfg.rms_norm_eps, st));
   for (int l = L - 1; l >= 0; --l) GLT_TRY(backward_layer(l, st));
   return finish_step(step, total_steps, out, st);
+}
+
+// logits[0:rows] = gathered live rows [r0, r0+rows) . lm_head^T (bf16); the
+// GEMM runs min(rows, n_live - r0) rows, n_live read on the device.
+int Model::lm_head_live_chunk(int r0, int rows, cudaStream_t st) {
+  const bool vec = V % 8 == 0;
+  if (V >= 1024) {
+    EpiBF16<256> e{logits, V, nullptr, 0, rows, V, vec ? 1 : 0};
+    GLT_PROF(GLT_PROF_LM_HEAD, (launch_gemm<256, 4, false, false>(kmaj(xn + static_cast<int64_t>(r0) * D, D),
+                                                                    kmaj(lm_head, D), rows, V, D, e, st, 1, nullptr,
+                                                                    INT_MAX, 32, n_lm_rows, r0)));
+  } else {
+    EpiBF16<128> e{logits, V, nullptr, 0, rows, V, vec ? 1 : 0};
+    GLT_PROF(GLT_PROF_LM_HEAD, (launch_gemm<128, 6, false, false>(kmaj(xn + static_cast<int64_t>(r0) * D, D),
+                                                                    kmaj(lm_head, D), rows, V, D, e, st, 1, nullptr,
+                                                                    INT_MAX, 32, n_lm_rows, r0)));
+  }
+  return GLT_OK;
 }
 
 // logits[0:rows] = final-norm rows [r0, r0+rows) . lm_head^T (bf16)

@@ -95,6 +95,8 @@ struct Model {
   float* var_in = nullptr;
   uint16_t* logits = nullptr;
   int ce_rows = 0;
+  int* lm_rows = nullptr;      // token rows that carry LM loss, compacted [M]
+  int* n_lm_rows = nullptr;    // their count (device)
   float* cos_t = nullptr;
   float* sin_t = nullptr;
   DevStats* stats = nullptr;
@@ -143,6 +145,7 @@ struct Model {
                  uint16_t* out, float* dx_out, cudaStream_t st);
   int activation(int which, int layer, void** ptr, int64_t* numel);
   int lm_head_chunk(int r0, int rows, cudaStream_t st);
+  int lm_head_live_chunk(int r0, int rows, cudaStream_t st);
   int load_safetensors(const char* path, cudaStream_t st);  // safetensors_io.cu
 
   // eval.cu: eval-only / shadow-eval metrics and the model's own shadow bake

@@ -203,6 +203,12 @@ struct GemmShape {
   int a2_n_tile;       // n-tiles >= this use the second A operand map (INT_MAX: never)
   int group_m;         // m-tiles per raster group (L2 reuse)
   unsigned int* err;   // device error word
+  // Optional device-side row count: the kernel runs min(M, *m_dev - m_off)
+  // rows (clamped at 0), read once at start by every thread.  M stays the
+  // capacity the tensor maps were built for; a row count produced by an
+  // earlier kernel on the stream then needs no host round trip.
+  const int* m_dev = nullptr;
+  int m_off = 0;
 };
 
 // Per-thread view handed to epilogue functors.
@@ -271,7 +277,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  const int num_m = (shape.M + BM - 1) / BM;
+  int m_rows = shape.M;
+  if (shape.m_dev) {
+    const int v = *shape.m_dev - shape.m_off;
+    m_rows = v < 0 ? 0 : (v < m_rows ? v : m_rows);
+  }
+  const int num_m = (m_rows + BM - 1) / BM;
   const int num_n = (shape.N + BN - 1) / BN;
   const int units = num_m * num_n * shape.k_splits;
   const int k_per_split = (shape.K + shape.k_splits - 1) / shape.k_splits;

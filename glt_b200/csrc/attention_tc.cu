@@ -373,18 +373,20 @@ int launch_fwd_tc(const uint16_t* qkv, uint16_t* o, float* lse, const AttnShape&
 //     dS^T = P^T (dP^T - rowsum(dO*O)); both written bf16 to smem tiles
 //   dV  += P^T . dO     dK  += dS^T . Q          (M=128 keys, N=128 d, K=64)
 //   dQ^T = K^T . dS^T                            (M=128 d, N=64 q, K=128)
-// Pipeline: the MMA thread issues S/dP of item i+1 before dV/dK/dQ of item
-// i, so the compute warps' exponentials for item i+1 overlap the tensor
-// core's work on item i.  S/dP are double-buffered in TMEM; dQ^T of item i
-// lands in the S^T columns of its own buffer (consumed by then), and the
-// buffer is released once the compute warps have read dQ^T out.
+// Pipeline: S/dP live in one TMEM buffer that the compute warps release as
+// soon as they have loaded item i into registers, so the MMA thread issues
+// S/dP of item i+1 while the warps are still computing item i, and those
+// products run ahead of dV/dK/dQ of item i on the tensor core.  dQ^T gets
+// two TMEM buffers of its own: item i writes buffer i & 1, which the warps
+// drain during item i+1 and which item i+2 reuses, so draining dQ never
+// holds up the next item's S/dP.
 // Eight compute warps, two per TMEM lane quarter: warp (quarter, half) owns
 // key rows [32 quarter, +32) and query columns [32 half, +32) of each item
 // (the backward has no reduction over queries, so the halves never talk).
 // Each stages its [32 q][32 d] block of dQ and adds it into the global fp32
 // dQ accumulator with its own TMA bulk reduce-add.
-// TMEM: buffer b (b = 0, 1): S^T / dQ^T [128b, 128b+64), dP^T [128b+64,
-// 128b+128); dV [256, 384); dK [384, 512).
+// TMEM: S^T [0, 64), dP^T [64, 128); dQ^T buffers [128, 192), [192, 256);
+// dV [256, 384); dK [384, 512).
 // ---------------------------------------------------------------------------
 constexpr int BK_KEYS = 128;  // keys per CTA
 constexpr int BQ = 64;        // queries per item
@@ -409,7 +411,7 @@ struct BwdSmem {
   static constexpr uint32_t OFF_DS = OFF_P + T_BYTES;
   static constexpr uint32_t OFF_DQ = OFF_DS + T_BYTES;      // [8 warps]
   static constexpr uint32_t OFF_BAR = OFF_DQ + 8 * DQW_BYTES;
-  static constexpr uint32_t NUM_BARS = 1 + 2 * QD_STAGES + 2 + 2 + 1 + 1 + 1;
+  static constexpr uint32_t NUM_BARS = 1 + 2 * QD_STAGES + 1 + 1 + 2 + 1 + 1 + 1;
   static constexpr uint32_t TOTAL = 1024 + OFF_BAR + NUM_BARS * 8 + 16;
 };
 static_assert(BwdSmem::TOTAL <= 232448, "attention backward: shared memory over 227 KB");
@@ -440,7 +442,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   using L = BwdSmem;
   constexpr int HD = 128;
   constexpr uint32_t TMEM_COLS = 512;
-  constexpr uint32_t COL_DV = 256, COL_DK = 384;
+  constexpr uint32_t COL_S = 0, COL_DP = 64, COL_DQ = 128, COL_DV = 256, COL_DK = 384;
   constexpr uint32_t ID_SDP = make_idesc(BQ, false, false);   // M=128, N=64, K-major x K-major
   constexpr uint32_t ID_DVK = make_idesc(HD, false, true);    // M=128, N=128, A K-major, B MN-major
   constexpr uint32_t ID_DQ = make_idesc(BQ, true, true);      // M=128, N=64,  A MN, B MN
@@ -451,9 +453,10 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   uint64_t* kv_full = bars;
   uint64_t* qd_full = kv_full + 1;            // [QD_STAGES]
   uint64_t* qd_empty = qd_full + QD_STAGES;   // [QD_STAGES]
-  uint64_t* sdp_full = qd_empty + QD_STAGES;  // [2] per TMEM buffer
-  uint64_t* sdp_free = sdp_full + 2;  // [2] per TMEM buffer (dQ^T read out)
-  uint64_t* p_full = sdp_free + 2;
+  uint64_t* sdp_full = qd_empty + QD_STAGES;  // S/dP of the current item in TMEM
+  uint64_t* sdp_free = sdp_full + 1;          // ... loaded into the warps' registers
+  uint64_t* dq_free = sdp_free + 1;           // [2] dQ^T buffer drained
+  uint64_t* p_full = dq_free + 2;
   uint64_t* mm_done = p_full + 1;
   uint64_t* drain = mm_done + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -476,10 +479,9 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       mbar_init(&qd_full[i], 1);
       mbar_init(&qd_empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&sdp_full[i], 1);
-      mbar_init(&sdp_free[i], 8);
-    }
+    mbar_init(sdp_full, 1);
+    mbar_init(sdp_free, 8);
+    for (int i = 0; i < 2; ++i) mbar_init(&dq_free[i], 8);
     mbar_init(p_full, 8);
     mbar_init(mm_done, 1);
     mbar_init(drain, 1);
@@ -529,23 +531,23 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   } else if (warp == 1) {
     // ------------------------------ MMA issuer ----------------------------
     if (lane == 0) {
-      // S^T(j), dP^T(j) into TMEM buffer j & 1 (both operands K-major)
+      // S^T(j), dP^T(j) into TMEM columns [0, 128) (both operands K-major),
+      // once the warps have loaded item j-1's S/dP
       auto issue_sdp = [&](int j) -> bool {
-        const int st = j % QD_STAGES, bf = j & 1;
+        const int st = j % QD_STAGES;
         if (!mbar_wait(&qd_full[st], (j / QD_STAGES) & 1, err)) return false;
-        if (!mbar_wait(&sdp_free[bf], ((j >> 1) & 1) ^ 1, err)) return false;
+        if (j > 0 && !mbar_wait(sdp_free, (j - 1) & 1, err)) return false;
         tc_fence_after();
         const uint32_t qb = sQ + st * L::QD_BYTES, db = sDO + st * L::QD_BYTES;
-        const uint32_t col = 128u * bf;
 #pragma unroll
         for (int k = 0; k < HD / 16; ++k)
-          umma_bf16(tmem + col, desc_kmajor(sK + (k >> 2) * (BK_KEYS * 128), k & 3),
+          umma_bf16(tmem + COL_S, desc_kmajor(sK + (k >> 2) * (BK_KEYS * 128), k & 3),
                     desc_kmajor(qb + (k >> 2) * (BQ * 128), k & 3), ID_SDP, k > 0);
 #pragma unroll
         for (int k = 0; k < HD / 16; ++k)
-          umma_bf16(tmem + col + 64, desc_kmajor(sV + (k >> 2) * (BK_KEYS * 128), k & 3),
+          umma_bf16(tmem + COL_DP, desc_kmajor(sV + (k >> 2) * (BK_KEYS * 128), k & 3),
                     desc_kmajor(db + (k >> 2) * (BQ * 128), k & 3), ID_SDP, k > 0);
-        umma_commit(&sdp_full[bf]);
+        umma_commit(sdp_full);
         return true;
       };
       bool ok = mbar_wait(kv_full, 0, err);
@@ -561,12 +563,14 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
           umma_bf16(tmem + COL_DV, desc_kmajor(sP, k), desc_mnmajor(db, k), ID_DVK, (i > 0 || k > 0));
           umma_bf16(tmem + COL_DK, desc_kmajor(sDS, k), desc_mnmajor(qb, k), ID_DVK, (i > 0 || k > 0));
         }
-        // dQ^T = K^T . dS^T into the (consumed) S^T columns of buffer i & 1:
+        // dQ^T = K^T . dS^T into dQ buffer i & 1, drained (item i-2) by now:
         // A = K tile read MN-major (d contiguous, 16 KB between d blocks),
         // B = dS^T tile read MN-major (q contiguous)
+        if (!mbar_wait(&dq_free[i & 1], ((i >> 1) & 1) ^ 1, err)) { ok = false; break; }
+        tc_fence_after();
 #pragma unroll
         for (int k = 0; k < BK_KEYS / 16; ++k)
-          umma_bf16(tmem + 128u * (i & 1), make_sdesc(sK + k * (UMMA_K * 128), BK_KEYS * 128, 1024),
+          umma_bf16(tmem + COL_DQ + 64u * (i & 1), make_sdesc(sK + k * (UMMA_K * 128), BK_KEYS * 128, 1024),
                     make_sdesc(sDS + k * (UMMA_K * 128), 8192, 1024), ID_DQ, k > 0);
         umma_commit(mm_done);
         umma_commit(&qd_empty[st]);
@@ -594,16 +598,15 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       pl = lse[lse_index(0)];
       pd = dsum[lse_index(0)];
     }
-    // dQ of item j: TMEM -> this warp's [32 q][32 d] tile -> TMA reduce-add
-    auto flush_dq = [&](int j) -> bool {
-      if (!mbar_wait(mm_done, j & 1, err)) return false;
-      tc_fence_after();
+    // dQ of item j: TMEM buffer j & 1 -> this warp's [32 q][32 d] tile -> TMA
+    // reduce-add (mm_done of item j already waited)
+    auto flush_dq = [&](int j) {
       float t[32];
-      tmem_ld32(tmem + lane_off + 128u * (j & 1) + 32 * half, t);
+      tmem_ld32(tmem + lane_off + COL_DQ + 64u * (j & 1) + 32 * half, t);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(&sdp_free[j & 1]);
+        mbar_arrive(&dq_free[j & 1]);
         bulk_wait_read0();                          // this warp's previous reduce has read its tile
       }
       __syncwarp();
@@ -616,7 +619,6 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         tma_reduce_add_2d(&tm_dq, sDQW, h * HD + sub * 32, row0 + qt * BQ + 32 * half);
         bulk_commit();
       }
-      return true;
     };
     bool ok = true;
     for (int i = 0; i < n_items; ++i) {
@@ -627,14 +629,17 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         pl = lse[lse_index(i + 1)];
         pd = dsum[lse_index(i + 1)];
       }
-      if (!mbar_wait(&sdp_full[i & 1], (i >> 1) & 1, err)) { ok = false; break; }
+      if (!mbar_wait(sdp_full, i & 1, err)) { ok = false; break; }
       tc_fence_after();
       uint32_t pw[16], dw[16];   // P^T and dS^T row segments, packed bf16 pairs
       {
-        const uint32_t col = 128u * (i & 1) + 32 * half;
         float sv[32], dv[32];
-        tmem_ld32(tmem + lane_off + col, sv);
-        tmem_ld32(tmem + lane_off + col + 64, dv);
+        tmem_ld32(tmem + lane_off + COL_S + 32 * half, sv);
+        tmem_ld32(tmem + lane_off + COL_DP + 32 * half, dv);
+        // S/dP are in registers: the MMA thread may overwrite them with item i+1
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(sdp_free);
         const bool diag = qt * BQ < (kt + 1) * BK_KEYS;
         // causal: query qt*BQ + 32 half + c sees this key iff c >= lim
         const int lim = key - qt * BQ - 32 * half;
@@ -660,11 +665,13 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
           dw[(c >> 1) + 1] = pack_bf16x2_rn(p2 * (dv[c + 2] - d4.z), p3 * (dv[c + 3] - d4.w));
         }
       }
-      // S^T/dP^T are in registers; dQ of the previous item frees its buffer
-      if (i > 0 && !flush_dq(i - 1)) { ok = false; break; }
+      // the P^T / dS^T tiles are free once item i-1's products are done
+      if (i > 0) {
+        if (!mbar_wait(mm_done, (i - 1) & 1, err)) { ok = false; break; }
+        tc_fence_after();
+      }
       // P^T and dS^T row segments -> 128-byte swizzled smem rows (16-byte
-      // chunks 4 half .. 4 half + 3; the previous item's tiles are free: its
-      // mm_done was waited in flush_dq)
+      // chunks 4 half .. 4 half + 3)
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         const uint32_t off = r * 128 + (((4 * half + c) ^ (r & 7)) << 4);
@@ -679,8 +686,16 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
+      // drain dQ of item i-1 (its products completed: mm_done waited above)
+      if (i > 0) flush_dq(i - 1);
     }
-    if (ok && n_items > 0) ok = flush_dq(n_items - 1);
+    if (ok && n_items > 0) {
+      ok = mbar_wait(mm_done, (n_items - 1) & 1, err);
+      if (ok) {
+        tc_fence_after();
+        flush_dq(n_items - 1);
+      }
+    }
     if (ok && n_items > 0) {
       // dK (scaled) and dV of this CTA's keys, d columns [64 half, 64 half + 64)
       // (mm_done of the last item was waited)

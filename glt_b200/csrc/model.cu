@@ -645,9 +645,10 @@ int Model::backward_layer(int l, cudaStream_t st) {
   Layer& y = layers[l];
   AttnShape as{B, T, nh, nkv, hd, QKV, AD, 1.0f / sqrtf(static_cast<float>(hd))};
   GLT_TRY(ffn_backward(l, st));
-  if (dp_world > 1) {
+  if (dp_world > 1 && l % dp_bucket == 0) {
+    // graft grads of layers [l, l + dp_bucket) are final (layers run L-1 .. 0)
     GLT_CUDA_TRY(cudaEventRecord(layer_done[l], st));
-    GLT_TRY(dp_allreduce_layer(l));
+    GLT_TRY(dp_allreduce_layers(l, std::min(L, l + dp_bucket)));
   }
   // post-attention RMSNorm backward + residual: dx = grad wrt x_post
   GLT_PROF(GLT_PROF_RMSNORM, rmsnorm_bwd(dtmp, y.x_post, y.post_norm, y.var2, dx, dx, dy_b, M, D, cfg.rms_norm_eps, st));

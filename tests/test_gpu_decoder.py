@@ -126,3 +126,35 @@ def test_two_steps_reduce_loss_and_host_inputs_match_device_inputs():
     assert s_host["total_loss"] == pytest.approx(s_dev["total_loss"], rel=1e-5)
     torch.testing.assert_close(g_host, g_dev, rtol=0, atol=1e-6)
     assert losses[-1] < losses[0]
+
+
+@pytest.mark.parametrize("mask", ["random", "all_ood", "all_domain"])
+def test_train_step_with_any_ood_mask_matches_oracle(mask):
+    """The LM head runs only over positions whose next-token label carries LM
+    loss (t < T-1 and ood[t+1] == 0, compacted on the device); any mask --
+    token-level random, all OOD (no LM rows: the LM-head GEMMs run zero
+    tiles) or all domain -- gives the oracle's losses and graft gradients."""
+    rc = small_cfg()
+    B, T = 4, 128
+    w, delta, ids, _ = problem(rc, B, T, std=0.05, graft_std=0.05)
+    g = torch.Generator().manual_seed(99)
+    if mask == "random":
+        ood = (torch.rand(B, T, generator=g) < 0.4).to(torch.int32)
+    elif mask == "all_ood":
+        ood = torch.ones(B, T, dtype=torch.int32)
+    else:
+        ood = torch.zeros(B, T, dtype=torch.int32)
+    m = gpu_model(rc, w, delta, B, T)
+    st = m.train_step(ids, ood, step=0, total_steps=10)
+    grad_gpu = m.read_graft("grad").cpu()
+    m.close()
+    grad_ref, stats, _ = rm.compute_grads(ids, ood, w, delta.clone(), rc)
+    if mask == "all_ood":
+        assert st["lm_loss"] == 0.0 and stats["lm_loss"] == 0.0
+    else:
+        assert st["lm_loss"] == pytest.approx(stats["lm_loss"], rel=1e-2)
+    assert st["total_loss"] == pytest.approx(stats["total_loss"], rel=1e-2, abs=1e-6)
+    if float(grad_ref.abs().max()) > 0:
+        assert_close_bf16(grad_gpu, grad_ref, f"graft grads ({mask} mask)")
+    else:
+        assert float(grad_gpu.abs().max()) == 0.0

@@ -83,6 +83,7 @@ SIGNATURES: dict[str, tuple] = {
     "glt_get_lr": (_f32, [_cfgp, _i32, _i32]),
     "glt_delta_offset": (_i64, [_i32, _i32, _i32, _i32]),
     "glt_adamw_all": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _f32, _vp]),
+    "glt_grad_clip": (_i32, [_vp, _i64, _f32, _i32, _vp, _i64, _vp, _vp, _vp]),
     "glt_swiglu_fwd": (_i32, [_vp, _vp, _vp, _i32, _i32, _i64, _i64, _i64, _vp]),
     "glt_swiglu_bwd": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _vp]),
     "glt_stack_grafts": (_i32, [C.POINTER(_vp), _i32, _i32, _i32, _i32, _vp, _vp]),

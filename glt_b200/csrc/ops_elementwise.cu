@@ -9,6 +9,8 @@
 //   glt_stack_grafts  N sibling grafts -> one block-diagonal overlay graft
 //                   (the explicit-injection stack of
 //                    tests/test6_stack_vs_bake_f32.cpp, as one graft)
+//   glt_grad_clip   global-norm clip of a gradient buffer (reduce_l2 /
+//                   calc_scale / apply_scale, kernels_elementwise_impl.inc:125-213)
 //   glt_adamw_all   AdamW over every projection of the flat [3L, S, H] graft,
 //                   skipping disabled projection kinds, optional bf16 image at
 //                   the same flat index (adamw_fused_kernel + execute_adamw_all,
@@ -117,6 +119,68 @@ __global__ void adamw_flat_kernel(float* __restrict__ w, uint16_t* __restrict__ 
       *reinterpret_cast<uint2*>(w_bf16 + i) = b;
     }
   }
+}
+
+// Global-norm gradient clip, three passes like the reference
+// (reduce_l2_kernel / calc_scale_kernel / apply_scale_kernel): per-CTA
+// partial sums of squares (fp64), one CTA turning them into
+// norm = sqrt(sum + 1e-8) and scale = clip / norm if norm > clip else 1,
+// and an optional in-place rescale of the gradients.
+constexpr int CLIP_THREADS = 256;
+constexpr int CLIP_MAX_BLOCKS = 1024;
+__global__ void __launch_bounds__(CLIP_THREADS) clip_partial_kernel(const float* __restrict__ g,
+                                                                    int64_t n, double* __restrict__ partial) {
+  __shared__ double red[CLIP_THREADS / 32];
+  double acc = 0.0;
+  const int64_t nv = n >> 2;
+  for (int64_t q = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; q < nv;
+       q += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float4 v = reinterpret_cast<const float4*>(g)[q];
+    acc += static_cast<double>(v.x) * v.x + static_cast<double>(v.y) * v.y +
+           static_cast<double>(v.z) * v.z + static_cast<double>(v.w) * v.w;
+  }
+  if (blockIdx.x == 0)   // scalar tail
+    for (int64_t i = (nv << 2) + threadIdx.x; i < n; i += blockDim.x) acc += static_cast<double>(g[i]) * g[i];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int w = 0; w < CLIP_THREADS / 32; ++w) t += red[w];
+    partial[blockIdx.x] = t;
+  }
+}
+
+__global__ void __launch_bounds__(CLIP_MAX_BLOCKS) clip_scale_kernel(const double* __restrict__ partial, int np,
+                                                                     float clip, float* __restrict__ scale,
+                                                                     float* __restrict__ norm_out) {
+  __shared__ double red[CLIP_MAX_BLOCKS / 32];
+  double acc = threadIdx.x < np ? partial[threadIdx.x] : 0.0;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int w = 0; w < CLIP_MAX_BLOCKS / 32; ++w) t += red[w];
+    const float norm = sqrtf(static_cast<float>(t) + 1e-8f);
+    *scale = norm > clip ? clip / norm : 1.0f;
+    if (norm_out) *norm_out = norm;
+  }
+}
+
+__global__ void clip_apply_kernel(float* __restrict__ g, int64_t n, const float* __restrict__ scale) {
+  const float sc = *scale;
+  const int64_t nv = n >> 2;
+  for (int64_t q = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; q < nv;
+       q += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float4 v = reinterpret_cast<float4*>(g)[q];
+    v.x *= sc; v.y *= sc; v.z *= sc; v.w *= sc;
+    reinterpret_cast<float4*>(g)[q] = v;
+  }
+  if (blockIdx.x == 0)
+    for (int64_t i = (nv << 2) + threadIdx.x; i < n; i += blockDim.x) g[i] *= sc;
 }
 
 constexpr int MAX_STACK = 8;
@@ -250,5 +314,29 @@ extern "C" int glt_stack_grafts(const float* const* grafts, int n, int num_layer
   glt::stack_grafts_kernel<<<glt::ew_grid(nvec, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       src, n, projs, S, H, out);
   GLT_LAUNCH_CHECK();
+  return GLT_OK;
+}
+
+extern "C" int glt_grad_clip(float* grads, int64_t n, float clip_norm, int apply_in_place,
+                             void* workspace, int64_t workspace_bytes, float* scale_out,
+                             float* norm_out, void* stream) {
+  if (!grads || !workspace || !scale_out) return glt::fail(GLT_EINVAL, "null argument");
+  if (n < 0) return glt::fail(GLT_EINVAL, "negative size");
+  if (workspace_bytes < static_cast<int64_t>(sizeof(double)) * glt::CLIP_MAX_BLOCKS)
+    return glt::fail(GLT_EINVAL, "grad_clip: workspace must hold %d bytes", (int)(sizeof(double) * glt::CLIP_MAX_BLOCKS));
+  if (!glt::aligned16(grads) || (reinterpret_cast<uintptr_t>(workspace) & 7u))
+    return glt::fail(GLT_EINVAL, "grad_clip: grads must be 16-byte aligned, workspace 8-byte");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int blocks = glt::ew_grid(n / 4 + 1, glt::CLIP_THREADS);
+  if (blocks > glt::CLIP_MAX_BLOCKS) blocks = glt::CLIP_MAX_BLOCKS;
+  double* partial = static_cast<double*>(workspace);
+  glt::clip_partial_kernel<<<blocks, glt::CLIP_THREADS, 0, st>>>(grads, n, partial);
+  GLT_LAUNCH_CHECK();
+  glt::clip_scale_kernel<<<1, glt::CLIP_MAX_BLOCKS, 0, st>>>(partial, blocks, clip_norm, scale_out, norm_out);
+  GLT_LAUNCH_CHECK();
+  if (apply_in_place) {
+    glt::clip_apply_kernel<<<glt::ew_grid(n / 4 + 1, 256), 256, 0, st>>>(grads, n, scale_out);
+    GLT_LAUNCH_CHECK();
+  }
   return GLT_OK;
 }

@@ -260,6 +260,17 @@ GLT_API int64_t glt_delta_offset(int layer, int proj, int slice_dim, int h_slice
 /* host array of n (<= 8) device pointers; out is device memory; H % 4 == 0. */
 GLT_API int glt_stack_grafts(const float* const* grafts, int n, int num_layers, int S, int H,
                              float* out, void* stream);
+/* glt_grad_clip replaces the clip of grafting.hip:1150-1164 (reduce_l2 /   */
+/* calc_scale / apply_scale, kernels_elementwise_impl.inc:125-213): with     */
+/* norm = sqrt(sum g^2 + 1e-8) over the n fp32 grads (16-byte aligned),      */
+/* writes scale = clip_norm / norm if norm > clip_norm else 1 to *scale_out */
+/* (device), the norm to *norm_out (device, nullable), and with              */
+/* apply_in_place = 1 multiplies the grads by it; with 0 pass scale_out as   */
+/* glt_adamw_all's grad_scale instead.  The sum of squares is fp64.          */
+/* workspace: device memory of at least 8192 bytes (8-byte aligned).         */
+GLT_API int glt_grad_clip(float* grads, int64_t n, float clip_norm, int apply_in_place,
+                          void* workspace, int64_t workspace_bytes, float* scale_out,
+                          float* norm_out, void* stream);
 /* glt_adamw_all replaces execute_adamw_all + adamw_fused_kernel             */
 /* (kernels_optimizer_impl.inc:11-77): one AdamW step over the flat          */
 /* [3L, S, H] graft (weights, grads, adam_m, adam_v fp32, 16-byte aligned), */

@@ -141,3 +141,28 @@ def test_fused_weight_image_tracks_master_after_steps():
         assert torch.equal(wgu[gate_rows + 128], bits(master[l, 1])), f"up image L{l}"
         assert torch.equal(wd[:, F_pad:F_pad + S], bits(master[l, 2]).t()), f"down image L{l}"
     m.close()
+
+
+@pytest.mark.parametrize("n,gscale,apply", [(4096 * 3 + 5, 1e-2, 1), (1 << 20, 1e-5, 1), (777, 1.0, 0)])
+def test_grad_clip_matches_oracle(n, gscale, apply):
+    g = torch.randn(n, generator=torch.Generator().manual_seed(n)) * gscale
+    dg = g.cuda()
+    work = torch.empty(1024, dtype=torch.float64, device="cuda")
+    scale = torch.empty(1, device="cuda")
+    norm = torch.empty(1, device="cuda")
+    _lib.check(lib.glt_grad_clip(vp(dg), n, 1.0, apply, vp(work), work.numel() * 8, vp(scale), vp(norm),
+                                 stream()))
+    torch.cuda.synchronize()
+    ref = g.clone()
+    ref_norm, ref_scale = rm.clip_grads(ref, 1.0)
+    assert float(norm) == pytest.approx(ref_norm, rel=1e-5)
+    assert float(scale) == pytest.approx(ref_scale, rel=1e-5)
+    torch.testing.assert_close(dg.cpu(), ref if apply else g, rtol=1e-6, atol=0)
+
+
+def test_grad_clip_rejects_small_workspace():
+    dg = torch.zeros(64, device="cuda")
+    work = torch.empty(16, dtype=torch.float64, device="cuda")
+    scale = torch.empty(1, device="cuda")
+    assert lib.glt_grad_clip(vp(dg), 64, 1.0, 1, vp(work), 128, vp(scale), None, stream()) == 1
+    assert "workspace" in _lib.last_error()

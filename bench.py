@@ -5,7 +5,9 @@
 
 One step = one full grafted training step of the decoder (embedding, 32
 layers with attention and the [base | graft] SwiGLU MLP, LM head + CE on
-domain tokens, OOD silence loss, backward with FFN recompute, all-reduce of
+domain tokens, OOD silence loss, backward -- SwiGLU's backward fused into the
+dh GEMM from the gate_pre/up the forward stored, or the reference's FFN
+recompute when the device has no room for them -- all-reduce of
 the graft gradients across ranks, global-norm clip, graft-only AdamW) over a
 16 x 2048-token microbatch per GPU.  Prints one JSON line (rank 0).
 
@@ -310,7 +312,8 @@ def main():
     mlp_alg = (12.0 * D * Fp + 6.0 * D * S) * M * L      # per step, recompute excluded
     mlp_kinds = (0, 1, 2, 6, 7, 8, 9, 10)
     mlp_ms = sum(kms[k] for k in mlp_kinds) / args.steps
-    mlp_exec = mlp_alg + (4.0 * D * Fp + 2.0 * D * S) * M * L  # + recompute + delta_down
+    store_on, store_bytes = model.mlp_store()
+    mlp_exec = mlp_alg + (2.0 * D * S + (0.0 if store_on else 4.0 * D * Fp)) * M * L  # + delta_down (+ recompute)
     roofline = {
         "kernel": "tc_gemm_kernel<256,4,K,K,EpiSwiGLUFwd> (gate/up GEMM + fused SwiGLU)",
         "bound": "tensor", "achieved": achieved, "peak": pk["tf_sus"], "unit": "TFLOP/s",
@@ -326,7 +329,7 @@ def main():
             "executed_tflops": mlp_exec / (mlp_ms / 1e3) / 1e12,
             "ms_per_step": mlp_ms,
             "definition": "(12*D*F' + 6*D*S) * tokens * layers / time of all MLP GEMM kernels "
-                          "(recompute time included, its FLOPs not)",
+                          "(a recompute's time included, its FLOPs not)",
         },
     }
     kernels = {n: {"ms_per_step": kms[i] / args.steps, "launches_per_step": kn[i] / args.steps}
@@ -370,6 +373,8 @@ def main():
             "data": "synthetic: uniform-random token ids, seeded N(0,0.02) random-init weights",
             "config": {"workload": wl["label"], "global_batch": world * B, "seq_len": T,
                        "parallelism": f"dp{world}", "graft": "concat [base | graft], gate+up+down",
+                       "mlp_activations": (f"stored: bf16 gate_pre/up of every layer, {store_bytes / 1e9:.1f} GB"
+                                           if store_on else "recomputed in the backward (recompute_ffn)"),
                        "l2": f"no flush: the step streams {w_bytes / 1e9:.1f} GB of weights, and its "
                              f"activations, through the 126 MB L2"},
             "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu,

@@ -90,6 +90,7 @@ SIGNATURES: dict[str, tuple] = {
     "glt_model_create": (_i32, [_cfgp, _i32, _i32, _i32, C.POINTER(_vp)]),
     "glt_model_destroy": (_i32, [_vp]),
     "glt_model_memory": (_i32, [_vp, C.POINTER(_i64), C.POINTER(_i64)]),
+    "glt_model_mlp_store": (_i32, [_vp, _i32, C.POINTER(_i32), C.POINTER(_i64)]),
     "glt_model_init_random": (_i32, [_vp, _u64, _f32, _f32, _f32]),
     "glt_model_set_weight": (_i32, [_vp, _i32, _i32, _vp, _i64, _i32, _vp]),
     "glt_model_graft_buffers": (_i32, [_vp, _fp, _fp, _fp, _fp, C.POINTER(_i64)]),

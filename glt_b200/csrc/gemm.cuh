@@ -83,7 +83,7 @@ int launch_gemm(const Operand& A, const Operand& B, int M, int N, int K, const E
   GLT_TRY(ensure_smem_attr(reinterpret_cast<const void*>(kern), smem));
   const int units = ((M + BM - 1) / BM) * ((N + BN - 1) / BN) * shape.k_splits;
   const int grid = units < num_sms() ? units : num_sms();
-  kern<<<grid, NUM_THREADS, smem, stream>>>(ta, ta2, tb, shape, epi);
+  kern<<<grid, gemm_threads<Epi>(), smem, stream>>>(ta, ta2, tb, shape, epi);
   GLT_LAUNCH_CHECK();
   return GLT_OK;
 }

@@ -112,7 +112,7 @@ int gemm_f32(const Operand& a, const Operand& b, int M, int N, int K, float* C, 
   GLT_TRY(ensure_smem_attr(reinterpret_cast<const void*>(kern), smem));
   const int units = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int grid = units < num_sms() ? units : num_sms();
-  kern<<<grid, NUM_THREADS, smem, st>>>(ta, ta, tb, shape, epi);
+  kern<<<grid, gemm_threads<EpiF32<BN>>(), smem, st>>>(ta, ta, tb, shape, epi);
   GLT_LAUNCH_CHECK();
   return GLT_OK;
 }

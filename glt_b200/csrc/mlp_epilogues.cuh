@@ -18,11 +18,26 @@ namespace glt {
 
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.f / (1.f + __expf(-x)); }
 
+// Layout of the stored gate_pre/up (EpiSwiGLUFwd::gu, EpiSwiGLUBwdStored):
+// a private buffer, so it is laid out for the epilogues' access pattern, in
+// which lane i of a warp owns row 32b + i of a 32-row band: element (r, c) of
+// the [M, 2F'] matrix (c in W_gu's interleaved order) sits at
+//   ((r / 32) * (2F' / 8) + c / 8) * 256 + (r % 32) * 8 + c % 8.
+// A warp's 16-byte accesses to 8 columns of its 32 rows are then one
+// contiguous 512-byte run (fully coalesced), where the row-major layout
+// touches 32 separate lines.
+__device__ __forceinline__ int64_t gu_block_offset(int row, int col8, int64_t groups) {
+  return ((static_cast<int64_t>(row >> 5) * groups + col8) << 8) + ((row & 31) << 3);
+}
+
 // Forward: h[t, c] = bf16(silu(gate) * up) for the 128 columns of the tile;
 // for graft columns also accumulate sum(gate^2) and sum(up^2) per token
 // (the delta energies of fused_inject_clone_energy_kernel,
 // src/kernels_elementwise_impl.inc:287-367, where in concat geometry the
-// graft columns of gate_pre/up ARE the expand deltas).
+// graft columns of gate_pre/up ARE the expand deltas).  With `gu` set the
+// tile's gate_pre and up are also stored bf16, in W_gu's interleaving, for
+// the backward (EpiSwiGLUBwdStored) -- the bf16 gate_pre/up tensors that
+// the reference's recompute_ffn (src/layer_recompute_impl.inc:8-91) rebuilds.
 struct EpiSwiGLUFwd {
   uint16_t* h;
   int64_t ldh;
@@ -30,16 +45,34 @@ struct EpiSwiGLUFwd {
   int g0, g1;          // graft intermediate columns [g0, g1)
   float* esq_gate;     // [M] or null
   float* esq_up;       // [M] or null
+  uint16_t* gu = nullptr;  // stored gate_pre/up (gu_block_offset layout) or null
+  int64_t gu_groups = 0;   // 2F' / 8
+  static constexpr int kParts = 2;   // two epilogue warps per 32 rows, 64 columns each
   __device__ __forceinline__ void operator()(const tc::EpiCtx<256>& c) const {
     const int cb = c.n0 >> 1;
     const bool graft = (cb + 128 > g0) && (cb < g1);
     float eg = 0.f, eu = 0.f;
+    const int j0 = c.part * (128 / kParts);
 #pragma unroll 1
-    for (int j = 0; j < 128; j += 32) {
+    for (int j = j0; j < j0 + 128 / kParts; j += 32) {
       float g[32], u[32];
       c.load(j, g);
       c.load(128 + j, u);
       if (c.row < M) {
+        if (gu) {
+          const int g8 = (c.n0 + j) >> 3;   // gate columns; up is 128 columns (16 groups) on
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            uint4 a, b;
+            a.x = pack_bf16x2(g[i], g[i + 1]); a.y = pack_bf16x2(g[i + 2], g[i + 3]);
+            a.z = pack_bf16x2(g[i + 4], g[i + 5]); a.w = pack_bf16x2(g[i + 6], g[i + 7]);
+            b.x = pack_bf16x2(u[i], u[i + 1]); b.y = pack_bf16x2(u[i + 2], u[i + 3]);
+            b.z = pack_bf16x2(u[i + 4], u[i + 5]); b.w = pack_bf16x2(u[i + 6], u[i + 7]);
+            // streaming stores: read once, a whole forward/backward later
+            __stcs(reinterpret_cast<uint4*>(gu + gu_block_offset(c.row, g8 + i / 8, gu_groups)), a);
+            __stcs(reinterpret_cast<uint4*>(gu + gu_block_offset(c.row, g8 + 16 + i / 8, gu_groups)), b);
+          }
+        }
         uint16_t* dst = h + static_cast<int64_t>(c.row) * ldh + cb + j;
 #pragma unroll
         for (int i = 0; i < 32; i += 8) {
@@ -91,6 +124,7 @@ struct EpiSwiGLUBwd {
   const float* esq_up;
   const int32_t* ood;
   const DevStats* stats;
+  static constexpr int kParts = 2;
   __device__ __forceinline__ void operator()(const tc::EpiCtx<256>& c) const {
     const int cb = c.n0 >> 1;
     const bool graft = (cb + 128 > g0) && (cb < g1);
@@ -101,17 +135,32 @@ struct EpiSwiGLUBwd {
       if (esq_gate) sg_s = lam / (sqrtf(esq_gate[c.row] + 1e-8f) * rs + 1e-8f);
       if (esq_up) su_s = lam / (sqrtf(esq_up[c.row] + 1e-8f) * rs + 1e-8f);
     }
+    // dh of 32 columns is fetched one chunk ahead (chunk 0 before the
+    // accumulator is read) so its latency overlaps the previous chunk
+    const int j0 = c.part * (128 / kParts), j1 = j0 + 128 / kParts;
+    const uint4* dhrow = reinterpret_cast<const uint4*>(dh + static_cast<int64_t>(c.row) * lddh + cb);
+    uint4 nd[4];
+    if (c.row < M) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) nd[q] = __ldg(dhrow + j0 / 8 + q);
+    }
 #pragma unroll 1
-    for (int j = 0; j < 128; j += 32) {
+    for (int j = j0; j < j1; j += 32) {
       float g[32], u[32];
       c.load(j, g);
       c.load(128 + j, u);
       if (c.row >= M) continue;
-      const uint16_t* dhr = dh + static_cast<int64_t>(c.row) * lddh + cb + j;
+      uint4 dcur[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) dcur[q] = nd[q];
+      if (j + 32 < j1) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) nd[q] = __ldg(dhrow + (j + 32) / 8 + q);
+      }
       uint16_t* dgr = dgu + static_cast<int64_t>(c.row) * ldgu + c.n0 + j;
 #pragma unroll
       for (int i = 0; i < 32; i += 8) {
-        const uint4 dv = *reinterpret_cast<const uint4*>(dhr + i);
+        const uint4 dv = dcur[i / 8];
         const float d[8] = {bf16_lo(dv.x), bf16_hi(dv.x), bf16_lo(dv.y), bf16_hi(dv.y),
                             bf16_lo(dv.z), bf16_hi(dv.z), bf16_lo(dv.w), bf16_hi(dv.w)};
         float og[8], ou[8], hh[8];
@@ -130,6 +179,112 @@ struct EpiSwiGLUBwd {
             if (col >= g0 && col < g1) {
               og[k] += sg_s * g[i + k];
               ou[k] += su_s * u[i + k];
+              if (hg) hg[static_cast<int64_t>(c.row) * ldhg + (col - g0)] = f32_to_bf16_bits(hh[k]);
+            }
+          }
+        }
+        uint4 a, b;
+        a.x = pack_bf16x2(og[0], og[1]); a.y = pack_bf16x2(og[2], og[3]);
+        a.z = pack_bf16x2(og[4], og[5]); a.w = pack_bf16x2(og[6], og[7]);
+        b.x = pack_bf16x2(ou[0], ou[1]); b.y = pack_bf16x2(ou[2], ou[3]);
+        b.z = pack_bf16x2(ou[4], ou[5]); b.w = pack_bf16x2(ou[6], ou[7]);
+        *reinterpret_cast<uint4*>(dgr + i) = a;
+        *reinterpret_cast<uint4*>(dgr + 128 + i) = b;
+      }
+    }
+  }
+};
+
+// Backward without the recompute: fused into dh = [dy | dyg] . W_d itself
+// (N = intermediate columns).  The accumulator is dh (fp32); gate_pre and up
+// come from the bf16 copies the training forward stored (EpiSwiGLUFwd::gu,
+// gu_block_offset layout), as in the reference, whose
+// fused_gate_up_bwd_kernel reads the bf16 gate_pre/up of recompute_ffn.
+// Same formulas, silence terms and hg output as EpiSwiGLUBwd; dgu is written
+// row-major in W_gu's interleaving, where intermediate column c sits at
+// 256 (c / 128) + c % 128 (gate) and +128 (up).
+template <int BN>
+struct EpiSwiGLUBwdStored {
+  const uint16_t* gu;
+  int64_t gu_groups;   // 2F' / 8
+  uint16_t* dgu;
+  int64_t ldgu_out;
+  uint16_t* hg;        // [M, ldhg] graft h (bf16) or null
+  int64_t ldhg;
+  int M, N;
+  int g0, g1;
+  int S;
+  const float* esq_gate;
+  const float* esq_up;
+  const int32_t* ood;
+  const DevStats* stats;
+  static constexpr int kParts = 2;   // two epilogue warps per 32 rows, BN/2 columns each
+
+  // offset of intermediate column col0 (a multiple of 32) in a gu/dgu row
+  __device__ __forceinline__ static int64_t pos(int col0) {
+    return 2 * static_cast<int64_t>(col0 & ~127) + (col0 & 127);
+  }
+  __device__ __forceinline__ void fetch(int row, int col0, uint4 (&g)[4], uint4 (&u)[4]) const {
+    const int g8 = static_cast<int>(pos(col0) >> 3);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {   // last use: evict first
+      g[q] = __ldcs(reinterpret_cast<const uint4*>(gu + gu_block_offset(row, g8 + q, gu_groups)));
+      u[q] = __ldcs(reinterpret_cast<const uint4*>(gu + gu_block_offset(row, g8 + 16 + q, gu_groups)));
+    }
+  }
+
+  // The stored operands of 32 columns are fetched one chunk ahead (chunk 0
+  // before the accumulator is read), so the HBM latency overlaps the TMEM
+  // loads and the math of the previous chunk instead of serialising with
+  // every store.
+  __device__ __forceinline__ void operator()(const tc::EpiCtx<BN>& c) const {
+    const bool graft = (c.n0 + BN > g0) && (c.n0 < g1);
+    const bool row_ok = c.row < M;
+    float sg_s = 0.f, su_s = 0.f;
+    if (graft && row_ok && ood[c.row]) {
+      const float lam = stats->lambda_eff;
+      const float rs = sqrtf(static_cast<float>(S));
+      if (esq_gate) sg_s = lam / (sqrtf(esq_gate[c.row] + 1e-8f) * rs + 1e-8f);
+      if (esq_up) su_s = lam / (sqrtf(esq_up[c.row] + 1e-8f) * rs + 1e-8f);
+    }
+    uint16_t* drow = dgu + static_cast<int64_t>(c.row) * ldgu_out;
+    const int j0 = c.part * (BN / kParts), j1 = j0 + BN / kParts;
+    uint4 ng[4], nu[4];
+    if (row_ok && c.n0 + j0 < N) fetch(c.row, c.n0 + j0, ng, nu);
+#pragma unroll 1
+    for (int j = j0; j < j1; j += 32) {
+      float d[32];
+      c.load(j, d);   // warp-collective: every lane loads
+      const int col0 = c.n0 + j;
+      const bool ok = row_ok && col0 < N;
+      uint4 gv[4], uv[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) { gv[q] = ng[q]; uv[q] = nu[q]; }
+      if (row_ok && j + 32 < j1 && col0 + 32 < N) fetch(c.row, col0 + 32, ng, nu);
+      if (!ok) continue;
+      uint16_t* dgr = drow + pos(col0);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int i = 8 * q;
+        const float g[8] = {bf16_lo(gv[q].x), bf16_hi(gv[q].x), bf16_lo(gv[q].y), bf16_hi(gv[q].y),
+                            bf16_lo(gv[q].z), bf16_hi(gv[q].z), bf16_lo(gv[q].w), bf16_hi(gv[q].w)};
+        const float u[8] = {bf16_lo(uv[q].x), bf16_hi(uv[q].x), bf16_lo(uv[q].y), bf16_hi(uv[q].y),
+                            bf16_lo(uv[q].z), bf16_hi(uv[q].z), bf16_lo(uv[q].w), bf16_hi(uv[q].w)};
+        float og[8], ou[8], hh[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float sg = sigmoidf_(g[k]);
+          og[k] = d[i + k] * u[k] * sg * (1.f + g[k] * (1.f - sg));
+          ou[k] = d[i + k] * g[k] * sg;
+          hh[k] = g[k] * sg * u[k];
+        }
+        if (graft) {
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const int col = col0 + i + k;
+            if (col >= g0 && col < g1) {
+              og[k] += sg_s * g[k];
+              ou[k] += su_s * u[k];
               if (hg) hg[static_cast<int64_t>(c.row) * ldhg + (col - g0)] = f32_to_bf16_bits(hh[k]);
             }
           }

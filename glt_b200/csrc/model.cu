@@ -13,6 +13,7 @@
 //   forward_model + train loop grafting.hip:224-271, 954-1172 -> Model::train_step
 //   allocate_arena       src/arena_impl.inc:14-126           -> Model::allocate
 #include <math.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <algorithm>
@@ -209,6 +210,7 @@ Model::~Model() {
   dp_shutdown();
   if (arena) cudaFree(arena);
   if (graft_mem) cudaFree(graft_mem);
+  if (gu_mem) cudaFree(gu_mem);
   if (pinned_stats) cudaFreeHost(pinned_stats);
   if (eval_mem) cudaFree(eval_mem);
   if (ev_pinned) cudaFreeHost(ev_pinned);
@@ -265,7 +267,76 @@ int Model::setup(const GltModelConfig& c, int batch, int seq, int k) {
       enabled.push_back(on ? 1 : 0);
       active_grafts += on ? 1 : 0;
     }
+  if (const char* e = getenv("GLT_MLP_STORE")) {
+    const int v = atoi(e);
+    if (v < 0 || v > 2) return fail(GLT_EINVAL, "GLT_MLP_STORE=%s (0 recompute, 1 store, 2 auto)", e);
+    store_mode = v;
+  }
   return allocate();
+}
+
+// ---------------------- stored MLP activations -----------------------------
+namespace {
+// Marks a training forward (whose MLPs write the store) for its scope.
+struct SavingScope {
+  bool& flag;
+  explicit SavingScope(bool& f) : flag(f) { flag = true; }
+  ~SavingScope() { flag = false; }
+};
+}  // namespace
+
+void Model::free_mlp_store() {
+  if (gu_mem) cudaFree(gu_mem);
+  gu_mem = nullptr;
+  gu_bytes = 0;
+  for (auto& y : layers) y.gu = nullptr;
+}
+
+int Model::alloc_mlp_store(bool required) {
+  if (gu_mem) return GLT_OK;
+  if (overlay) {
+    if (required) return fail(GLT_EINVAL, "stored MLP activations need the concat geometry");
+    return GLT_OK;
+  }
+  // gu_block_offset layout: 32-row bands
+  const size_t per = static_cast<size_t>(rup(rup(M, 32) * 2 * FF * 2, 256));
+  const size_t bytes = per * L;
+  if (!required) {
+    // auto: store only with room to spare for the caller's own buffers
+    size_t fr = 0, tot = 0;
+    GLT_CUDA_TRY(cudaMemGetInfo(&fr, &tot));
+    const size_t reserve = std::max(static_cast<size_t>(8) << 30, tot / 16);
+    if (fr < bytes + reserve) return GLT_OK;
+  }
+  const cudaError_t e = cudaMalloc(&gu_mem, bytes);
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    gu_mem = nullptr;
+    if (required)
+      return fail(GLT_ENOMEM, "stored MLP activations: cudaMalloc(%zu bytes) failed: %s", bytes,
+                  cudaGetErrorString(e));
+    return GLT_OK;
+  }
+  gu_bytes = bytes;
+  for (int l = 0; l < L; ++l) layers[l].gu = reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(gu_mem) + per * l);
+  return GLT_OK;
+}
+
+int Model::set_mlp_store(int mode) {
+  if (mode < 0 || mode > 2) return fail(GLT_EINVAL, "MLP store mode %d (0 recompute, 1 store, 2 auto)", mode);
+  GLT_CUDA_TRY(cudaDeviceSynchronize());   // no step may still read the store
+  store_mode = mode;
+  store_decided = false;
+  if (mode == 0) free_mlp_store();
+  if (mode == 1) return ensure_mlp_store();
+  return GLT_OK;
+}
+
+int Model::ensure_mlp_store() {
+  if (store_decided) return GLT_OK;
+  store_decided = true;
+  if (store_mode == 0) return GLT_OK;
+  return alloc_mlp_store(store_mode == 1);
 }
 
 int Model::allocate() {
@@ -561,7 +632,8 @@ int Model::ffn_forward(int l, const uint16_t* x_in, uint16_t* x_out, float* var_
   {
     EpiSwiGLUFwd e{h, FF, M, F_pad, F_pad + S,
                    (grafted && enabled[3 * l]) ? y.esq : nullptr,
-                   (grafted && enabled[3 * l + 1]) ? y.esq + M : nullptr};
+                   (grafted && enabled[3 * l + 1]) ? y.esq + M : nullptr,
+                   saving ? y.gu : nullptr, 2 * static_cast<int64_t>(FF) / 8};
     GLT_PROF(GLT_PROF_GATE_UP_FWD,
              (launch_gemm<256, 4, false, false>(kmaj(y.x_ffn, D), kmaj(y.w_gu, D), M, 2 * ff, D, e, st)));
   }
@@ -608,13 +680,29 @@ int Model::ffn_backward(int l, cudaStream_t st) {
   // dy = bf16(dx); dyg = bf16(dx + silence_down)
   GLT_TRY(silence_down_prep(dx, down ? y.dd : nullptr, D, y.esq + 2 * static_cast<int64_t>(M), ood,
                             stats, dy_b, dyg_b, D, M, D, 0, D, st));
-  // dh = [dy | dyg] . W_d   (graft columns read the silence-blended gradient)
-  {
+  if (y.gu) {
+    // dh = [dy | dyg] . W_d with SwiGLU's backward in its epilogue, from the
+    // gate_pre/up the forward stored -> dgu (+ graft h for the down grad)
     Operand a2 = kmaj(dyg_b, D);
-    GLT_PROF(GLT_PROF_DH, g_bf16(kmaj(dy_b, D), mnmaj(y.w_d, FF), M, ff, D, dh, FF, nullptr, 0, st, &a2, F_pad));
-  }
-  // recompute gate/up and SwiGLU backward -> dgu (+ graft h for the down grad)
-  {
+    const int64_t ld2 = 2 * static_cast<int64_t>(FF);
+    if (ff >= 1024) {
+      EpiSwiGLUBwdStored<256> e{y.gu, ld2 / 8, dgu, ld2, down ? hg : nullptr, S_pad, M, ff, F_pad, F_pad + S, S,
+                                gate ? y.esq : nullptr, up ? y.esq + M : nullptr, ood, stats};
+      GLT_PROF(GLT_PROF_DH, (launch_gemm<256, 4, false, true>(kmaj(dy_b, D), mnmaj(y.w_d, FF), M, ff, D, e, st,
+                                                               1, &a2, F_pad / 256)));
+    } else {
+      EpiSwiGLUBwdStored<128> e{y.gu, ld2 / 8, dgu, ld2, down ? hg : nullptr, S_pad, M, ff, F_pad, F_pad + S, S,
+                                gate ? y.esq : nullptr, up ? y.esq + M : nullptr, ood, stats};
+      GLT_PROF(GLT_PROF_DH, (launch_gemm<128, 6, false, true>(kmaj(dy_b, D), mnmaj(y.w_d, FF), M, ff, D, e, st,
+                                                               1, &a2, F_pad / 128)));
+    }
+  } else {
+    // dh = [dy | dyg] . W_d   (graft columns read the silence-blended gradient)
+    {
+      Operand a2 = kmaj(dyg_b, D);
+      GLT_PROF(GLT_PROF_DH, g_bf16(kmaj(dy_b, D), mnmaj(y.w_d, FF), M, ff, D, dh, FF, nullptr, 0, st, &a2, F_pad));
+    }
+    // recompute gate/up and SwiGLU backward -> dgu (+ graft h for the down grad)
     EpiSwiGLUBwd e{dh, FF, dgu, 2 * static_cast<int64_t>(FF), down ? hg : nullptr, S_pad, M,
                    F_pad, F_pad + S, S, gate ? y.esq : nullptr, up ? y.esq + M : nullptr, ood,
                    stats};
@@ -689,7 +777,11 @@ int Model::train_step(const int32_t* ids_in, const int32_t* ood_in, int host, in
   GLT_CUDA_TRY(cudaMemsetAsync(grad, 0, graft_numel * 4, st));
   GLT_CUDA_TRY(cudaMemsetAsync(esq_all, 0, sizeof(float) * 3 * static_cast<size_t>(L) * M, st));
   GLT_TRY(count_tokens(ood, B, T, stats, st));
-  GLT_TRY(forward_all(true, st));
+  GLT_TRY(ensure_mlp_store());
+  {
+    SavingScope sv(saving);
+    GLT_TRY(forward_all(true, st));
+  }
   // LM head + cross-entropy + dlogits . E over the rows that carry LM loss
   // only: a position whose label is OOD (or that has no label) contributes
   // nothing to the loss, and its logit gradient is zero (cross_entropy's
@@ -798,7 +890,11 @@ int Model::block_step(const uint16_t* x, const float* y_t, float lr, int step, f
   GLT_CUDA_TRY(cudaMemsetAsync(ood, 0, sizeof(int32_t) * M, st));
   GLT_CUDA_TRY(cudaMemsetAsync(layers[0].esq, 0, sizeof(float) * 3 * M, st));
   GLT_CUDA_TRY(cudaMemcpyAsync(xs[0], x, static_cast<size_t>(M) * D * 2, cudaMemcpyDeviceToDevice, st));
-  GLT_TRY(ffn_forward(0, xs[0], xs[1], var_in, true, st));
+  GLT_TRY(ensure_mlp_store());
+  {
+    SavingScope sv(saving);
+    GLT_TRY(ffn_forward(0, xs[0], xs[1], var_in, true, st));
+  }
   GLT_TRY(mse_grad(xs[1], y_t, dx, stats, M, D, st));
   GLT_TRY(ffn_backward(0, st));
   GLT_TRY(rmsnorm_bwd(dtmp, xs[0], layers[0].post_norm, var_in, dx, dx, nullptr, M, D, cfg.rms_norm_eps, st));
@@ -882,6 +978,15 @@ extern "C" int glt_model_memory(const GltModel* m, int64_t* arena_bytes, int64_t
   const Model* mm = reinterpret_cast<const Model*>(m);
   if (arena_bytes) *arena_bytes = static_cast<int64_t>(mm->arena_bytes);
   if (graft_bytes) *graft_bytes = static_cast<int64_t>(mm->graft_bytes);
+  return GLT_OK;
+}
+
+extern "C" int glt_model_mlp_store(GltModel* m, int mode, int* active, int64_t* bytes) {
+  if (!m) return glt::fail(GLT_EINVAL, "null model");
+  Model* mm = reinterpret_cast<Model*>(m);
+  if (mode != -1) GLT_TRY(mm->set_mlp_store(mode));
+  if (active) *active = mm->gu_mem ? 1 : 0;
+  if (bytes) *bytes = static_cast<int64_t>(mm->gu_bytes);
   return GLT_OK;
 }
 

@@ -33,6 +33,8 @@ struct Layer {
   float* var2 = nullptr;          // [M]
   float* esq = nullptr;           // [3][M] per-token sum of squares of gate/up/down deltas
   uint16_t* dd = nullptr;         // [M, H] delta_down (bf16), for the silence gradient
+  uint16_t* gu = nullptr;         // [M, 2F'] gate_pre/up (bf16, W_gu's interleaving) while
+                                  // the MLP store is on; null: the backward recomputes them
 };
 
 // Running eval totals on the device (eval.cu).
@@ -107,6 +109,19 @@ struct Model {
   int32_t* ids = nullptr;
   int32_t* ood = nullptr;
   float last_lr = 0.f;
+
+  // Stored MLP activations: the training forward keeps bf16 gate_pre/up of
+  // every layer (L * M * 2F' * 2 bytes) so the backward fuses SwiGLU's
+  // backward into the dh GEMM instead of recomputing x.W_gu^T.
+  void* gu_mem = nullptr;
+  size_t gu_bytes = 0;
+  int store_mode = 2;          // 0 recompute, 1 store, 2 auto (decided at the next training step)
+  bool store_decided = false;
+  bool saving = false;         // a training forward is running (writes layers[l].gu)
+  int set_mlp_store(int mode);
+  int ensure_mlp_store();
+  int alloc_mlp_store(bool required);
+  void free_mlp_store();
 
   // data parallel (NCCL, loaded at run time)
   void* nccl_comm = nullptr;

@@ -210,8 +210,6 @@ __global__ void stack_grafts_kernel(StackSrc src, int n, int64_t projs, int S, i
   }
 }
 
-inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
-
 // Grid for a grid-stride loop over n units: at most 16 CTAs per SM.
 inline int ew_grid(int64_t n, int threads) {
   int64_t b = (n + threads - 1) / threads;

@@ -9,11 +9,16 @@
 // forward (x.W^T), input-grad (dy.W) and weight-grad (X^T.dY, K = tokens)
 // contractions of the grafted MLP need no transposed copies.
 //
-// Structure (one persistent CTA per SM, 6 warps):
+// Structure (one persistent CTA per SM, 2 + 4 * parts warps):
 //   warp 0      TMA producer: 128B-swizzled tiles into a STAGES-deep ring
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
-//   warps 2..5  epilogue: tcgen05.ld of the 128 x BN fp32 accumulator,
-//               user epilogue functor (stores / SwiGLU / residual / atomics)
+//   warps 2..   epilogue: tcgen05.ld of the 128 x BN fp32 accumulator,
+//               user epilogue functor (stores / SwiGLU / residual / atomics).
+//               An epilogue functor with `static constexpr int kParts = 2`
+//               gets 8 epilogue warps: two per TMEM sub-partition (32 rows),
+//               which split the tile's columns (EpiCtx::part / parts); the
+//               memory-heavy SwiGLU epilogues use it for twice the loads and
+//               stores in flight.
 // Two TMEM accumulators (2*BN columns) let the epilogue of tile i overlap
 // the main loop of tile i+1.  Every TMA load is a plain per-CTA load into
 // the CTA's own shared memory, so the kernel is safe in multi-GPU jobs.
@@ -26,6 +31,8 @@
 #include <cuda.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace glt {
@@ -34,7 +41,7 @@ namespace tc {
 constexpr int BM = 128;
 constexpr int BK = 64;             // one 128-byte swizzle span of bf16
 constexpr int UMMA_K = 16;
-constexpr int NUM_THREADS = 192;   // 6 warps
+constexpr int NUM_THREADS = 192;   // 6 warps: producer, MMA, 4 epilogue warps (kParts = 1)
 constexpr uint64_t GLT_MBAR_TIMEOUT_NS = 4000000000ull;  // 4 s
 
 // ---------------------------------------------------------------------------
@@ -211,6 +218,21 @@ struct GemmShape {
   int m_off = 0;
 };
 
+// Epilogue warps per TMEM sub-partition: Epi::kParts when the functor
+// declares it, else 1.
+template <class Epi, class = void>
+struct EpiParts {
+  static constexpr int value = 1;
+};
+template <class Epi>
+struct EpiParts<Epi, std::void_t<decltype(Epi::kParts)>> {
+  static constexpr int value = Epi::kParts;
+};
+template <class Epi>
+constexpr int gemm_threads() {
+  return 64 + 128 * EpiParts<Epi>::value;
+}
+
 // Per-thread view handed to epilogue functors.
 template <int BN>
 struct EpiCtx {
@@ -218,6 +240,7 @@ struct EpiCtx {
   int row;            // global row of this thread
   int m0, n0;         // tile origin
   int split;          // split-K index of this work unit
+  int part, parts;    // this warp's share of the tile's columns (kParts > 1)
   __device__ __forceinline__ void load(int col, float (&v)[32]) const {
     tmem_ld32(tmem_row + static_cast<uint32_t>(col), v);
   }
@@ -249,13 +272,15 @@ __device__ __forceinline__ void unit_coords(int unit, const GemmShape& s, int nu
 }
 
 template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+__global__ void __launch_bounds__(gemm_threads<Epi>(), 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                    const __grid_constant__ CUtensorMap tmA2,
                    const __grid_constant__ CUtensorMap tmB, const GemmShape shape,
                    const Epi epi) {
   using L = SmemLayout<BN, STAGES>;
+  constexpr int PARTS = EpiParts<Epi>::value;
   static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN");
+  static_assert(PARTS == 1 || PARTS == 2, "kParts");
   constexpr uint32_t TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64
                                  : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
   constexpr uint32_t IDESC = make_idesc(BN, A_MN, B_MN);
@@ -296,7 +321,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull_bar[b], 1);
-      mbar_init(&tempty_bar[b], 4);
+      mbar_init(&tempty_bar[b], 4 * PARTS);
     }
     mbar_init(drain_bar, 1);
     s_abort = 0;
@@ -389,7 +414,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else {
     // -------------------------------- epilogue --------------------------------
     const int sub = warp & 3;  // TMEM sub-partition this warp may access
-    int local = 0;
+    const int part = (warp - 2) >> 2;    int local = 0;
     for (int unit = blockIdx.x; unit < units && !s_abort; unit += gridDim.x, ++local) {
       int mt, nt, split;
       unit_coords(unit, shape, num_m, num_n, mt, nt, split);
@@ -403,6 +428,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       ctx.n0 = nt * BN;
       ctx.row = ctx.m0 + sub * 32 + lane;
       ctx.split = split;
+      ctx.part = part;
+      ctx.parts = PARTS;
       epi(ctx);
       tc_fence_before();
       __syncwarp();

@@ -221,6 +221,14 @@ class GraftModel:
                                  C.c_void_p(dx.data_ptr()), _stream()))
         return dict(loss=loss.value, out=out, dx=dx)
 
+    def mlp_store(self, mode: int = -1) -> tuple[bool, int]:
+        """Stored MLP activations: mode 0 recompute, 1 store, 2 auto, -1 query.
+        Returns (active, bytes)."""
+        act = C.c_int32()
+        nb = C.c_int64()
+        check(lib.glt_model_mlp_store(self.handle, int(mode), C.byref(act), C.byref(nb)))
+        return bool(act.value), int(nb.value)
+
     def profile(self, enable: bool) -> None:
         check(lib.glt_model_profile(self.handle, int(enable)))
 

@@ -308,6 +308,21 @@ GLT_API int glt_model_create(const GltModelConfig* cfg, int batch_size, int seq_
 GLT_API int glt_model_destroy(GltModel* m);
 /* Bytes of device memory held by the model (arena + graft buffers). */
 GLT_API int glt_model_memory(const GltModel* m, int64_t* arena_bytes, int64_t* graft_bytes);
+/* Stored MLP activations.  No counterpart in the reference, whose backward
+ * recomputes gate_pre/up per layer (recompute_ffn,
+ * src/layer_recompute_impl.inc:8-91).  With the store on, the training
+ * forward keeps the bf16 gate_pre/up of every layer (num_layers * M * 2F' * 2
+ * bytes, F' = intermediate + slice columns rounded up) and the backward
+ * fuses SwiGLU's backward into the dh GEMM: no recompute GEMM.  mode 0:
+ * recompute (the reference's memory profile); 1: store, allocated now
+ * (GLT_ENOMEM when it does not fit); 2: auto, the default -- decided at the
+ * next training step, store when free device memory exceeds the store plus
+ * max(8 GiB, 1/16 of the device); -1: query only.  Concat geometry only
+ * (overlay recomputes; mode 1 on overlay is GLT_EINVAL).  GLT_MLP_STORE=0|1|2
+ * in the environment sets the mode at glt_model_create.  *active (nullable)
+ * = 1 while the store is allocated, *bytes (nullable) = its size.
+ * Synchronizes the device. */
+GLT_API int glt_model_mlp_store(GltModel* m, int mode, int* active, int64_t* bytes);
 
 /* load_base_model_safetensors (src/model_io_impl.inc:57-190): path is one
  * .safetensors file or a directory of shards (read in sorted order); HF

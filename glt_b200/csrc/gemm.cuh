@@ -79,7 +79,7 @@ int launch_gemm(const Operand& A, const Operand& B, int M, int N, int K, const E
   shape.err = device_error_word();
   if (!shape.err) return fail(GLT_ECUDA, "device error word unavailable");
   auto kern = tc_gemm_kernel<BN, STAGES, A_MN, B_MN, Epi>;
-  constexpr int smem = SmemLayout<BN, STAGES>::TOTAL;
+  constexpr int smem = gemm_smem_bytes<BN, STAGES, Epi>();
   GLT_TRY(ensure_smem_attr(reinterpret_cast<const void*>(kern), smem));
   const int units = ((M + BM - 1) / BM) * ((N + BN - 1) / BN) * shape.k_splits;
   const int grid = units < num_sms() ? units : num_sms();

@@ -108,7 +108,7 @@ int gemm_f32(const Operand& a, const Operand& b, int M, int N, int K, float* C, 
   shape.group_m = 8;
   shape.err = err;
   auto kern = tc_gemm_kernel<BN, STAGES, AMN, BMN, EpiF32<BN>>;
-  constexpr int smem = SmemLayout<BN, STAGES>::TOTAL;
+  constexpr int smem = gemm_smem_bytes<BN, STAGES, EpiF32<BN>>();
   GLT_TRY(ensure_smem_attr(reinterpret_cast<const void*>(kern), smem));
   const int units = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int grid = units < num_sms() ? units : num_sms();

@@ -30,6 +30,43 @@ __device__ __forceinline__ int64_t gu_block_offset(int row, int col8, int64_t gr
   return ((static_cast<int64_t>(row >> 5) * groups + col8) << 8) + ((row & 31) << 3);
 }
 
+// Bulk prefetch of `bytes` (a multiple of 16) at a 16-byte aligned global
+// address into L2 (no data returned to the SM).
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// Row-major stores of a warp's 32 rows x 32 bf16 columns, where lane i holds
+// row i's 64 bytes as four uint4 (v[0..3]).  The block goes through `stage`
+// (2 KB of shared memory per matrix) and leaves as 8-row x 64-byte runs, so
+// each store instruction fills whole 32-byte sectors of 8 lines instead of
+// half-sectors of 32 lines.  16-byte slots are XOR-swizzled by row so both
+// the row-per-lane writes and the run reads are free of bank conflicts.
+// dst(m) = dst_m + r * ld for band rows r < rows (rows past M are skipped).
+// stage_put writes this lane's 16-byte piece q of matrix m; stage_flush is
+// warp-collective (every lane calls it with the same arguments).
+__device__ __forceinline__ void stage_put(uint8_t* stage, int m, int q, uint4 v) {
+  const int lane = threadIdx.x & 31;
+  *reinterpret_cast<uint4*>(stage + m * 2048 + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4)) = v;
+}
+template <int NMAT>
+__device__ __forceinline__ void stage_flush(const uint8_t* stage, uint16_t* const (&dst)[NMAT], int64_t ld,
+                                            int rows) {
+  const int lane = threadIdx.x & 31;
+  __syncwarp();
+  const int u = lane & 3;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int r = 8 * k + (lane >> 2);
+#pragma unroll
+    for (int m = 0; m < NMAT; ++m) {
+      const uint4 w = *reinterpret_cast<const uint4*>(stage + m * 2048 + r * 64 + ((u ^ ((r >> 1) & 3)) << 4));
+      if (r < rows) *reinterpret_cast<uint4*>(dst[m] + r * ld + 8 * u) = w;
+    }
+  }
+  __syncwarp();
+}
+
 // Forward: h[t, c] = bf16(silu(gate) * up) for the 128 columns of the tile;
 // for graft columns also accumulate sum(gate^2) and sum(up^2) per token
 // (the delta energies of fused_inject_clone_energy_kernel,
@@ -48,16 +85,28 @@ struct EpiSwiGLUFwd {
   uint16_t* gu = nullptr;  // stored gate_pre/up (gu_block_offset layout) or null
   int64_t gu_groups = 0;   // 2F' / 8
   static constexpr int kParts = 2;   // two epilogue warps per 32 rows, 64 columns each
+  static constexpr int kScratchPerWarp = 2048;   // h staging (stage_store_32x32)
   __device__ __forceinline__ void operator()(const tc::EpiCtx<256>& c) const {
     const int cb = c.n0 >> 1;
     const bool graft = (cb + 128 > g0) && (cb < g1);
     float eg = 0.f, eu = 0.f;
     const int j0 = c.part * (128 / kParts);
+    const int band0 = c.row & ~31;
 #pragma unroll 1
     for (int j = j0; j < j0 + 128 / kParts; j += 32) {
       float g[32], u[32];
       c.load(j, g);
       c.load(128 + j, u);
+#pragma unroll
+      for (int i = 0; i < 32; i += 8) {
+        float o[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) o[k] = g[i + k] * sigmoidf_(g[i + k]) * u[i + k];
+        stage_put(c.scratch, 0, i / 8, make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]),
+                                                   pack_bf16x2(o[4], o[5]), pack_bf16x2(o[6], o[7])));
+      }
+      uint16_t* const hdst[1] = {h + static_cast<int64_t>(band0) * ldh + cb + j};
+      stage_flush<1>(c.scratch, hdst, ldh, M - band0);
       if (c.row < M) {
         if (gu) {
           const int g8 = (c.n0 + j) >> 3;   // gate columns; up is 128 columns (16 groups) on
@@ -72,17 +121,6 @@ struct EpiSwiGLUFwd {
             __stcs(reinterpret_cast<uint4*>(gu + gu_block_offset(c.row, g8 + i / 8, gu_groups)), a);
             __stcs(reinterpret_cast<uint4*>(gu + gu_block_offset(c.row, g8 + 16 + i / 8, gu_groups)), b);
           }
-        }
-        uint16_t* dst = h + static_cast<int64_t>(c.row) * ldh + cb + j;
-#pragma unroll
-        for (int i = 0; i < 32; i += 8) {
-          float o[8];
-#pragma unroll
-          for (int k = 0; k < 8; ++k) o[k] = g[i + k] * sigmoidf_(g[i + k]) * u[i + k];
-          uint4 w;
-          w.x = pack_bf16x2(o[0], o[1]); w.y = pack_bf16x2(o[2], o[3]);
-          w.z = pack_bf16x2(o[4], o[5]); w.w = pack_bf16x2(o[6], o[7]);
-          *reinterpret_cast<uint4*>(dst + i) = w;
         }
         if (graft) {
 #pragma unroll
@@ -219,6 +257,7 @@ struct EpiSwiGLUBwdStored {
   const int32_t* ood;
   const DevStats* stats;
   static constexpr int kParts = 2;   // two epilogue warps per 32 rows, BN/2 columns each
+  static constexpr int kScratchPerWarp = 4096;   // dgu gate + up staging (stage_store_32x32)
 
   // offset of intermediate column col0 (a multiple of 32) in a gu/dgu row
   __device__ __forceinline__ static int64_t pos(int col0) {
@@ -233,11 +272,29 @@ struct EpiSwiGLUBwdStored {
     }
   }
 
+  // L2 prefetch of this warp's stored operands of the CTA's next tile: per
+  // 32-column chunk one contiguous 2 KB run of gate_pre and one of up.
+  __device__ __forceinline__ void prefetch_next(const tc::EpiCtx<BN>& c) const {
+    if (c.next_m0 < 0 || (threadIdx.x & 31) != 0) return;
+    const int band0 = c.next_m0 + (c.row & 127 & ~31);   // this warp's rows in the next tile
+    if (band0 >= M) return;
+    const int j0 = c.part * (BN / kParts);
+#pragma unroll 1
+    for (int j = j0; j < j0 + BN / kParts; j += 32) {
+      const int col0 = c.next_n0 + j;
+      if (col0 >= N) break;
+      const int g8 = static_cast<int>(pos(col0) >> 3);
+      prefetch_l2_bulk(gu + gu_block_offset(band0, g8, gu_groups), 2048);
+      prefetch_l2_bulk(gu + gu_block_offset(band0, g8 + 16, gu_groups), 2048);
+    }
+  }
+
   // The stored operands of 32 columns are fetched one chunk ahead (chunk 0
   // before the accumulator is read), so the HBM latency overlaps the TMEM
   // loads and the math of the previous chunk instead of serialising with
-  // every store.
+  // every store; the next tile's are prefetched into L2 meanwhile.
   __device__ __forceinline__ void operator()(const tc::EpiCtx<BN>& c) const {
+    prefetch_next(c);
     const bool graft = (c.n0 + BN > g0) && (c.n0 < g1);
     const bool row_ok = c.row < M;
     float sg_s = 0.f, su_s = 0.f;
@@ -247,22 +304,20 @@ struct EpiSwiGLUBwdStored {
       if (esq_gate) sg_s = lam / (sqrtf(esq_gate[c.row] + 1e-8f) * rs + 1e-8f);
       if (esq_up) su_s = lam / (sqrtf(esq_up[c.row] + 1e-8f) * rs + 1e-8f);
     }
-    uint16_t* drow = dgu + static_cast<int64_t>(c.row) * ldgu_out;
     const int j0 = c.part * (BN / kParts), j1 = j0 + BN / kParts;
-    uint4 ng[4], nu[4];
+    const int band0 = c.row & ~31;
+    uint4 ng[4] = {}, nu[4] = {};
     if (row_ok && c.n0 + j0 < N) fetch(c.row, c.n0 + j0, ng, nu);
 #pragma unroll 1
     for (int j = j0; j < j1; j += 32) {
       float d[32];
       c.load(j, d);   // warp-collective: every lane loads
       const int col0 = c.n0 + j;
-      const bool ok = row_ok && col0 < N;
+      if (col0 >= N) continue;   // the same for the whole warp
       uint4 gv[4], uv[4];
 #pragma unroll
       for (int q = 0; q < 4; ++q) { gv[q] = ng[q]; uv[q] = nu[q]; }
       if (row_ok && j + 32 < j1 && col0 + 32 < N) fetch(c.row, col0 + 32, ng, nu);
-      if (!ok) continue;
-      uint16_t* dgr = drow + pos(col0);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const int i = 8 * q;
@@ -278,7 +333,7 @@ struct EpiSwiGLUBwdStored {
           ou[k] = d[i + k] * g[k] * sg;
           hh[k] = g[k] * sg * u[k];
         }
-        if (graft) {
+        if (graft && row_ok) {
 #pragma unroll
           for (int k = 0; k < 8; ++k) {
             const int col = col0 + i + k;
@@ -289,14 +344,14 @@ struct EpiSwiGLUBwdStored {
             }
           }
         }
-        uint4 a, b;
-        a.x = pack_bf16x2(og[0], og[1]); a.y = pack_bf16x2(og[2], og[3]);
-        a.z = pack_bf16x2(og[4], og[5]); a.w = pack_bf16x2(og[6], og[7]);
-        b.x = pack_bf16x2(ou[0], ou[1]); b.y = pack_bf16x2(ou[2], ou[3]);
-        b.z = pack_bf16x2(ou[4], ou[5]); b.w = pack_bf16x2(ou[6], ou[7]);
-        *reinterpret_cast<uint4*>(dgr + i) = a;
-        *reinterpret_cast<uint4*>(dgr + 128 + i) = b;
+        stage_put(c.scratch, 0, q, make_uint4(pack_bf16x2(og[0], og[1]), pack_bf16x2(og[2], og[3]),
+                                              pack_bf16x2(og[4], og[5]), pack_bf16x2(og[6], og[7])));
+        stage_put(c.scratch, 1, q, make_uint4(pack_bf16x2(ou[0], ou[1]), pack_bf16x2(ou[2], ou[3]),
+                                              pack_bf16x2(ou[4], ou[5]), pack_bf16x2(ou[6], ou[7])));
       }
+      uint16_t* const g_dst = dgu + static_cast<int64_t>(band0) * ldgu_out + pos(col0);
+      uint16_t* const dsts[2] = {g_dst, g_dst + 128};
+      stage_flush<2>(c.scratch, dsts, ldgu_out, M - band0);
     }
   }
 };

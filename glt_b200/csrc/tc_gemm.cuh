@@ -18,7 +18,10 @@
 //               gets 8 epilogue warps: two per TMEM sub-partition (32 rows),
 //               which split the tile's columns (EpiCtx::part / parts); the
 //               memory-heavy SwiGLU epilogues use it for twice the loads and
-//               stores in flight.
+//               stores in flight.  `static constexpr int kScratchPerWarp`
+//               reserves that many bytes of shared memory per epilogue warp
+//               (EpiCtx::scratch), used to turn row-per-lane results into
+//               coalesced stores.
 // Two TMEM accumulators (2*BN columns) let the epilogue of tile i overlap
 // the main loop of tile i+1.  Every TMA load is a plain per-CTA load into
 // the CTA's own shared memory, so the kernel is safe in multi-GPU jobs.
@@ -232,6 +235,15 @@ template <class Epi>
 constexpr int gemm_threads() {
   return 64 + 128 * EpiParts<Epi>::value;
 }
+// Shared memory per epilogue warp: Epi::kScratchPerWarp when declared, else 0.
+template <class Epi, class = void>
+struct EpiScratch {
+  static constexpr int value = 0;
+};
+template <class Epi>
+struct EpiScratch<Epi, std::void_t<decltype(Epi::kScratchPerWarp)>> {
+  static constexpr int value = Epi::kScratchPerWarp;
+};
 
 // Per-thread view handed to epilogue functors.
 template <int BN>
@@ -241,6 +253,8 @@ struct EpiCtx {
   int m0, n0;         // tile origin
   int split;          // split-K index of this work unit
   int part, parts;    // this warp's share of the tile's columns (kParts > 1)
+  uint8_t* scratch;   // this warp's kScratchPerWarp bytes of shared memory (128-byte aligned)
+  int next_m0, next_n0;  // origin of this CTA's next tile (-1: none), for L2 prefetches
   __device__ __forceinline__ void load(int col, float (&v)[32]) const {
     tmem_ld32(tmem_row + static_cast<uint32_t>(col), v);
   }
@@ -255,7 +269,18 @@ struct SmemLayout {
   // barriers + tmem slot after the tiles
   static constexpr uint32_t BAR_BYTES = (2 * STAGES + 5) * 8 + 16;
   static constexpr uint32_t TOTAL = 1024 /*align slack*/ + TILES_BYTES + BAR_BYTES;
+  // epilogue scratch after the barriers
+  static constexpr uint32_t SCRATCH_OFF = (TILES_BYTES + BAR_BYTES + 127) / 128 * 128;
 };
+
+// Dynamic shared memory of tc_gemm_kernel<BN, STAGES, *, *, Epi>.
+template <int BN, int STAGES, class Epi>
+constexpr uint32_t gemm_smem_bytes() {
+  using L = SmemLayout<BN, STAGES>;
+  return EpiScratch<Epi>::value == 0
+             ? L::TOTAL
+             : 1024 + L::SCRATCH_OFF + 4 * EpiParts<Epi>::value * EpiScratch<Epi>::value;
+}
 
 __device__ __forceinline__ void unit_coords(int unit, const GemmShape& s, int num_m, int num_n,
                                             int& mt, int& nt, int& split) {
@@ -281,6 +306,7 @@ __global__ void __launch_bounds__(gemm_threads<Epi>(), 1)
   constexpr int PARTS = EpiParts<Epi>::value;
   static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN");
   static_assert(PARTS == 1 || PARTS == 2, "kParts");
+  static_assert(gemm_smem_bytes<BN, STAGES, Epi>() <= 232448 - 64, "shared memory");
   constexpr uint32_t TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64
                                  : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
   constexpr uint32_t IDESC = make_idesc(BN, A_MN, B_MN);
@@ -430,6 +456,14 @@ __global__ void __launch_bounds__(gemm_threads<Epi>(), 1)
       ctx.split = split;
       ctx.part = part;
       ctx.parts = PARTS;
+      ctx.scratch = smem + L::SCRATCH_OFF + (warp - 2) * EpiScratch<Epi>::value;
+      ctx.next_m0 = ctx.next_n0 = -1;
+      if (unit + static_cast<int>(gridDim.x) < units) {
+        int nmt, nnt, nsplit;
+        unit_coords(unit + gridDim.x, shape, num_m, num_n, nmt, nnt, nsplit);
+        ctx.next_m0 = nmt * BM;
+        ctx.next_n0 = nnt * BN;
+      }
       epi(ctx);
       tc_fence_before();
       __syncwarp();

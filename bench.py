@@ -50,12 +50,15 @@ WORKLOADS = {
 METRIC = "graft-train tokens/s at Llama-3-8B shape, 1-8 B200; MLP GEMM % of bf16 peak"
 # ncu DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one
 # gate/up GEMM launch at the config-3 layer shape (M = 32768 tokens, K = 4096,
-# N = 2F' = 30720): 2,329,381,376 B read + 996,020,480 B written, captured on
-# the identical launch of `python -m glt_b200.mlp_bench --tokens 32768 --slice
-# 1024` (the full training step is too large for a capture under the
-# profiling rules); algorithmic bytes are 1.53 GB (x 268 MB + W_gu 252 MB
-# read, h 1007 MB written).
-GATE_UP_TRAFFIC_BYTES = 2329381376 + 996020480
+# N = 2F' = 30720), captured on the identical launch of `python -m
+# glt_b200.mlp_bench --tokens 32768 --slice 1024` (the full training step is
+# too large for a capture under the profiling rules):
+#   MLP store on:  2,496,413,184 B read + 2,991,854,080 B written; algorithmic
+#                  3.54 GB (x 268 MB + W_gu 252 MB read, h 1007 MB + bf16
+#                  gate_pre/up 2014 MB written);
+#   recompute:     2,329,381,376 B read + 996,020,480 B written; algorithmic
+#                  1.53 GB (no gate_pre/up written).
+GATE_UP_TRAFFIC_BYTES = {True: 2496413184 + 2991854080, False: 2329381376 + 996020480}
 
 
 def peaks():
@@ -319,7 +322,7 @@ def main():
         "bound": "tensor", "achieved": achieved, "peak": pk["tf_sus"], "unit": "TFLOP/s",
         "frac": achieved / pk["tf_sus"],
         "peak_note": f"{pk['src']} bf16_tflops_sustained (kernel timed inside a long step)",
-        "traffic": GATE_UP_TRAFFIC_BYTES,
+        "traffic": GATE_UP_TRAFFIC_BYTES[store_on],
         "algorithmic_flops_per_launch": gu_flops, "avg_launch_ms": gu_ms,
         "mlp_gemm": {
             "pct_of_peak_algorithmic": 100.0 * mlp_alg / (mlp_ms / 1e3) / 1e12 / pk["tf_sus"],

@@ -30,17 +30,12 @@ __device__ __forceinline__ int64_t gu_block_offset(int row, int col8, int64_t gr
   return ((static_cast<int64_t>(row >> 5) * groups + col8) << 8) + ((row & 31) << 3);
 }
 
-// Bulk prefetch of `bytes` (a multiple of 16) at a 16-byte aligned global
-// address into L2 (no data returned to the SM).
-__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
-
 // Row-major stores of a warp's 32 rows x 32 bf16 columns, where lane i holds
 // row i's 64 bytes as four uint4 (v[0..3]).  The block goes through `stage`
 // (2 KB of shared memory per matrix) and leaves as 8-row x 64-byte runs, so
 // each store instruction fills whole 32-byte sectors of 8 lines instead of
-// half-sectors of 32 lines.  16-byte slots are XOR-swizzled by row so both
+// half-sectors of 32 lines.  The stores are evict-first: h and dgu are larger
+// than L2 and would otherwise push the GEMM's operand rows out of it.  16-byte slots are XOR-swizzled by row so both
 // the row-per-lane writes and the run reads are free of bank conflicts.
 // dst(m) = dst_m + r * ld for band rows r < rows (rows past M are skipped).
 // stage_put writes this lane's 16-byte piece q of matrix m; stage_flush is
@@ -61,7 +56,7 @@ __device__ __forceinline__ void stage_flush(const uint8_t* stage, uint16_t* cons
 #pragma unroll
     for (int m = 0; m < NMAT; ++m) {
       const uint4 w = *reinterpret_cast<const uint4*>(stage + m * 2048 + r * 64 + ((u ^ ((r >> 1) & 3)) << 4));
-      if (r < rows) *reinterpret_cast<uint4*>(dst[m] + r * ld + 8 * u) = w;
+      if (r < rows) __stcs(reinterpret_cast<uint4*>(dst[m] + r * ld + 8 * u), w);   // streaming
     }
   }
   __syncwarp();
@@ -272,29 +267,11 @@ struct EpiSwiGLUBwdStored {
     }
   }
 
-  // L2 prefetch of this warp's stored operands of the CTA's next tile: per
-  // 32-column chunk one contiguous 2 KB run of gate_pre and one of up.
-  __device__ __forceinline__ void prefetch_next(const tc::EpiCtx<BN>& c) const {
-    if (c.next_m0 < 0 || (threadIdx.x & 31) != 0) return;
-    const int band0 = c.next_m0 + (c.row & 127 & ~31);   // this warp's rows in the next tile
-    if (band0 >= M) return;
-    const int j0 = c.part * (BN / kParts);
-#pragma unroll 1
-    for (int j = j0; j < j0 + BN / kParts; j += 32) {
-      const int col0 = c.next_n0 + j;
-      if (col0 >= N) break;
-      const int g8 = static_cast<int>(pos(col0) >> 3);
-      prefetch_l2_bulk(gu + gu_block_offset(band0, g8, gu_groups), 2048);
-      prefetch_l2_bulk(gu + gu_block_offset(band0, g8 + 16, gu_groups), 2048);
-    }
-  }
-
   // The stored operands of 32 columns are fetched one chunk ahead (chunk 0
   // before the accumulator is read), so the HBM latency overlaps the TMEM
   // loads and the math of the previous chunk instead of serialising with
-  // every store; the next tile's are prefetched into L2 meanwhile.
+  // every store.
   __device__ __forceinline__ void operator()(const tc::EpiCtx<BN>& c) const {
-    prefetch_next(c);
     const bool graft = (c.n0 + BN > g0) && (c.n0 < g1);
     const bool row_ok = c.row < M;
     float sg_s = 0.f, su_s = 0.f;

@@ -109,6 +109,21 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, ui
       "l"(reinterpret_cast<uint64_t>(tm)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
       : "memory");
 }
+// Same load with an L2 eviction-priority policy (createpolicy value).
+__device__ __forceinline__ void tma_load_2d_hint(void* dst, const CUtensorMap* tm, uint64_t* bar,
+                                                 int c0, int c1, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "l"(policy)
+      : "memory");
+}
+// L2 policy: keep the lines (evicted after evict_normal/evict_first lines).
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* tm) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tm)) : "memory");
 }
@@ -254,7 +269,6 @@ struct EpiCtx {
   int split;          // split-K index of this work unit
   int part, parts;    // this warp's share of the tile's columns (kParts > 1)
   uint8_t* scratch;   // this warp's kScratchPerWarp bytes of shared memory (128-byte aligned)
-  int next_m0, next_n0;  // origin of this CTA's next tile (-1: none), for L2 prefetches
   __device__ __forceinline__ void load(int col, float (&v)[32]) const {
     tmem_ld32(tmem_row + static_cast<uint32_t>(col), v);
   }
@@ -370,6 +384,11 @@ __global__ void __launch_bounds__(gemm_threads<Epi>(), 1)
   if (warp == 0) {
     // ------------------------------ TMA producer ------------------------------
     if (lane == 0) {
+      // A rows are reused by every N tile of the raster group (one group
+      // sweeps N in ~10 waves of the grid) while epilogues stream far more
+      // than L2 through it: A loads carry evict_last, B loads (reused by the
+      // group's M tiles within about one wave) the default.
+      const uint64_t pol_a = l2_policy_evict_last();
       int it = 0;
       for (int unit = blockIdx.x; unit < units && !s_abort; unit += gridDim.x) {
         int mt, nt, split;
@@ -388,9 +407,9 @@ __global__ void __launch_bounds__(gemm_threads<Epi>(), 1)
           if (A_MN) {
 #pragma unroll
             for (int c = 0; c < BM / 64; ++c)
-              tma_load_2d(a_tile + c * 8192, tma, &full_bar[s], m0 + 64 * c, k0);
+              tma_load_2d_hint(a_tile + c * 8192, tma, &full_bar[s], m0 + 64 * c, k0, pol_a);
           } else {
-            tma_load_2d(a_tile, tma, &full_bar[s], k0, m0);
+            tma_load_2d_hint(a_tile, tma, &full_bar[s], k0, m0, pol_a);
           }
           if (B_MN) {
 #pragma unroll
@@ -457,13 +476,6 @@ __global__ void __launch_bounds__(gemm_threads<Epi>(), 1)
       ctx.part = part;
       ctx.parts = PARTS;
       ctx.scratch = smem + L::SCRATCH_OFF + (warp - 2) * EpiScratch<Epi>::value;
-      ctx.next_m0 = ctx.next_n0 = -1;
-      if (unit + static_cast<int>(gridDim.x) < units) {
-        int nmt, nnt, nsplit;
-        unit_coords(unit + gridDim.x, shape, num_m, num_n, nmt, nnt, nsplit);
-        ctx.next_m0 = nmt * BM;
-        ctx.next_n0 = nnt * BN;
-      }
       epi(ctx);
       tc_fence_before();
       __syncwarp();

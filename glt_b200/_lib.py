@@ -89,6 +89,12 @@ SIGNATURES: dict[str, tuple] = {
     "glt_stack_grafts": (_i32, [C.POINTER(_vp), _i32, _i32, _i32, _i32, _vp, _vp]),
     "glt_model_create": (_i32, [_cfgp, _i32, _i32, _i32, C.POINTER(_vp)]),
     "glt_model_destroy": (_i32, [_vp]),
+    "glt_train_state_save": (_i32, [C.c_char_p, _vp, _vp, _vp, _i64, _i32, C.c_char_p, _i32, _i32, _i32,
+                                    _i32, _i32, _i64]),
+    "glt_train_state_load": (_i32, [C.c_char_p, _vp, _vp, _vp, _i64, _i32, C.c_char_p, _i32, _i32, _i32,
+                                    _i32, C.POINTER(_i64)]),
+    "glt_model_save_train_state": (_i32, [_vp, C.c_char_p, C.c_char_p, _i32, _i64]),
+    "glt_model_load_train_state": (_i32, [_vp, C.c_char_p, C.c_char_p, _i32, C.POINTER(_i64)]),
     "glt_model_memory": (_i32, [_vp, C.POINTER(_i64), C.POINTER(_i64)]),
     "glt_model_mlp_store": (_i32, [_vp, _i32, C.POINTER(_i32), C.POINTER(_i64)]),
     "glt_model_init_random": (_i32, [_vp, _u64, _f32, _f32, _f32]),

@@ -43,10 +43,13 @@ struct GltFailure : std::runtime_error {
                        std::to_string(__LINE__) + ": " + glt_last_error());                    \
   } while (0)
 
-const char* kProfNames[GLT_PROF_KINDS] = {
+const char* const kProfNames[] = {
     "gate_up_fwd", "down_fwd",  "delta_down", "qkv",     "o_proj",  "attn_fwd",   "dh",
     "recompute_swiglu_bwd", "wgrad_down", "wgrad_gate_up", "dx_gate_up", "do", "attn_bwd",
-    "dx_qkv", "lm_head", "lm_dx", "cross_entropy", "delta_expand", "graft_dgrad"};
+    "dx_qkv", "lm_head", "lm_dx", "cross_entropy", "delta_expand", "graft_dgrad", "rmsnorm",
+    "rope", "adamw"};
+static_assert(sizeof(kProfNames) / sizeof(kProfNames[0]) == GLT_PROF_KINDS,
+              "one name per GLT_PROF_* kind");
 
 void print_usage(const char* argv0) {
   std::cout
@@ -64,7 +67,10 @@ void print_usage(const char* argv0) {
       << "  --graft-proj-down 1 --allow-expansion-trap --graft-gemm-backend rocblas|hipblaslt-selective\n"
       << "  --delta-bf16-mirror --use-aten-delta-input-grad --profile-graft-gemms\n"
       << "  --parity-dump DIR --parity-dump-layer N --contract-probe --verbose --help\n"
-      << "  --graft-layout overlay|concat   (new; overlay is the reference geometry)\n";
+      << "  --graft-layout overlay|concat   (new; overlay is the reference geometry)\n"
+      << "  --save-state STATE --resume-state STATE --stop-after K\n"
+      << "      (new: fp32 graft + Adam moments + next step; --steps stays the schedule length,\n"
+      << "       --stop-after ends this run after step K-1 of it)\n";
 }
 
 bool is_dir(const std::string& p) {
@@ -75,6 +81,11 @@ bool exists(const std::string& p) {
   struct stat sb;
   return stat(p.c_str(), &sb) == 0;
 }
+long long file_size(const std::string& p) {
+  struct stat s;
+  return stat(p.c_str(), &s) == 0 ? static_cast<long long>(s.st_size) : -1;
+}
+
 std::string parent_of(const std::string& p) {
   const size_t k = p.find_last_of('/');
   return k == std::string::npos ? std::string() : p.substr(0, k);
@@ -147,11 +158,12 @@ int run(int argc, char** argv) {
   CHECK(glt_config_default(&cfg));
   std::string safetensors_path, domain_data_path, output_path, checkpoint_path, parity_dump_dir;
   std::vector<std::string> ood_data_paths;
-  std::string init_deltas_path, eval_data_path, session_id;
+  std::string init_deltas_path, eval_data_path, session_id, save_state_path, resume_state_path;
   std::string backend = "rocblas", layout = "overlay";
   int domain_id = 0, max_domains = 4, steps = 200, batch_size = 16, max_len = 512, seed = 42;
   float lr = 2e-4f;
   int parity_dump_layer = -1;
+  int stop_after = 0;
   bool eval_only = false, shadow_eval = false, profile = false, contract_probe = false, verbose = false;
   std::vector<int> no_rope;
 
@@ -220,6 +232,9 @@ int run(int argc, char** argv) {
     else if (a == "--contract-probe") contract_probe = true;
     else if (a == "--verbose") verbose = true;
     else if (a == "--graft-layout" && nx) layout = argv[++i];
+    else if (a == "--save-state" && nx) save_state_path = argv[++i];
+    else if (a == "--resume-state" && nx) resume_state_path = argv[++i];
+    else if (a == "--stop-after" && nx) stop_after = std::stoi(argv[++i]);
     else if (a == "--help") {
       print_usage(argv[0]);
       return 0;
@@ -257,6 +272,34 @@ int run(int argc, char** argv) {
   const int S = cfg.slice_dim;
   const int64_t graft_numel = static_cast<int64_t>(3) * cfg.num_layers * S * H;
   const char* sid = session_id.empty() ? nullptr : session_id.c_str();
+
+  // training-state flags (new): refused before any device work
+  const bool state_flags = !save_state_path.empty() || !resume_state_path.empty() || stop_after != 0;
+  if ((eval_only || shadow_eval) && state_flags) {
+    std::cerr << "Error: --save-state, --resume-state and --stop-after are training-only.\n";
+    return EXIT_FAILURE;
+  }
+  if (stop_after < 0) {
+    std::cerr << "Error: --stop-after must be positive.\n";
+    return EXIT_FAILURE;
+  }
+  if (!resume_state_path.empty() && (!checkpoint_path.empty() || !init_deltas_path.empty())) {
+    std::cerr << "Error: --resume-state restores the graft itself; it is incompatible with --checkpoint "
+                 "and --init-deltas.\n";
+    return EXIT_FAILURE;
+  }
+  if (!resume_state_path.empty() && !exists(resume_state_path)) {
+    std::cerr << "Error: training state '" << resume_state_path << "' does not exist.\n";
+    return EXIT_FAILURE;
+  }
+  if (!save_state_path.empty()) {
+    const std::string parent = parent_of(save_state_path);
+    if (is_dir(save_state_path) || (!parent.empty() && !exists(parent))) {
+      std::cerr << "Error: --save-state path '" << save_state_path
+                << "' is a directory or its parent directory does not exist.\n";
+      return EXIT_FAILURE;
+    }
+  }
 
   // ------------------------------ shadow eval ------------------------------
   if (shadow_eval) {
@@ -456,6 +499,28 @@ int run(int argc, char** argv) {
     if (!parity_dump_dir.empty()) write_raw(parity_dump_dir + "/delta_weights_loaded.raw", host.data(), expected);
   }
 
+  int start_step = 0;
+  if (!resume_state_path.empty()) {
+    int64_t k = 0;
+    std::cout << "[State] Resuming from " << resume_state_path << "\n";
+    if (glt_model_load_train_state(m, resume_state_path.c_str(), sid, domain_id, &k) != GLT_OK) {
+      std::cerr << "Error: " << glt_last_error() << "\n";
+      return EXIT_FAILURE;
+    }
+    if (k >= steps) {
+      std::cerr << "Error: the training state is at step " << k << "; --steps " << steps
+                << " is the length of the schedule and leaves nothing to run.\n";
+      return EXIT_FAILURE;
+    }
+    start_step = static_cast<int>(k);
+    std::cout << "[State] Restored the fp32 graft, the Adam moments and step " << k << ".\n";
+  }
+  const int end_step = stop_after > 0 ? std::min(steps, stop_after) : steps;
+  if (end_step <= start_step) {
+    std::cerr << "Error: --stop-after " << stop_after << " leaves nothing to run from step " << start_step << ".\n";
+    return EXIT_FAILURE;
+  }
+
   if (contract_probe) {  // run_contract_sparse_probe (graft_ops_impl.inc:158-212)
     std::cout << "[ContractProbe] Running synthetic sparse contract-forward test.\n";
     const int M = 2, stride = cfg.intermediate_dim;
@@ -501,11 +566,17 @@ int run(int argc, char** argv) {
 
   // grafting.hip:932-933: everything before the last '.', then "_log.csv"
   const std::string log_path = output_path.substr(0, output_path.find_last_of('.')) + "_log.csv";
-  std::ofstream log_file(log_path);
-  if (log_file)
+  // a resumed run appends to the log of the run it continues
+  const bool fresh_log = start_step == 0 || file_size(log_path) <= 0;
+  std::ofstream log_file(log_path, fresh_log ? std::ios::trunc : std::ios::app);
+  if (log_file && fresh_log)
     log_file << "step,lm_loss,silence_loss,domain_graft_energy,ood_graft_energy,domain_ood_energy_ratio,"
                 "total_loss,lr,grad_norm,step_time_sec\n";
-  std::cout << "[Loop] Starting training for " << steps << " steps.\n       Logging to " << log_path << "\n";
+  if (start_step)
+    std::cout << "[Loop] Resuming training at step " << start_step << " of " << steps
+              << ".\n       Logging to " << log_path << "\n";
+  else
+    std::cout << "[Loop] Starting training for " << steps << " steps.\n       Logging to " << log_path << "\n";
   if (profile) CHECK(glt_model_profile(m, 1));
 
   int dpos = 0, opos = 0;
@@ -514,7 +585,10 @@ int run(int argc, char** argv) {
   std::vector<int32_t> ids(static_cast<size_t>(batch_size) * T), mask(ids.size());
   std::vector<double> steady;
   float prev_norm = -1.f;
-  for (int step = 0; step < steps; ++step) {
+  for (int s = 0; s < start_step; ++s)  // the data walk of the steps already taken
+    CHECK(glt_batch_step(domain.tokens.data(), domain.num_sequences, ood.tokens.data(), ood.num_sequences, T,
+                         batch_size, &dpos, &opos, ids.data(), mask.data()));
+  for (int step = start_step; step < end_step; ++step) {
     CHECK(glt_batch_step(domain.tokens.data(), domain.num_sequences, ood.tokens.data(), ood.num_sequences, T,
                          batch_size, &dpos, &opos, ids.data(), mask.data()));
     GltStepStats st;
@@ -522,12 +596,12 @@ int run(int argc, char** argv) {
     CHECK(glt_train_step(m, ids.data(), mask.data(), 1, step, steps, &st, nullptr));
     const double sec = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
     peak_mb = std::max(peak_mb, used_mb());
-    if (step > 0) steady.push_back(sec);
+    if (step > start_step) steady.push_back(sec);
     // The reference logs the previous step's clip coefficient read back
     // asynchronously: grad_norm = clip / scale, scale = norm > clip ? clip / norm : 1
     // (calc_scale_kernel, kernels_elementwise_impl.inc:167-196), -1 at step 0.
     float grad_norm = -1.f, host_scale = -1.f;
-    if (step > 0) {
+    if (step > start_step) {
       host_scale = prev_norm > cfg.gradient_clip_norm ? cfg.gradient_clip_norm / prev_norm : 1.f;
       grad_norm = host_scale > 0.f ? cfg.gradient_clip_norm / host_scale : 0.f;
     }
@@ -571,6 +645,10 @@ int run(int argc, char** argv) {
   std::cout.unsetf(std::ios::fixed);
   std::cout << "[Save] Writing safetensors to " << output_path << "\n";
   CHECK(glt_model_save_checkpoint(m, output_path.c_str(), session_id.c_str(), domain_id));
+  if (!save_state_path.empty()) {
+    std::cout << "[State] Writing the training state (step " << end_step << ") to " << save_state_path << "\n";
+    CHECK(glt_model_save_train_state(m, save_state_path.c_str(), session_id.c_str(), domain_id, end_step));
+  }
   if (profile) {  // write_gemm_profile_stats_json (checkpoint_impl.inc:107-168), per fused kernel kind
     double ms[GLT_PROF_KINDS];
     int64_t calls[GLT_PROF_KINDS];

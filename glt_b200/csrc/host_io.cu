@@ -1,12 +1,15 @@
 // Host-side I/O of the graft path: the GRFT checkpoint (src/checkpoint_impl.inc),
-// the .bin token files and the seeded batch walk (src/data_impl.inc,
-// grafting.hip:924-988).  Pure C++ (no device code) except for the optional
-// device source/destination of the checkpoint weights; these entry points
-// work on GPU-less hosts when given host buffers.
+// the training-state file (fp32 graft + Adam moments + step, which the
+// reference does not keep), the .bin token files and the seeded batch walk
+// (src/data_impl.inc, grafting.hip:924-988).  Pure C++ (no device code)
+// except for the optional device source/destination of the weights; these
+// entry points work on GPU-less hosts when given host buffers.
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 #include <sys/stat.h>
 
+#include <map>
 #include <string>
 #include <vector>
 
@@ -166,6 +169,107 @@ bool parse_header(const char* p, size_t n, StHeader& h) {
   return false;
 }
 
+// ---- training state ("GLTS") ----
+constexpr uint32_t kStateMagic = 0x53544C47u;  // "GLTS" little endian
+constexpr uint8_t kStateVersion = 1;
+const char* const kStateTensors[3] = {"weights", "adam_m", "adam_v"};
+
+std::string json_escape(const char* s) {
+  std::string o;
+  for (; s && *s; ++s) {
+    const unsigned char c = static_cast<unsigned char>(*s);
+    if (c == '"' || c == '\\') { o.push_back('\\'); o.push_back(static_cast<char>(c)); }
+    else if (c < 0x20) { char b[8]; snprintf(b, sizeof(b), "\\u%04x", c); o += b; }
+    else o.push_back(static_cast<char>(c));
+  }
+  return o;
+}
+
+std::string state_header(const char* session, int domain, int S, int H, int D, int L, long long step) {
+  const long long total = 3LL * L;
+  const long long nb = total * S * static_cast<long long>(H) * 4;
+  char buf[256];
+  std::string s = "{\"__metadata__\":{\"format\":\"glt-train-state\",\"session_id\":\"";
+  s += json_escape(session);
+  snprintf(buf, sizeof(buf),
+           "\",\"domain_id\":\"%d\",\"slice_dim\":\"%d\",\"h_slice_dim\":\"%d\",\"hidden_dim\":\"%d\","
+           "\"num_layers\":\"%d\",\"step\":\"%lld\"}",
+           domain, S, H, D, L, step);
+  s += buf;
+  for (int t = 0; t < 3; ++t) {
+    snprintf(buf, sizeof(buf), ",\"%s\":{\"dtype\":\"F32\",\"shape\":[%lld,%d,%d],\"data_offsets\":[%lld,%lld]}",
+             kStateTensors[t], total, S, H, nb * t, nb * (t + 1));
+    s += buf;
+  }
+  return s + "}";
+}
+
+struct StTensor {
+  std::string dtype;
+  std::vector<long long> shape;
+  long long off0 = -1, off1 = -1;
+};
+
+// Any safetensors-style header: string metadata and every tensor entry.
+bool parse_header_all(const char* p, size_t n, std::map<std::string, std::string>& meta,
+                      std::map<std::string, StTensor>& tensors) {
+  Json j{p, p + n};
+  if (!j.eat('{')) return false;
+  if (j.eat('}')) return true;
+  while (j.ok) {
+    std::string key;
+    if (!j.str(key) || !j.eat(':')) return false;
+    if (key == "__metadata__") {
+      if (!j.eat('{')) return false;
+      if (!j.eat('}')) {
+        while (j.ok) {
+          std::string k, v;
+          if (!j.str(k) || !j.eat(':') || !j.str(v)) return false;
+          meta[k] = v;
+          if (j.eat(',')) continue;
+          if (j.eat('}')) break;
+          return false;
+        }
+      }
+    } else {
+      StTensor t;
+      if (!j.eat('{')) return false;
+      while (j.ok) {
+        std::string k;
+        if (!j.str(k) || !j.eat(':')) return false;
+        if (k == "dtype") {
+          if (!j.str(t.dtype)) return false;
+        } else if (k == "shape" || k == "data_offsets") {
+          if (!j.eat('[')) return false;
+          std::vector<long long> v;
+          if (!j.eat(']')) {
+            while (true) {
+              long long x;
+              if (!j.num(x)) return false;
+              v.push_back(x);
+              if (j.eat(',')) continue;
+              if (j.eat(']')) break;
+              return false;
+            }
+          }
+          if (k == "shape") t.shape = v;
+          else if (v.size() == 2) { t.off0 = v[0]; t.off1 = v[1]; }
+        } else if (!j.skip()) {
+          return false;
+        }
+        if (j.eat(',')) continue;
+        if (j.eat('}')) break;
+        return false;
+      }
+      tensors[key] = t;
+    }
+    if (j.eat(',')) continue;
+    if (j.eat('}')) return true;
+    return false;
+  }
+  return false;
+}
+
 bool read_file(const char* path, std::vector<char>& buf) {
   FILE* f = fopen(path, "rb");
   if (!f) return false;
@@ -249,6 +353,96 @@ int checkpoint_load(const char* path, float* host_w, int64_t numel, int expected
   return GLT_OK;
 }
 
+// Training state.  Each of the three tensors goes through `host_buf`
+// (numel floats): `fetch(t, host_buf)` supplies tensor t for a save and
+// `store(t, host_buf)` takes it after a load, so a device-resident state
+// needs one host staging buffer rather than three.
+template <class Fetch>
+int train_state_write(const char* path, int64_t numel, const char* session, int domain, int S, int H,
+                      int D, int L, int64_t step, float* host_buf, Fetch fetch) {
+  if (!path) return fail(GLT_EINVAL, "null argument");
+  if (numel != 3LL * L * S * H) return fail(GLT_EINVAL, "state numel %lld != 3*L*S*H", (long long)numel);
+  if (step < 0) return fail(GLT_EINVAL, "step must be >= 0");
+  if (is_dir(path)) return fail(GLT_EIO, "train state: path is a directory, not a file: %s", path);
+  const std::string par = parent_of(path);
+  if (!par.empty() && !is_dir(par.c_str()))
+    return fail(GLT_EIO, "train state: parent directory does not exist: %s", par.c_str());
+  const std::string hdr = state_header(session, domain, S, H, D, L, step);
+  const uint64_t pad = (8 - hdr.size() % 8) % 8;
+  const uint64_t hsize = hdr.size() + pad;
+  FILE* f = fopen(path, "wb");
+  if (!f) return fail(GLT_EIO, "cannot open %s for writing", path);
+  const uint32_t magic = kStateMagic;
+  const uint8_t ver = kStateVersion;
+  bool ok = fwrite(&magic, 4, 1, f) == 1 && fwrite(&ver, 1, 1, f) == 1 &&
+            fwrite(&hsize, 8, 1, f) == 1 && fwrite(hdr.data(), 1, hdr.size(), f) == hdr.size();
+  for (uint64_t i = 0; ok && i < pad; ++i) ok = fputc(0, f) != EOF;
+  for (int t = 0; ok && t < 3; ++t) {
+    const int st = fetch(t, host_buf);
+    if (st != GLT_OK) { fclose(f); return st; }
+    ok = numel == 0 || fwrite(host_buf, 4, static_cast<size_t>(numel), f) == static_cast<size_t>(numel);
+  }
+  ok = (fclose(f) == 0) && ok;
+  if (!ok) return fail(GLT_EIO, "short write to %s", path);
+  return GLT_OK;
+}
+
+template <class Store>
+int train_state_read(const char* path, int64_t numel, const char* session, int expected_domain,
+                     int total_proj, int S, int H, int64_t* step_out, float* host_buf, Store store) {
+  if (!path) return fail(GLT_EINVAL, "null argument");
+  FILE* f = fopen(path, "rb");
+  if (!f) return fail(GLT_EIO, "cannot open train state %s", path);
+  struct Closer { FILE* f; ~Closer() { fclose(f); } } closer{f};
+  fseeko(f, 0, SEEK_END);
+  const int64_t fsize = static_cast<int64_t>(ftello(f));
+  fseeko(f, 0, SEEK_SET);
+  uint32_t magic = 0;
+  uint8_t ver = 0;
+  uint64_t hlen = 0;
+  if (fsize < 13 || fread(&magic, 4, 1, f) != 1 || fread(&ver, 1, 1, f) != 1 || fread(&hlen, 8, 1, f) != 1)
+    return fail(GLT_EIO, "train state %s: file too small", path);
+  if (magic != kStateMagic) return fail(GLT_EIO, "%s is not a training-state file (magic)", path);
+  if (ver != kStateVersion) return fail(GLT_EIO, "train state %s: unsupported version %d", path, ver);
+  if (hlen > static_cast<uint64_t>(fsize - 13)) return fail(GLT_EIO, "train state: header past end of file");
+  std::string hdr(static_cast<size_t>(hlen), '\0');
+  if (hlen && fread(&hdr[0], 1, static_cast<size_t>(hlen), f) != hlen)
+    return fail(GLT_EIO, "train state: short header read");
+  std::map<std::string, std::string> meta;
+  std::map<std::string, StTensor> tensors;
+  if (!parse_header_all(hdr.data(), hdr.size(), meta, tensors))
+    return fail(GLT_EIO, "train state parse failed: bad JSON header");
+  if (meta["format"] != "glt-train-state") return fail(GLT_EIO, "train state: wrong format tag");
+  if (session && *session && !meta["session_id"].empty() && meta["session_id"] != session)
+    return fail(GLT_EIO, "session_id mismatch! State has '%s', current training session is '%s'",
+                meta["session_id"].c_str(), session);
+  if (meta.count("domain_id") == 0 || atoi(meta["domain_id"].c_str()) != expected_domain)
+    return fail(GLT_EIO, "train state domain_id mismatch: state has %s, expected %d",
+                meta.count("domain_id") ? meta["domain_id"].c_str() : "none", expected_domain);
+  if (meta.count("step") == 0) return fail(GLT_EIO, "train state: no step");
+  const long long step = atoll(meta["step"].c_str());
+  if (step < 0) return fail(GLT_EIO, "train state: negative step");
+  const int64_t n = static_cast<int64_t>(total_proj) * S * H;
+  if (numel != n) return fail(GLT_EINVAL, "destination holds %lld elements, need %lld", (long long)numel, (long long)n);
+  const int64_t data0 = 13 + static_cast<int64_t>(hlen);
+  for (int t = 0; t < 3; ++t) {
+    auto it = tensors.find(kStateTensors[t]);
+    if (it == tensors.end()) return fail(GLT_EIO, "'%s' not found in %s", kStateTensors[t], path);
+    const StTensor& ts = it->second;
+    if (ts.dtype != "F32") return fail(GLT_EIO, "%s dtype is not F32", kStateTensors[t]);
+    if (ts.shape.size() != 3 || ts.shape[0] != total_proj || ts.shape[1] != S || ts.shape[2] != H)
+      return fail(GLT_EIO, "%s shape mismatch. Expected [%d,%d,%d]", kStateTensors[t], total_proj, S, H);
+    if (ts.off0 < 0 || ts.off1 - ts.off0 != n * 4 || data0 + ts.off1 > fsize)
+      return fail(GLT_EIO, "truncated %s data in %s", kStateTensors[t], path);
+    if (fseeko(f, static_cast<off_t>(data0 + ts.off0), SEEK_SET) != 0 ||
+        (n && fread(host_buf, 4, static_cast<size_t>(n), f) != static_cast<size_t>(n)))
+      return fail(GLT_EIO, "short read of %s from %s", kStateTensors[t], path);
+    GLT_TRY(store(t, host_buf));
+  }
+  if (step_out) *step_out = step;
+  return GLT_OK;
+}
+
 }  // namespace glt
 
 // ------------------------------- C ABI -------------------------------------
@@ -307,6 +501,75 @@ extern "C" int glt_model_load_checkpoint(GltModel* m, const char* path, const ch
   if (!mm->gw) return glt::fail(GLT_ESTATE, "graft storage was freed by the shadow bake");
   GLT_TRY(glt_checkpoint_load(path, mm->gw, mm->graft_numel, 0, expected_domain_id, session_id,
                               3 * mm->L, mm->S, mm->H, nullptr));
+  GLT_TRY(mm->refresh_graft(nullptr));
+  GLT_CUDA_TRY(cudaDeviceSynchronize());
+  return GLT_OK;
+}
+
+extern "C" int glt_train_state_save(const char* path, const float* weights, const float* adam_m,
+                                    const float* adam_v, int64_t numel, int src_is_host,
+                                    const char* session_id, int domain_id, int slice_dim,
+                                    int h_slice_dim, int hidden_dim, int num_layers, int64_t step) {
+  if (!weights || !adam_m || !adam_v) return glt::fail(GLT_EINVAL, "null state buffer");
+  if (numel < 0) return glt::fail(GLT_EINVAL, "negative numel");
+  const float* src[3] = {weights, adam_m, adam_v};
+  std::vector<float> host(src_is_host ? 0 : static_cast<size_t>(numel));
+  float* hb = host.data();
+  return glt::train_state_write(path, numel, session_id, domain_id, slice_dim, h_slice_dim, hidden_dim,
+                                num_layers, step, src_is_host ? nullptr : hb,
+                                [&](int t, float*& buf) -> int {
+                                  if (src_is_host) { buf = const_cast<float*>(src[t]); return GLT_OK; }
+                                  return copy_weights(buf, src[t], numel * 4, 1, 0);
+                                });
+}
+
+extern "C" int glt_train_state_load(const char* path, float* weights, float* adam_m, float* adam_v,
+                                    int64_t numel, int dst_is_host, const char* session_id,
+                                    int expected_domain_id, int total_projections, int slice_dim,
+                                    int h_slice_dim, int64_t* step) {
+  if (!weights || !adam_m || !adam_v) return glt::fail(GLT_EINVAL, "null state buffer");
+  if (numel < 0) return glt::fail(GLT_EINVAL, "negative numel");
+  float* dst[3] = {weights, adam_m, adam_v};
+  std::vector<float> host(static_cast<size_t>(numel));
+  // read into a scratch buffer first, so a file that fails a check part way
+  // leaves the caller's buffers as they were
+  std::vector<float> staged(dst_is_host ? 3 * static_cast<size_t>(numel) : 0);
+  int64_t st_step = 0;
+  GLT_TRY(glt::train_state_read(path, numel, session_id, expected_domain_id, total_projections, slice_dim,
+                                h_slice_dim, &st_step, host.data(), [&](int t, float* buf) -> int {
+                                  if (dst_is_host) {
+                                    memcpy(staged.data() + static_cast<size_t>(t) * numel, buf,
+                                           static_cast<size_t>(numel) * 4);
+                                    return GLT_OK;
+                                  }
+                                  return copy_weights(dst[t], buf, numel * 4, 0, 1);
+                                }));
+  if (dst_is_host)
+    for (int t = 0; t < 3; ++t)
+      memcpy(dst[t], staged.data() + static_cast<size_t>(t) * numel, static_cast<size_t>(numel) * 4);
+  if (step) *step = st_step;
+  return GLT_OK;
+}
+
+extern "C" int glt_model_save_train_state(GltModel* m, const char* path, const char* session_id,
+                                          int domain_id, int64_t step) {
+  if (!m) return glt::fail(GLT_EINVAL, "null model");
+  glt::Model* mm = reinterpret_cast<glt::Model*>(m);
+  if (!mm->gw) return glt::fail(GLT_ESTATE, "graft storage was freed by the shadow bake");
+  GLT_CUDA_TRY(cudaDeviceSynchronize());
+  return glt_train_state_save(path, mm->gw, mm->adam_m, mm->adam_v, mm->graft_numel, 0, session_id,
+                              domain_id, mm->S, mm->H, mm->D, mm->L, step);
+}
+
+extern "C" int glt_model_load_train_state(GltModel* m, const char* path, const char* session_id,
+                                          int expected_domain_id, int64_t* step) {
+  if (!m) return glt::fail(GLT_EINVAL, "null model");
+  glt::Model* mm = reinterpret_cast<glt::Model*>(m);
+  if (!mm->gw) return glt::fail(GLT_ESTATE, "graft storage was freed by the shadow bake");
+  if (mm->shadow_baked) return glt::fail(GLT_ESTATE, "the model is shadow-baked");
+  GLT_CUDA_TRY(cudaDeviceSynchronize());
+  GLT_TRY(glt_train_state_load(path, mm->gw, mm->adam_m, mm->adam_v, mm->graft_numel, 0, session_id,
+                               expected_domain_id, 3 * mm->L, mm->S, mm->H, step));
   GLT_TRY(mm->refresh_graft(nullptr));
   GLT_CUDA_TRY(cudaDeviceSynchronize());
   return GLT_OK;

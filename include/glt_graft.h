@@ -487,6 +487,35 @@ GLT_API int glt_model_load_checkpoint(GltModel* m, const char* path, const char*
                                       int expected_domain_id);
 
 /* ------------------------------------------------------------------------ */
+/* Training state: no counterpart in the reference, whose checkpoint holds  */
+/* only the bf16 deltas, so that --checkpoint restarts Adam's moments, its  */
+/* bias correction and the LR schedule (grafting.hip:876-880).  This file   */
+/* resumes a run exactly: the fp32 master graft, both Adam moments and the  */
+/* index of the next step.  Bytes: u32 "GLTS" LE | u8 1 | u64 header size  */
+/* (JSON NUL-padded to 8) | JSON {"__metadata__": {format "glt-train-state",*/
+/* session_id, domain_id, slice_dim, h_slice_dim, hidden_dim, num_layers,   */
+/* step}, "weights" / "adam_m" / "adam_v": F32 [3L,S,H] with data_offsets}  */
+/* | fp32 LE data.  load checks format, dtype, shape, session_id (when both */
+/* are set) and domain_id, and leaves the destination untouched on failure  */
+/* (host destinations; device ones are written tensor by tensor).           */
+/* ------------------------------------------------------------------------ */
+GLT_API int glt_train_state_save(const char* path, const float* weights, const float* adam_m,
+                                 const float* adam_v, int64_t numel, int src_is_host,
+                                 const char* session_id, int domain_id, int slice_dim,
+                                 int h_slice_dim, int hidden_dim, int num_layers, int64_t step);
+GLT_API int glt_train_state_load(const char* path, float* weights, float* adam_m, float* adam_v,
+                                 int64_t numel, int dst_is_host, const char* session_id,
+                                 int expected_domain_id, int total_projections, int slice_dim,
+                                 int h_slice_dim, int64_t* step);
+/* Model-level: its fp32 graft and Adam state; load also refreshes the bf16
+ * graft copies in the fused weights.  `step` is the index of the next
+ * training step (glt_train_step's step argument). */
+GLT_API int glt_model_save_train_state(GltModel* m, const char* path, const char* session_id,
+                                       int domain_id, int64_t step);
+GLT_API int glt_model_load_train_state(GltModel* m, const char* path, const char* session_id,
+                                       int expected_domain_id, int64_t* step);
+
+/* ------------------------------------------------------------------------ */
 /* Token data (host).  .bin = [i32 nseq][i32 seq_len][i32 tokens...] with   */
 /* the checks of load_bin (src/data_impl.inc:9-58); tokens = NULL reads and */
 /* validates only the header.  The batch walk is grafting.hip:924-988:      */

@@ -85,3 +85,16 @@ def test_safetensors_tensor_info(tmp_path):
     with pytest.raises(_lib.GltError):
         _lib.check(_lib.lib.glt_safetensors_tensor_info(str(bad).encode(), b"x", C.byref(found), shape,
                                                         C.byref(nd)))
+
+
+def test_train_state_flag_refusals(tmp_path):
+    r = run_cli("--eval-only", "--safetensors", "m", "--eval-data", "e.bin", "--save-state", "x.state")
+    assert r.returncode != 0 and "training-only" in r.stderr
+    r = run_cli(*TRAIN, "--resume-state", "x.state", "--checkpoint", "c.graft")
+    assert r.returncode != 0 and "incompatible with --checkpoint" in r.stderr
+    r = run_cli(*TRAIN, "--resume-state", str(tmp_path / "none.state"))
+    assert r.returncode != 0 and "does not exist" in r.stderr
+    r = run_cli(*TRAIN, "--save-state", str(tmp_path))
+    assert r.returncode != 0 and "--save-state path" in r.stderr
+    r = run_cli("--help")
+    assert "--resume-state" in r.stdout

@@ -147,3 +147,35 @@ def test_untied_transposed_lm_head_and_contract_probe(files, tmp_path):
     assert p.returncode == 0, p.stderr[-2000:]
     assert "out[0,11]=14" in p.stdout and "out[1,23]=65" in p.stdout
     assert "max_abs=65" in p.stdout
+
+
+def test_stop_and_resume_continue_the_run(files, tmp_path):
+    """--stop-after 2 + --save-state, then --resume-state, follows the same
+    4-step schedule as one uninterrupted run: same batch walk, LR, losses
+    (to the rounding of fp32 atomics) and trained graft; the resumed run
+    appends to the log."""
+    d, rc, w, dom, ood, ev = files
+    common = ["--safetensors", d / "model.safetensors", "--domain-data", d / "dom.bin", "--ood-data",
+              d / "ood1.bin", d / "ood2.bin", "--steps", 4, "--batch-size", 2, "--lr", 1e-3,
+              "--warmup-steps", 1, "--seed", 7, "--session-id", "s1", *DIMS]
+    full = run_cli(*common, "--output", tmp_path / "full.graft")
+    part = run_cli(*common, "--output", tmp_path / "part.graft", "--stop-after", 2,
+                   "--save-state", tmp_path / "s.state")
+    rest = run_cli(*common, "--output", tmp_path / "part.graft", "--resume-state", tmp_path / "s.state",
+                   "--save-state", tmp_path / "s2.state")
+    for p in (full, part, rest):
+        assert p.returncode == 0, p.stdout[-2000:] + p.stderr[-2000:]
+    assert "Resuming training at step 2 of 4" in rest.stdout
+    a = list(csv.DictReader(open(tmp_path / "full_log.csv")))
+    b = list(csv.DictReader(open(tmp_path / "part_log.csv")))
+    assert [r["step"] for r in b] == ["0", "1", "2", "3"]
+    for ra, rb in zip(a, b):
+        assert float(rb["lr"]) == float(ra["lr"])
+        for k in ("lm_loss", "silence_loss", "total_loss"):
+            assert float(rb[k]) == pytest.approx(float(ra[k]), rel=1e-4, abs=1e-7), (ra["step"], k)
+    blob = open(tmp_path / "s2.state", "rb").read()
+    assert blob[:4] == b"GLTS" and b'"step":"4"' in blob
+    n, S, H = rc.total_projections, rc.slice_dim, rc.h_slice_dim
+    ga = bx.parse_grft(open(tmp_path / "full.graft", "rb").read(), 1, "s1", n, S, H)
+    gb = bx.parse_grft(open(tmp_path / "part.graft", "rb").read(), 1, "s1", n, S, H)
+    np.testing.assert_allclose(gb, ga, rtol=0, atol=1e-2 * float(np.abs(ga).max()))

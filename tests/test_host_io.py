@@ -139,3 +139,103 @@ def test_batch_step_rejects_odd_batch():
     a = np.zeros(8, np.int32)
     dp, op = C.c_int(0), C.c_int(0)
     assert lib.glt_batch_step(_ptr(a), 1, _ptr(a), 1, 4, 3, C.byref(dp), C.byref(op), _ptr(a), _ptr(a)) == 1
+
+
+# ---------------------------------------------------------------------------
+# Training state (fp32 graft + Adam moments + next step): a format of this
+# build (the reference keeps only the bf16 deltas), so the checks are exact
+# round trips, the header's contents and the refusals.
+# ---------------------------------------------------------------------------
+def state_arrays(n, seed=3):
+    rng = np.random.default_rng(seed)
+    return [rng.standard_normal(n).astype(np.float32) for _ in range(3)]
+
+
+def state_save(path, arrs, step=7, session="sess", domain=1, S=4, H=8, D=32, L=2):
+    w, m, v = arrs
+    return lib.glt_train_state_save(path.encode(), _ptr(w), _ptr(m), _ptr(v), w.size, 1, session.encode(),
+                                    domain, S, H, D, L, step)
+
+
+def state_load(path, n, session="sess", domain=1, S=4, H=8, L=2, fill=0.0):
+    outs = [np.full(n, fill, np.float32) for _ in range(3)]
+    step = C.c_int64(-1)
+    st = lib.glt_train_state_load(path.encode(), _ptr(outs[0]), _ptr(outs[1]), _ptr(outs[2]), n, 1,
+                                  session.encode(), domain, 3 * L, S, H, C.byref(step))
+    return st, outs, step.value
+
+
+def test_train_state_roundtrip_is_exact(tmp_path):
+    arrs = state_arrays(3 * 2 * 4 * 8)
+    arrs[0][5] = np.float32(np.nan)           # bit patterns survive, NaN included
+    arrs[1][0] = np.float32(-0.0)
+    p = str(tmp_path / "run.state")
+    assert state_save(p, arrs, step=123) == 0, _lib.last_error()
+    st, outs, step = state_load(p, arrs[0].size)
+    assert st == 0 and step == 123, _lib.last_error()
+    for a, b in zip(arrs, outs):
+        assert a.tobytes() == b.tobytes()
+
+
+def test_train_state_bytes(tmp_path):
+    n = 3 * 2 * 4 * 8
+    arrs = state_arrays(n)
+    p = str(tmp_path / "run.state")
+    assert state_save(p, arrs, step=9, session='a"b') == 0
+    blob = open(p, "rb").read()
+    assert blob[:4] == b"GLTS" and blob[4] == 1
+    hlen = struct.unpack("<Q", blob[5:13])[0]
+    assert hlen % 8 == 0
+    import json
+    hdr = json.loads(blob[13:13 + hlen].rstrip(b"\0"))
+    meta = hdr["__metadata__"]
+    assert meta == {"format": "glt-train-state", "session_id": 'a"b', "domain_id": "1", "slice_dim": "4",
+                    "h_slice_dim": "8", "hidden_dim": "32", "num_layers": "2", "step": "9"}
+    data = blob[13 + hlen:]
+    assert len(data) == 3 * n * 4
+    for k, (name, a) in enumerate(zip(("weights", "adam_m", "adam_v"), arrs)):
+        assert hdr[name] == {"dtype": "F32", "shape": [6, 4, 8], "data_offsets": [k * n * 4, (k + 1) * n * 4]}
+        assert data[k * n * 4:(k + 1) * n * 4] == a.astype("<f4").tobytes()
+
+
+@pytest.mark.parametrize("case", ["domain", "session", "shape", "dtype", "truncated", "missing", "grft",
+                                  "format"])
+def test_train_state_load_rejections_leave_buffers(tmp_path, case):
+    n = 3 * 2 * 4 * 8
+    arrs = state_arrays(n)
+    p = str(tmp_path / "run.state")
+    assert state_save(p, arrs) == 0
+    kw = {}
+    if case == "domain":
+        kw["domain"] = 0
+    elif case == "session":
+        kw["session"] = "other"
+    elif case == "shape":
+        kw["S"] = 5
+    elif case == "dtype":
+        blob = open(p, "rb").read().replace(b'"F32"', b'"F16"', 1)
+        open(p, "wb").write(blob)
+    elif case == "truncated":
+        blob = open(p, "rb").read()
+        open(p, "wb").write(blob[:-4])
+    elif case == "missing":
+        p = str(tmp_path / "nope.state")
+    elif case == "grft":
+        assert save(p, arrs[0]) == 0            # a GRFT checkpoint is not a training state
+    elif case == "format":
+        blob = open(p, "rb").read().replace(b"glt-train-state", b"glt-train-stat_", 1)
+        open(p, "wb").write(blob)
+    m = n if case != "shape" else 3 * 2 * 5 * 8
+    st, outs, step = state_load(p, m, fill=2.5, **kw)
+    assert st in (1, 4), (case, st)
+    assert step == -1
+    assert all(np.all(o == 2.5) for o in outs)   # untouched on failure
+
+
+def test_train_state_save_refusals(tmp_path):
+    arrs = state_arrays(3 * 2 * 4 * 8)
+    assert state_save(str(tmp_path), arrs) == 4
+    assert state_save(str(tmp_path / "no" / "dir" / "x.state"), arrs) == 4
+    assert state_save(str(tmp_path / "x.state"), arrs, step=-1) == 1
+    bad = [a[:-1] for a in arrs]
+    assert state_save(str(tmp_path / "x.state"), bad) == 1

@@ -89,12 +89,13 @@ int launch_gemm(const Operand& A, const Operand& B, int M, int N, int K, const E
 }
 
 // Picks a k-split so that the work units fill the SMs (weight-grad GEMMs have
-// few output tiles and a long K = token dimension).
-inline int pick_k_splits(int M, int N, int K, int bn) {
+// few output tiles and a long K = token dimension): about `waves2 / 2` waves
+// of units (default 2 waves; fewer splits mean fewer fp32 atomics).
+inline int pick_k_splits(int M, int N, int K, int bn, int waves2 = 4) {
   const int tiles = ((M + 127) / 128) * ((N + bn - 1) / bn);
   const int sms = num_sms();
   if (tiles >= sms) return 1;
-  int s = (2 * sms + tiles - 1) / tiles;  // aim for ~2 waves of units
+  int s = (waves2 * sms + 2 * tiles - 1) / (2 * tiles);
   const int max_s = K / (tc::BK * 4);    // keep >= 4 k-blocks per split
   if (s > max_s) s = max_s;
   return s < 1 ? 1 : s;

@@ -709,19 +709,21 @@ int Model::ffn_backward(int l, cudaStream_t st) {
     GLT_PROF(GLT_PROF_RECOMPUTE,
              (launch_gemm<256, 4, false, false>(kmaj(y.x_ffn, D), kmaj(y.w_gu, D), M, 2 * ff, D, e, st)));
   }
-  // graft weight gradients (K = tokens, split-K with atomic accumulation)
+  // graft weight gradients (K = tokens, split-K with atomic accumulation).
+  // 128x256 tiles: at the config-3 shapes they ran 1.5x faster than 128x128
+  // (half the L2 operand traffic per FLOP), with splits for ~1.5 waves.
   if (down) {
-    const int sp = pick_k_splits(S, D, M, 128);
-    EpiF32<128> e{grad + (3 * l + 2) * SH, H, S, D, 1.f, 0.f, 1, 1};
-    GLT_PROF(GLT_PROF_WGRAD_DOWN, (launch_gemm<128, 6, true, true>(mnmaj(hg, S_pad), mnmaj(dyg_b, D), S, D, M, e, st, sp)));
+    const int sp = pick_k_splits(S, D, M, 256, 3);
+    EpiF32<256> e{grad + (3 * l + 2) * SH, H, S, D, 1.f, 0.f, 1, 1};
+    GLT_PROF(GLT_PROF_WGRAD_DOWN, (launch_gemm<256, 4, true, true>(mnmaj(hg, S_pad), mnmaj(dyg_b, D), S, D, M, e, st, sp)));
   }
   if (gate || up) {
     const int rows = 2 * S_pad;
-    const int sp = pick_k_splits(rows, D, M, 128);
-    EpiGradGateUp<128> e{gate ? grad + (3 * l) * SH : nullptr, up ? grad + (3 * l + 1) * SH : nullptr,
+    const int sp = pick_k_splits(rows, D, M, 256, 3);
+    EpiGradGateUp<256> e{gate ? grad + (3 * l) * SH : nullptr, up ? grad + (3 * l + 1) * SH : nullptr,
                          H, S, D};
     GLT_PROF(GLT_PROF_WGRAD_GATE_UP,
-             (launch_gemm<128, 6, true, true>(mnmaj(dgu + 2 * static_cast<int64_t>(F_pad), 2 * static_cast<int64_t>(FF)),
+             (launch_gemm<256, 4, true, true>(mnmaj(dgu + 2 * static_cast<int64_t>(F_pad), 2 * static_cast<int64_t>(FF)),
                                               mnmaj(y.x_ffn, D), rows, D, M, e, st, sp)));
   }
   // input grad through the fused gate/up weights

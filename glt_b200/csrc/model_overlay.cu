@@ -119,21 +119,34 @@ int Model::ffn_backward_overlay(int l, cudaStream_t st) {
              (launch_gemm<256, 4, false, false>(kmaj(y.x_ffn, D), kmaj(y.w_gu, D), M, 2 * FF, D, e, st)));
   }
   // ContractWeightGrad (graft_ops_impl.inc:214-228): dDelta_down = h_sliceᵀ . dyh
-  if (d) {
-    const int sp = pick_k_splits(S, H, M, 128);
-    EpiF32<128> e{grad + (3 * l + 2) * SH, H, S, H, 1.f, 0.f, 1, 1};
-    GLT_PROF(GLT_PROF_WGRAD_DOWN, (launch_gemm<128, 6, true, true>(mnmaj(hg, S_pad), mnmaj(dyg_b, H),
-                                                                   S, H, M, e, st, sp)));
-  }
   // ExpandWeightGrad (graft_ops_impl.inc:120-156): dDelta_{gate,up} = dysᵀ . x_h
+  // 128x256 tiles when the H slice is wide (half the L2 operand traffic per
+  // FLOP of 128x128), splits for ~1.5 waves.
+  const bool wide = H >= 512;
+  if (d) {
+    if (wide) {
+      EpiF32<256> e{grad + (3 * l + 2) * SH, H, S, H, 1.f, 0.f, 1, 1};
+      GLT_PROF(GLT_PROF_WGRAD_DOWN, (launch_gemm<256, 4, true, true>(mnmaj(hg, S_pad), mnmaj(dyg_b, H), S, H, M,
+                                                                     e, st, pick_k_splits(S, H, M, 256, 3))));
+    } else {
+      EpiF32<128> e{grad + (3 * l + 2) * SH, H, S, H, 1.f, 0.f, 1, 1};
+      GLT_PROF(GLT_PROF_WGRAD_DOWN, (launch_gemm<128, 6, true, true>(mnmaj(hg, S_pad), mnmaj(dyg_b, H), S, H, M,
+                                                                     e, st, pick_k_splits(S, H, M, 128))));
+    }
+  }
   if (g || u) {
     const int p0 = g ? 0 : 1;
     const int rows = (g && u) ? 2 * S : S;
-    const int sp = pick_k_splits(rows, H, M, 128);
-    EpiF32<128> e{grad + (3 * l + p0) * SH, H, rows, H, 1.f, 0.f, 1, 1};
-    GLT_PROF(GLT_PROF_WGRAD_GATE_UP,
-             (launch_gemm<128, 6, true, true>(mnmaj(dys + p0 * S, S2), mnmaj(y.x_ffn + h0, D), rows, H,
-                                              M, e, st, sp)));
+    const Operand a = mnmaj(dys + p0 * S, S2), b = mnmaj(y.x_ffn + h0, D);
+    if (wide) {
+      EpiF32<256> e{grad + (3 * l + p0) * SH, H, rows, H, 1.f, 0.f, 1, 1};
+      GLT_PROF(GLT_PROF_WGRAD_GATE_UP,
+               (launch_gemm<256, 4, true, true>(a, b, rows, H, M, e, st, pick_k_splits(rows, H, M, 256, 3))));
+    } else {
+      EpiF32<128> e{grad + (3 * l + p0) * SH, H, rows, H, 1.f, 0.f, 1, 1};
+      GLT_PROF(GLT_PROF_WGRAD_GATE_UP,
+               (launch_gemm<128, 6, true, true>(a, b, rows, H, M, e, st, pick_k_splits(rows, H, M, 128))));
+    }
   }
   // base input grad through gate/up
   {

@@ -68,8 +68,13 @@ def test_overlay_forward_matches_oracle(domain_id):
 
 
 @pytest.mark.parametrize("projs", [(0, 0, 1), (1, 0, 1), (0, 1, 0), (1, 1, 1)])
-def test_overlay_train_step_matches_oracle(projs):
-    rc = ov_cfg(graft_proj_gate=projs[0], graft_proj_up=projs[1], graft_proj_down=projs[2])
+def test_overlay_train_step_matches_oracle(projs, wide=False):
+    over = dict(graft_proj_gate=projs[0], graft_proj_up=projs[1], graft_proj_down=projs[2])
+    if wide:
+        # H = 2048 / 4 = 512: the weight-grad GEMMs take 128x256 tiles
+        over.update(hidden_dim=2048, num_heads=16, num_kv_heads=4, intermediate_dim=1024, slice_dim=256,
+                    num_layers=1, graft_layer_end=0)
+    rc = ov_cfg(**over)
     B, T = 4, 128
     w, delta, ids, ood = problem(rc, B, T)
     m = gpu_model(rc, w, delta, B, T)
@@ -100,6 +105,11 @@ def test_overlay_train_step_matches_oracle(projs):
     rm.clip_grads(g2, rc.gradient_clip_norm)
     rm.adamw(w_ref, g2, torch.zeros_like(w_ref), torch.zeros_like(w_ref), 0, rc.get_lr(0, 10), rc)
     torch.testing.assert_close(w_gpu, w_ref, rtol=1e-5, atol=1e-8)
+
+
+@pytest.mark.parametrize("projs", [(1, 1, 1), (0, 0, 1)])
+def test_overlay_train_step_wide_h_slice(projs):
+    test_overlay_train_step_matches_oracle(projs, wide=True)
 
 
 def test_overlay_layer_range_and_base_only_forward():

@@ -22,6 +22,7 @@
 #include <string.h>
 
 #include "common.cuh"
+#include "gemm.cuh"
 #include "model.cuh"
 
 namespace glt {
@@ -205,6 +206,7 @@ int Model::eval_alloc() {
 
 int Model::eval(const int32_t* ids_in, int64_t n_seq, int host, int use_graft, GltEvalStats* out,
                 cudaStream_t st) {
+  ScopedTileCounter tile_claims(gemm_counter());
   if (kind != GLT_MODEL_DECODER) return fail(GLT_ESTATE, "eval needs the decoder model");
   if (!ids_in || !out) return fail(GLT_EINVAL, "null argument");
   if (n_seq <= 0) return fail(GLT_EINVAL, "eval needs at least one sequence");

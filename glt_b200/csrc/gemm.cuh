@@ -25,6 +25,20 @@ int make_tmap_f32_plain(CUtensorMap* tm, const void* base, uint64_t inner, uint6
                         uint64_t ld, uint32_t box_inner, uint32_t box_outer);
 
 int num_sms();
+
+// Dynamic tile claiming (GemmShape::tile_ctr) for the GEMMs this host thread
+// launches: a device int[2], zero at rest, used by one stream at a time.
+// A model sets its own counter around its steps (ScopedTileCounter); every
+// other caller keeps the round-robin schedule.
+inline int*& gemm_tile_counter() {
+  static thread_local int* ctr = nullptr;
+  return ctr;
+}
+struct ScopedTileCounter {
+  int* prev;
+  explicit ScopedTileCounter(int* c) : prev(gemm_tile_counter()) { gemm_tile_counter() = c; }
+  ~ScopedTileCounter() { gemm_tile_counter() = prev; }
+};
 // Sets the dynamic-smem attribute of `func` to `bytes` once per process.
 int ensure_smem_attr(const void* func, int bytes);
 
@@ -76,6 +90,7 @@ int launch_gemm(const Operand& A, const Operand& B, int M, int N, int K, const E
   shape.group_m = group_m;
   shape.m_dev = m_dev;
   shape.m_off = m_off;
+  shape.tile_ctr = gemm_tile_counter();
   shape.err = device_error_word();
   if (!shape.err) return fail(GLT_ECUDA, "device error word unavailable");
   auto kern = tc_gemm_kernel<BN, STAGES, A_MN, B_MN, Epi>;

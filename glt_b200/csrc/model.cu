@@ -267,6 +267,11 @@ int Model::setup(const GltModelConfig& c, int batch, int seq, int k) {
       enabled.push_back(on ? 1 : 0);
       active_grafts += on ? 1 : 0;
     }
+  if (const char* e = getenv("GLT_GEMM_SCHEDULE")) {
+    if (strcmp(e, "dynamic") == 0) tile_ctr_on = true;
+    else if (strcmp(e, "static") != 0)
+      return fail(GLT_EINVAL, "GLT_GEMM_SCHEDULE=%s (static or dynamic)", e);
+  }
   if (const char* e = getenv("GLT_MLP_STORE")) {
     const int v = atoi(e);
     if (v < 0 || v > 2) return fail(GLT_EINVAL, "GLT_MLP_STORE=%s (0 recompute, 1 store, 2 auto)", e);
@@ -403,6 +408,7 @@ int Model::allocate() {
     add(reinterpret_cast<void**>(&dys), b2 * M * 2 * static_cast<size_t>(S));
   }
   add(reinterpret_cast<void**>(&stats), sizeof(DevStats));
+  add(reinterpret_cast<void**>(&tile_ctr), 2 * sizeof(int));   // zeroed with the arena
   add(reinterpret_cast<void**>(&d_enabled), sizeof(int) * 3 * L);
   add(reinterpret_cast<void**>(&d_gu_ptrs), sizeof(void*) * L);
   add(reinterpret_cast<void**>(&d_wd_ptrs), sizeof(void*) * L);
@@ -772,6 +778,7 @@ int Model::forward_all(bool use_graft, cudaStream_t st) {
 
 int Model::train_step(const int32_t* ids_in, const int32_t* ood_in, int host, int step,
                       int total_steps, GltStepStats* out, cudaStream_t st) {
+  ScopedTileCounter tile_claims(gemm_counter());
   if (kind != GLT_MODEL_DECODER) return fail(GLT_ESTATE, "train_step needs the decoder model");
   if (shadow_baked) return fail(GLT_ESTATE, "backward on a shadow-baked model is forbidden");
   GLT_TRY(load_inputs(ids_in, ood_in, host, st));
@@ -873,6 +880,7 @@ int Model::finish_step(int step, int total_steps, GltStepStats* out, cudaStream_
 
 int Model::forward_logits(const int32_t* ids_in, int host, int use_graft, uint16_t* out,
                           cudaStream_t st) {
+  ScopedTileCounter tile_claims(gemm_counter());
   if (kind != GLT_MODEL_DECODER) return fail(GLT_ESTATE, "forward needs the decoder model");
   if (use_graft && !gw) return fail(GLT_ESTATE, "graft storage was freed by the shadow bake");
   GLT_TRY(load_inputs(ids_in, nullptr, host, st));
@@ -885,6 +893,7 @@ int Model::forward_logits(const int32_t* ids_in, int host, int use_graft, uint16
 
 int Model::block_step(const uint16_t* x, const float* y_t, float lr, int step, float* loss,
                       uint16_t* out, float* dx_out, cudaStream_t st) {
+  ScopedTileCounter tile_claims(gemm_counter());
   if (kind != GLT_MODEL_MLP_BLOCK) return fail(GLT_ESTATE, "block_step needs the MLP-block model");
   if (!gw) return fail(GLT_ESTATE, "graft storage was freed by the shadow bake");
   GLT_CUDA_TRY(cudaMemsetAsync(stats, 0, sizeof(DevStats), st));

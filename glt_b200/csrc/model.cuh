@@ -109,6 +109,11 @@ struct Model {
   int32_t* ids = nullptr;
   int32_t* ood = nullptr;
   float last_lr = 0.f;
+  // GEMM tile-claim counter of this model's stream, used with
+  // GLT_GEMM_SCHEDULE=dynamic (default static: round-robin units)
+  int* tile_ctr = nullptr;
+  int* gemm_counter() const { return tile_ctr_on ? tile_ctr : nullptr; }
+  bool tile_ctr_on = false;
 
   // Stored MLP activations: the training forward keeps bf16 gate_pre/up of
   // every layer (L * M * 2F' * 2 bytes) so the backward fuses SwiGLU's

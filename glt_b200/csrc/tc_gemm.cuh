@@ -23,7 +23,12 @@
 //               (EpiCtx::scratch), used to turn row-per-lane results into
 //               coalesced stores.
 // Two TMEM accumulators (2*BN columns) let the epilogue of tile i overlap
-// the main loop of tile i+1.  Every TMA load is a plain per-CTA load into
+// the main loop of tile i+1.  The producer picks each CTA's work units and
+// hands them to the MMA and epilogue warps through a small shared-memory
+// ring: round-robin (unit = blockIdx.x + t * gridDim.x) by default, or, with
+// GemmShape::tile_ctr, claimed from a device counter in raster order, so a
+// CTA that starts late (its SM busy with another kernel, such as a
+// collective) takes fewer tiles instead of finishing last.  Every TMA load is a plain per-CTA load into
 // the CTA's own shared memory, so the kernel is safe in multi-GPU jobs.
 //
 // Every mbarrier wait is bounded (GLT_MBAR_TIMEOUT_NS of %globaltimer);
@@ -234,7 +239,13 @@ struct GemmShape {
   // earlier kernel on the stream then needs no host round trip.
   const int* m_dev = nullptr;
   int m_off = 0;
+  // Optional dynamic tile claiming: two ints, zero before the launch; the
+  // last CTA to finish sets them back to zero for the next launch on the
+  // stream.  One counter pair per stream (launches on it must not overlap).
+  int* tile_ctr = nullptr;
 };
+
+constexpr int UNIT_RING = 4;   // work units in flight between the producer and the consumers
 
 // Epilogue warps per TMEM sub-partition: Epi::kParts when the functor
 // declares it, else 1.
@@ -280,8 +291,8 @@ struct SmemLayout {
   static constexpr uint32_t B_BYTES = TileBytes<BN>::value;
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr uint32_t TILES_BYTES = STAGES * STAGE_BYTES;
-  // barriers + tmem slot after the tiles
-  static constexpr uint32_t BAR_BYTES = (2 * STAGES + 5) * 8 + 16;
+  // barriers (stages, accumulators, drain, unit ring) + unit ids + tmem slot after the tiles
+  static constexpr uint32_t BAR_BYTES = (2 * STAGES + 5 + 2 * UNIT_RING) * 8 + UNIT_RING * 4 + 16;
   static constexpr uint32_t TOTAL = 1024 /*align slack*/ + TILES_BYTES + BAR_BYTES;
   // epilogue scratch after the barriers
   static constexpr uint32_t SCRATCH_OFF = (TILES_BYTES + BAR_BYTES + 127) / 128 * 128;
@@ -335,7 +346,10 @@ __global__ void __launch_bounds__(gemm_threads<Epi>(), 1)
   uint64_t* tfull_bar = empty_bar + STAGES;   // [2]
   uint64_t* tempty_bar = tfull_bar + 2;       // [2]
   uint64_t* drain_bar = tempty_bar + 2;      // [1] final MMA drain
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  uint64_t* ufull_bar = drain_bar + 1;       // [UNIT_RING] unit id published
+  uint64_t* uempty_bar = ufull_bar + UNIT_RING;  // [UNIT_RING] unit id read by every consumer
+  volatile int* unit_ring = reinterpret_cast<volatile int*>(uempty_bar + UNIT_RING);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(const_cast<int*>(unit_ring) + UNIT_RING);
   __shared__ int s_abort_storage;
   volatile int& s_abort = s_abort_storage;
 
@@ -364,6 +378,10 @@ __global__ void __launch_bounds__(gemm_threads<Epi>(), 1)
       mbar_init(&tempty_bar[b], 4 * PARTS);
     }
     mbar_init(drain_bar, 1);
+    for (int r = 0; r < UNIT_RING; ++r) {
+      mbar_init(&ufull_bar[r], 1);
+      mbar_init(&uempty_bar[r], 1 + 4 * PARTS);   // MMA thread + epilogue warps
+    }
     s_abort = 0;
     fence_mbar_init();
   }
@@ -389,8 +407,19 @@ __global__ void __launch_bounds__(gemm_threads<Epi>(), 1)
       // than L2 through it: A loads carry evict_last, B loads (reused by the
       // group's M tiles within about one wave) the default.
       const uint64_t pol_a = l2_policy_evict_last();
+      int* const ctr = shape.tile_ctr;
+      int claim = ctr ? atomicAdd(ctr, 1) : static_cast<int>(blockIdx.x);
       int it = 0;
-      for (int unit = blockIdx.x; unit < units && !s_abort; unit += gridDim.x) {
+      for (int t = 0; !s_abort; ++t) {
+        // publish this CTA's next unit (-1: none left) to the MMA and epilogue warps
+        const int slot = t % UNIT_RING;
+        if (!mbar_wait(&uempty_bar[slot], ((t / UNIT_RING) & 1) ^ 1, shape.err)) { s_abort = 1; break; }
+        const int unit = claim < units ? claim : -1;
+        unit_ring[slot] = unit;
+        mbar_arrive(&ufull_bar[slot]);
+        if (unit < 0) break;
+        // the next claim is in flight while this unit's loads are issued
+        claim = ctr ? atomicAdd(ctr, 1) : unit + static_cast<int>(gridDim.x);
         int mt, nt, split;
         unit_coords(unit, shape, num_m, num_n, mt, nt, split);
         const CUtensorMap* tma = (nt >= shape.a2_n_tile) ? &tmA2 : &tmA;
@@ -420,12 +449,25 @@ __global__ void __launch_bounds__(gemm_threads<Epi>(), 1)
           }
         }
       }
+      if (ctr) {
+        // every claim of this CTA is done; the last CTA out re-arms the counter
+        __threadfence();
+        if (atomicAdd(ctr + 1, 1) == static_cast<int>(gridDim.x) - 1) {
+          atomicExch(ctr, 0);
+          atomicExch(ctr + 1, 0);
+        }
+      }
     }
   } else if (warp == 1) {
     // ------------------------------- MMA issuer -------------------------------
     if (lane == 0) {
-      int it = 0, local = 0;
-      for (int unit = blockIdx.x; unit < units && !s_abort; unit += gridDim.x, ++local) {
+      int it = 0;
+      for (int local = 0; !s_abort; ++local) {
+        const int slot = local % UNIT_RING;
+        if (!mbar_wait(&ufull_bar[slot], (local / UNIT_RING) & 1, shape.err)) { s_abort = 1; break; }
+        const int unit = unit_ring[slot];
+        mbar_arrive(&uempty_bar[slot]);
+        if (unit < 0) break;
         int mt, nt, split;
         unit_coords(unit, shape, num_m, num_n, mt, nt, split);
         const int k_begin = split * k_chunk;
@@ -459,12 +501,27 @@ __global__ void __launch_bounds__(gemm_threads<Epi>(), 1)
   } else {
     // -------------------------------- epilogue --------------------------------
     const int sub = warp & 3;  // TMEM sub-partition this warp may access
-    const int part = (warp - 2) >> 2;    int local = 0;
-    for (int unit = blockIdx.x; unit < units && !s_abort; unit += gridDim.x, ++local) {
+    const int part = (warp - 2) >> 2;
+    // every decision below is warp-uniform: the epilogue's TMEM loads are
+    // warp-collective
+    for (int local = 0;; ++local) {
+      if (__shfl_sync(0xffffffffu, static_cast<int>(s_abort), 0)) break;
+      const int slot = local % UNIT_RING;
+      if (!__all_sync(0xffffffffu, mbar_wait(&ufull_bar[slot], (local / UNIT_RING) & 1, shape.err))) {
+        s_abort = 1;
+        break;
+      }
+      const int unit = __shfl_sync(0xffffffffu, unit_ring[slot], 0);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&uempty_bar[slot]);
+      if (unit < 0) break;
       int mt, nt, split;
       unit_coords(unit, shape, num_m, num_n, mt, nt, split);
       const int buf = local & 1;
-      if (!mbar_wait(&tfull_bar[buf], (local >> 1) & 1, shape.err)) { s_abort = 1; break; }
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull_bar[buf], (local >> 1) & 1, shape.err))) {
+        s_abort = 1;
+        break;
+      }
       tc_fence_after();
       EpiCtx<BN> ctx;
       ctx.tmem_row = tmem_base + (static_cast<uint32_t>(sub * 32) << 16) +

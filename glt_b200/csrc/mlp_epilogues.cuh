@@ -506,6 +506,8 @@ struct EpiSwiGLUFwdOv {
   const float* du;  // up delta or null
   int64_t ld_inj;
   int i0, i1;
+  uint16_t* gu = nullptr;  // stored gate_pre/up after the injection (gu_block_offset layout) or null
+  int64_t gu_groups = 0;   // 2F' / 8
   __device__ __forceinline__ void operator()(const tc::EpiCtx<256>& c) const {
     const int cb = c.n0 >> 1;
 #pragma unroll 1
@@ -531,6 +533,14 @@ struct EpiSwiGLUFwdOv {
 #pragma unroll
             for (int k = 0; k < 8; ++k) u[i + k] += d[k];
           }
+        }
+        if (gu) {
+          const int g8 = ((c.n0 + j) >> 3) + i / 8;
+          float gg[8], uu[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) { gg[k] = g[i + k]; uu[k] = u[i + k]; }
+          __stcs(reinterpret_cast<uint4*>(gu + gu_block_offset(c.row, g8, gu_groups)), pack8(gg));
+          __stcs(reinterpret_cast<uint4*>(gu + gu_block_offset(c.row, g8 + 16, gu_groups)), pack8(uu));
         }
         float o[8];
 #pragma unroll
@@ -630,6 +640,127 @@ struct EpiSwiGLUBwdOv {
           if (hg) *reinterpret_cast<uint4*>(hg + static_cast<int64_t>(c.row) * ldhg + s) = pack8(hh);
         }
       }
+    }
+  }
+};
+
+// Overlay geometry without the recompute: dh = dy . W_d with, in the
+// epilogue, the ContractInputGrad slice gi (fp32 [M, S], intermediate columns
+// [i0, i1)) added, SwiGLU's backward from the stored bf16 gate_pre/up (base +
+// delta on the slice, EpiSwiGLUFwdOv::gu), dgu staged through shared memory,
+// and on the slice the silence-blended expand grads dys and h for the down
+// weight grad -- the outputs of EpiSwiGLUBwdOv, whose recompute GEMM this
+// replaces.  The expand deltas (dg, du) feed only the silence term.
+template <int BN>
+struct EpiSwiGLUBwdStoredOv {
+  const uint16_t* gu;
+  int64_t gu_groups;   // 2F' / 8
+  uint16_t* dgu;
+  int64_t ldgu_out;
+  const float* gi;     // [M, ld_gi] or null (down not grafted)
+  int64_t ld_gi;
+  const float* dg;     // [M, ld_inj] expand deltas or null
+  const float* du;
+  int64_t ld_inj;
+  uint16_t* dys;       // [M, lddys] or null
+  int64_t lddys;
+  uint16_t* hg;        // [M, ldhg] or null
+  int64_t ldhg;
+  int M, N, i0, i1, S;
+  const float* esq_gate;
+  const float* esq_up;
+  const int32_t* ood;
+  const DevStats* stats;
+  static constexpr int kParts = 2;
+  static constexpr int kScratchPerWarp = 4096;
+
+  __device__ __forceinline__ static int64_t pos(int col0) {
+    return 2 * static_cast<int64_t>(col0 & ~127) + (col0 & 127);
+  }
+  __device__ __forceinline__ void fetch(int row, int col0, uint4 (&g)[4], uint4 (&u)[4]) const {
+    const int g8 = static_cast<int>(pos(col0) >> 3);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      g[q] = __ldcs(reinterpret_cast<const uint4*>(gu + gu_block_offset(row, g8 + q, gu_groups)));
+      u[q] = __ldcs(reinterpret_cast<const uint4*>(gu + gu_block_offset(row, g8 + 16 + q, gu_groups)));
+    }
+  }
+
+  __device__ __forceinline__ void operator()(const tc::EpiCtx<BN>& c) const {
+    const bool slice = (c.n0 + BN > i0) && (c.n0 < i1);
+    const bool row_ok = c.row < M;
+    float sg_s = 0.f, su_s = 0.f;
+    if (slice && row_ok && ood[c.row]) {
+      const float lam = stats->lambda_eff;
+      const float rs = sqrtf(static_cast<float>(S));
+      if (dg) sg_s = lam / (sqrtf(esq_gate[c.row] + 1e-8f) * rs + 1e-8f);
+      if (du) su_s = lam / (sqrtf(esq_up[c.row] + 1e-8f) * rs + 1e-8f);
+    }
+    const int j0 = c.part * (BN / kParts), j1 = j0 + BN / kParts;
+    const int band0 = c.row & ~31;
+    uint4 ng[4] = {}, nu[4] = {};
+    if (row_ok && c.n0 + j0 < N) fetch(c.row, c.n0 + j0, ng, nu);
+#pragma unroll 1
+    for (int j = j0; j < j1; j += 32) {
+      float d[32];
+      c.load(j, d);   // warp-collective: every lane loads
+      const int col0 = c.n0 + j;
+      if (col0 >= N) continue;   // the same for the whole warp
+      uint4 gv[4], uv[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) { gv[q] = ng[q]; uv[q] = nu[q]; }
+      if (row_ok && j + 32 < j1 && col0 + 32 < N) fetch(c.row, col0 + 32, ng, nu);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int i = 8 * q;
+        const int col = col0 + i;
+        const bool in = row_ok && col >= i0 && col < i1;   // i0, S multiples of 8
+        float g[8], u[8], dd[8];
+        unpack8(gv[q], g);
+        unpack8(uv[q], u);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) dd[k] = d[i + k];
+        const int64_t off_s = col - i0;
+        if (in && gi) {
+          float t[8];
+          load8f(gi + static_cast<int64_t>(c.row) * ld_gi + off_s, t);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) dd[k] += t[k];
+        }
+        float og[8], ou[8], hh[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float sg = sigmoidf_(g[k]);
+          og[k] = dd[k] * u[k] * sg * (1.f + g[k] * (1.f - sg));
+          ou[k] = dd[k] * g[k] * sg;
+          hh[k] = g[k] * sg * u[k];
+        }
+        stage_put(c.scratch, 0, q, pack8(og));
+        stage_put(c.scratch, 1, q, pack8(ou));
+        if (in) {
+          if (dys) {
+            const int64_t off = static_cast<int64_t>(c.row) * ld_inj + off_s;
+            float de[8], b[8];
+            uint16_t* dr = dys + static_cast<int64_t>(c.row) * lddys + off_s;
+            if (dg) {
+              load8f(dg + off, de);
+#pragma unroll
+              for (int k = 0; k < 8; ++k) b[k] = og[k] + sg_s * de[k];
+              *reinterpret_cast<uint4*>(dr) = pack8(b);
+            }
+            if (du) {
+              load8f(du + off, de);
+#pragma unroll
+              for (int k = 0; k < 8; ++k) b[k] = ou[k] + su_s * de[k];
+              *reinterpret_cast<uint4*>(dr + S) = pack8(b);
+            }
+          }
+          if (hg) *reinterpret_cast<uint4*>(hg + static_cast<int64_t>(c.row) * ldhg + off_s) = pack8(hh);
+        }
+      }
+      uint16_t* const g_dst = dgu + static_cast<int64_t>(band0) * ldgu_out + pos(col0);
+      uint16_t* const dsts[2] = {g_dst, g_dst + 128};
+      stage_flush<2>(c.scratch, dsts, ldgu_out, M - band0);
     }
   }
 };

@@ -299,10 +299,6 @@ void Model::free_mlp_store() {
 
 int Model::alloc_mlp_store(bool required) {
   if (gu_mem) return GLT_OK;
-  if (overlay) {
-    if (required) return fail(GLT_EINVAL, "stored MLP activations need the concat geometry");
-    return GLT_OK;
-  }
   // gu_block_offset layout: 32-row bands
   const size_t per = static_cast<size_t>(rup(rup(M, 32) * 2 * FF * 2, 256));
   const size_t bytes = per * L;

@@ -65,7 +65,7 @@ int Model::ffn_forward_overlay(int l, const uint16_t* x_in, uint16_t* x_out, flo
   if (g || u) GLT_PROF(GLT_PROF_DELTA_EXPAND, expand_deltas(l, g, u, y.esq, y.esq + M, st));
   {
     EpiSwiGLUFwdOv e{h, FF, M, g ? dlt : nullptr, u ? dlt + S : nullptr, 2 * static_cast<int64_t>(S),
-                     i0, i0 + S};
+                     i0, i0 + S, saving ? y.gu : nullptr, 2 * static_cast<int64_t>(FF) / 8};
     GLT_PROF(GLT_PROF_GATE_UP_FWD,
              (launch_gemm<256, 4, false, false>(kmaj(y.x_ffn, D), kmaj(y.w_gu, D), M, 2 * FF, D, e, st)));
   }
@@ -95,6 +95,33 @@ int Model::ffn_backward_overlay(int l, cudaStream_t st) {
   // dy = bf16(dx);  dyh = bf16(dx[:, h0:h0+H] + silence_down)  [M, H]
   GLT_TRY(silence_down_prep(dx, d ? y.dd : nullptr, H, y.esq + 2 * static_cast<int64_t>(M), ood,
                             stats, dy_b, dyg_b, H, M, D, h0, H, st));
+  if (y.gu) {
+    // gate_pre/up (with the deltas) were stored by the forward: no recompute.
+    // ContractInputGrad (layer_backward_impl.inc:311-342): gi_slice =
+    // dyh . Delta_down^T -> dtmp [M, S] (free until the dx GEMM below); the
+    // expand deltas -> dlt for the silence term; then dh = dy . W_d with
+    // SwiGLU's backward in its epilogue.
+    float* gi = d ? dtmp : nullptr;
+    if (d) {
+      EpiF32<128> e1{gi, S, M, S, 1.f, 0.f, 0, 1};
+      EpiF32<256> e2{gi, S, M, S, 1.f, 0.f, 0, 1};
+      GLT_PROF(GLT_PROF_GRAFT_DGRAD, (launch_by_n<EpiF32<128>, EpiF32<256>, false, false>(
+                                kmaj(dyg_b, H), kmaj(gwb + (3 * l + 2) * SH, H), M, S, H, e1, e2, st)));
+    }
+    if (g || u) GLT_PROF(GLT_PROF_DELTA_EXPAND, expand_deltas(l, g, u, nullptr, nullptr, st));
+    const int64_t ld2 = 2 * static_cast<int64_t>(FF);
+    if (FF >= 1024) {
+      EpiSwiGLUBwdStoredOv<256> e{y.gu, ld2 / 8, dgu, ld2, gi, S, g ? dlt : nullptr, u ? dlt + S : nullptr, S2,
+                                  (g || u) ? dys : nullptr, S2, d ? hg : nullptr, S_pad, M, FF, i0, i0 + S, S,
+                                  y.esq, y.esq + M, ood, stats};
+      GLT_PROF(GLT_PROF_DH, (launch_gemm<256, 4, false, true>(kmaj(dy_b, D), mnmaj(y.w_d, FF), M, FF, D, e, st)));
+    } else {
+      EpiSwiGLUBwdStoredOv<128> e{y.gu, ld2 / 8, dgu, ld2, gi, S, g ? dlt : nullptr, u ? dlt + S : nullptr, S2,
+                                  (g || u) ? dys : nullptr, S2, d ? hg : nullptr, S_pad, M, FF, i0, i0 + S, S,
+                                  y.esq, y.esq + M, ood, stats};
+      GLT_PROF(GLT_PROF_DH, (launch_gemm<128, 6, false, true>(kmaj(dy_b, D), mnmaj(y.w_d, FF), M, FF, D, e, st)));
+    }
+  } else {
   // ContractInputGrad (layer_backward_impl.inc:311-342): gi_slice = dyh . Delta_down^T -> dlt [M, S]
   if (d) {
     EpiF32<128> e1{dlt, S, M, S, 1.f, 0.f, 0, 1};
@@ -117,6 +144,7 @@ int Model::ffn_backward_overlay(int l, cudaStream_t st) {
                      S_pad, M, i0, i0 + S, S, y.esq, y.esq + M, ood, stats};
     GLT_PROF(GLT_PROF_RECOMPUTE,
              (launch_gemm<256, 4, false, false>(kmaj(y.x_ffn, D), kmaj(y.w_gu, D), M, 2 * FF, D, e, st)));
+  }
   }
   // ContractWeightGrad (graft_ops_impl.inc:214-228): dDelta_down = h_sliceᵀ . dyh
   // ExpandWeightGrad (graft_ops_impl.inc:120-156): dDelta_{gate,up} = dysᵀ . x_h

@@ -317,8 +317,8 @@ GLT_API int glt_model_memory(const GltModel* m, int64_t* arena_bytes, int64_t* g
  * recompute (the reference's memory profile); 1: store, allocated now
  * (GLT_ENOMEM when it does not fit); 2: auto, the default -- decided at the
  * next training step, store when free device memory exceeds the store plus
- * max(8 GiB, 1/16 of the device); -1: query only.  Concat geometry only
- * (overlay recomputes; mode 1 on overlay is GLT_EINVAL).  GLT_MLP_STORE=0|1|2
+ * max(8 GiB, 1/16 of the device); -1: query only.  Both geometries (overlay
+ * stores the pre-activations after the delta injection).  GLT_MLP_STORE=0|1|2
  * in the environment sets the mode at glt_model_create.  *active (nullable)
  * = 1 while the store is allocated, *bytes (nullable) = its size.
  * Synchronizes the device. */

@@ -1,9 +1,10 @@
 """Stored MLP activations (glt_model_mlp_store): the training forward keeps
 bf16 gate_pre/up and the backward fuses SwiGLU's backward into the dh GEMM,
 against the recompute path (the reference's recompute_ffn,
-src/layer_recompute_impl.inc:8-91) and the fp32 oracle.  Both backward
-epilogue widths run: F' = 896 (128-column tiles) and F' = 1152 (256-column
-tiles, the last one half full)."""
+src/layer_recompute_impl.inc:8-91) and the fp32 oracle, in both
+geometries.  Both backward epilogue widths run: concat F' = 896
+(128-column tiles) and F' = 1152 (256-column tiles, the last one half
+full); overlay F' = 768 and 1024 with slices off the 32-column grid."""
 import pytest
 import torch
 
@@ -45,7 +46,8 @@ def gpu_model(rc, w, delta, B, T, mode):
 def store_bytes(rc, B, T):
     F_pad = -(-rc.intermediate_dim // 256) * 256
     S_pad = -(-rc.slice_dim // 128) * 128
-    per = B * T * 2 * (F_pad + S_pad) * 2
+    FF = F_pad if rc.layout == "overlay" else F_pad + S_pad
+    per = B * T * 2 * FF * 2
     return rc.num_layers * (-(-per // 256) * 256)
 
 
@@ -67,17 +69,42 @@ def test_store_modes():
     m.close()
 
 
-def test_overlay_recomputes():
-    from glt_b200._lib import GltError
-    rc = cfg(layout="overlay", max_domains=4, domain_id=1, slice_dim=160)
-    B, T = 2, 128
+@pytest.mark.parametrize("inter,S,dom,projs", [
+    (640, 40, 1, (1, 1, 1)),     # slice [40, 80): not on the 32-column chunk grid; 128-wide dh tiles
+    (640, 40, 1, (0, 0, 1)),
+    (640, 160, 1, (1, 0, 1)),
+    (1024, 16, 3, (1, 1, 1)),    # slice [48, 64), 256-wide dh tiles
+])
+def test_overlay_store_matches_recompute_and_oracle(inter, S, dom, projs):
+    """The reference's own geometry: the forward stores gate_pre/up after the
+    delta injection, the dh GEMM's epilogue adds the ContractInputGrad slice
+    and writes the silence-blended expand grads and the h slice."""
+    rc = cfg(layout="overlay", max_domains=4, domain_id=dom, intermediate_dim=inter, slice_dim=S,
+             graft_proj_gate=projs[0], graft_proj_up=projs[1], graft_proj_down=projs[2])
+    B, T = 4, 128
     w, delta, ids, ood = problem(rc, B, T)
-    m = gpu_model(rc, w, delta, B, T, AUTO)
-    m.train_step(ids, ood, 0, 4)
-    assert m.mlp_store(QUERY) == (False, 0)
-    with pytest.raises(GltError):
-        m.mlp_store(STORE)
-    m.close()
+    runs = {}
+    for mode in (RECOMPUTE, AUTO):
+        m = gpu_model(rc, w, delta, B, T, mode)
+        st = m.train_step(ids, ood, step=0, total_steps=10)
+        assert m.mlp_store(QUERY) == ((True, store_bytes(rc, B, T)) if mode == AUTO else (False, 0))
+        runs[mode] = (st, m.read_graft("grad").cpu())
+        m.close()
+    (s0, g0), (s1, g1) = runs[RECOMPUTE], runs[AUTO]
+    for k in ("lm_loss", "silence_loss", "domain_graft_energy", "ood_graft_energy"):
+        assert s1[k] == pytest.approx(s0[k], rel=1e-5, abs=1e-9), k
+    grad_ref, stats, _ = rm.compute_grads(ids, ood, w, delta.clone(), rc)
+    assert s1["total_loss"] == pytest.approx(stats["total_loss"], rel=1e-2)
+    SH = rc.slice_dim * rc.h_slice_dim
+    for l in range(rc.num_layers):
+        for p, name in enumerate(("gate", "up", "down")):
+            sl = slice((3 * l + p) * SH, (3 * l + p + 1) * SH)
+            if not rc.should_graft_proj(l, p):
+                assert float(g1[sl].abs().max()) == 0.0
+                continue
+            assert_close_bf16(g1[sl], grad_ref[sl], f"stored overlay: grad L{l} {name}")
+            assert_close_bf16(g1[sl], g0[sl], f"stored vs recompute overlay: grad L{l} {name}")
+    assert s1["grad_norm"] == pytest.approx(s0["grad_norm"], rel=1e-2)
 
 
 @pytest.mark.parametrize("inter", [640, 1024])

@@ -575,6 +575,90 @@ extern "C" int glt_model_load_train_state(GltModel* m, const char* path, const c
   return GLT_OK;
 }
 
+// --------------------------- sibling-graft stacks ---------------------------
+// The model's graft [3L, S, H] holds N siblings of S / N rows each: concat
+// geometry side by side over the full hidden width, the overlay stack
+// geometry (max_domains 1) block-diagonal with H / N columns each.
+namespace {
+struct StackGeom {
+  int n, S_sib, H_sib;
+  bool diag;
+};
+
+int stack_geom(const glt::Model* mm, int n, StackGeom* g) {
+  if (n < 1) return glt::fail(GLT_EINVAL, "stack needs at least one sibling");
+  if (mm->S % n) return glt::fail(GLT_EINVAL, "slice_dim %d is not a multiple of %d siblings", mm->S, n);
+  g->n = n;
+  g->S_sib = mm->S / n;
+  g->diag = mm->overlay;
+  if (mm->overlay) {
+    if (mm->cfg.max_domains != 1 || mm->cfg.domain_id != 0)
+      return glt::fail(GLT_EINVAL, "an overlay stack uses max_domains = 1, domain_id = 0");
+    if (mm->H % n) return glt::fail(GLT_EINVAL, "hidden slice %d is not a multiple of %d siblings", mm->H, n);
+    g->H_sib = mm->H / n;
+  } else {
+    g->H_sib = mm->H;
+  }
+  return GLT_OK;
+}
+
+// Copies sibling d between the stacked graft `all` [3L, S, H] and `sib`
+// [3L, S_sib, H_sib] (to_sib: extract; else place).
+void stack_copy(const StackGeom& g, int L, int S, int H, int d, float* all, float* sib, bool to_sib) {
+  const int c0 = g.diag ? d * g.H_sib : 0;
+  for (int64_t p = 0; p < 3LL * L; ++p)
+    for (int s = 0; s < g.S_sib; ++s) {
+      float* a = all + (p * S + static_cast<int64_t>(d) * g.S_sib + s) * H + c0;
+      float* b = sib + (p * g.S_sib + s) * g.H_sib;
+      if (to_sib) memcpy(b, a, sizeof(float) * g.H_sib);
+      else memcpy(a, b, sizeof(float) * g.H_sib);
+    }
+}
+}  // namespace
+
+extern "C" int glt_model_save_stack(GltModel* m, const char* const* paths, int n, const char* session_id) {
+  if (!m || !paths) return glt::fail(GLT_EINVAL, "null argument");
+  glt::Model* mm = reinterpret_cast<glt::Model*>(m);
+  if (!mm->gw) return glt::fail(GLT_ESTATE, "graft storage was freed by the shadow bake");
+  StackGeom g;
+  GLT_TRY(stack_geom(mm, n, &g));
+  for (int d = 0; d < n; ++d)
+    if (!paths[d]) return glt::fail(GLT_EINVAL, "null path for sibling %d", d);
+  GLT_CUDA_TRY(cudaDeviceSynchronize());
+  std::vector<float> all(static_cast<size_t>(mm->graft_numel));
+  GLT_TRY(copy_weights(all.data(), mm->gw, mm->graft_numel * 4, 1, 0));
+  const int64_t n_sib = 3LL * mm->L * g.S_sib * g.H_sib;
+  std::vector<float> sib(static_cast<size_t>(n_sib));
+  for (int d = 0; d < n; ++d) {
+    stack_copy(g, mm->L, mm->S, mm->H, d, all.data(), sib.data(), true);
+    GLT_TRY(glt::checkpoint_save(paths[d], sib.data(), n_sib, session_id, d, g.S_sib, g.H_sib, mm->D, mm->L));
+  }
+  return GLT_OK;
+}
+
+extern "C" int glt_model_load_stack(GltModel* m, const char* const* paths, int n, const char* session_id) {
+  if (!m || !paths) return glt::fail(GLT_EINVAL, "null argument");
+  glt::Model* mm = reinterpret_cast<glt::Model*>(m);
+  if (!mm->gw) return glt::fail(GLT_ESTATE, "graft storage was freed by the shadow bake");
+  if (mm->shadow_baked) return glt::fail(GLT_ESTATE, "the model is shadow-baked");
+  StackGeom g;
+  GLT_TRY(stack_geom(mm, n, &g));
+  const int64_t n_sib = 3LL * mm->L * g.S_sib * g.H_sib;
+  std::vector<float> all(static_cast<size_t>(mm->graft_numel), 0.f), sib(static_cast<size_t>(n_sib));
+  for (int d = 0; d < n; ++d) {
+    if (!paths[d]) return glt::fail(GLT_EINVAL, "null path for sibling %d", d);
+    // every file is read and checked before the model's graft changes
+    GLT_TRY(glt::checkpoint_load(paths[d], sib.data(), n_sib, d, session_id, 3 * mm->L, g.S_sib, g.H_sib,
+                                 nullptr));
+    stack_copy(g, mm->L, mm->S, mm->H, d, all.data(), sib.data(), false);
+  }
+  GLT_CUDA_TRY(cudaDeviceSynchronize());
+  GLT_TRY(copy_weights(mm->gw, all.data(), mm->graft_numel * 4, 0, 1));
+  GLT_TRY(mm->refresh_graft(nullptr));
+  GLT_CUDA_TRY(cudaDeviceSynchronize());
+  return GLT_OK;
+}
+
 // ---------------------------- .bin + batch walk ----------------------------
 extern "C" int glt_load_bin(const char* path, int32_t* num_sequences, int32_t* seq_len,
                             int32_t* tokens, int64_t capacity) {

@@ -507,6 +507,20 @@ GLT_API int glt_train_state_load(const char* path, float* weights, float* adam_m
                                  int64_t numel, int dst_is_host, const char* session_id,
                                  int expected_domain_id, int total_projections, int slice_dim,
                                  int h_slice_dim, int64_t* step);
+/* Sibling grafts of a stack, one GRFT file each (the reference trains and
+ * ships one graft per domain; test6_stack_vs_bake_f32.cpp runs N of them at
+ * once).  The model's graft holds the N siblings, slice_dim = N * S_sib:
+ * concat geometry side by side over the full hidden width (sibling d on
+ * graft rows [d*S_sib, (d+1)*S_sib) -- N slices trained jointly), or the
+ * overlay stack geometry of glt_stack_grafts (max_domains = 1, domain_id 0;
+ * block-diagonal, sibling d also on hidden columns [d*H_sib, (d+1)*H_sib),
+ * H_sib = H / N).  save writes sibling d to paths[d] as GRFT v4 with
+ * domain_id d and its own [3L, S_sib, H_sib] shape; load checks and reads
+ * all N files (domain_id d each, session_id when both are set), then sets the
+ * graft to their assembly (zeros elsewhere) and refreshes its bf16 copies;
+ * the Adam state is untouched. */
+GLT_API int glt_model_save_stack(GltModel* m, const char* const* paths, int n, const char* session_id);
+GLT_API int glt_model_load_stack(GltModel* m, const char* const* paths, int n, const char* session_id);
 /* Model-level: its fp32 graft and Adam state; load also refreshes the bf16
  * graft copies in the fused weights.  `step` is the index of the next
  * training step (glt_train_step's step argument). */

@@ -11,6 +11,8 @@ Concat geometry: N slices side by side in [base | s_0 | ... | s_{N-1}]; the
 bake turns the columns into base columns, so the logits are bit-identical."""
 import ctypes as C
 
+import numpy as np
+
 import pytest
 import torch
 
@@ -105,3 +107,61 @@ def test_concat_stack_bakes_to_identical_logits():
     assert torch.equal(stack, baked)
     ref, _, _, _ = rm.model_forward(ids, w, graft, rc)
     assert_close_bf16(stack.float().cpu(), ref.reshape(-1, rc.vocab_size), "concat stack vs oracle")
+
+
+# ---------------------------------------------------------------------------
+# One GRFT file per sibling (glt_model_save_stack / glt_model_load_stack)
+# ---------------------------------------------------------------------------
+def stack_model(geometry, S_sib=32):
+    from oracle import bitexact as bx  # noqa: F401  (parser used by the caller)
+    if geometry == "overlay":   # the stack geometry of glt_stack_grafts
+        rc = stack_cfg(slice_dim=N * S_sib, max_domains=1, domain_id=0)
+    else:
+        rc = stack_cfg(slice_dim=N * S_sib, layout="concat", max_domains=4)
+    w = make_decoder_weights(rc, 5, 0.02)
+    m = G.GraftModel(to_glt_config(rc), 2, 128, kind=G.MODEL_DECODER)
+    load_weights(m, w)
+    return rc, m
+
+
+def path_array(paths):
+    return (C.c_char_p * len(paths))(*[str(p).encode() for p in paths])
+
+
+@pytest.mark.parametrize("geometry", ["concat", "overlay"])
+def test_stack_files_roundtrip(tmp_path, geometry):
+    from oracle import bitexact as bx
+    rc, a = stack_model(geometry)
+    L, S, H, S_sib = rc.num_layers, rc.slice_dim, rc.h_slice_dim, rc.slice_dim // N
+    H_sib = H // N if geometry == "overlay" else H
+    g = torch.randn(3 * L * S * H, generator=torch.Generator().manual_seed(3)) * 0.05
+    a.write_graft("weight", g)
+    paths = [tmp_path / f"sib{d}.graft" for d in range(N)]
+    _lib.check(lib.glt_model_save_stack(a.handle, path_array(paths), N, b"sess"))
+    full = g.view(3 * L, S, H).numpy()
+    want = np.zeros_like(full)
+    for d in range(N):
+        c0 = d * H_sib if geometry == "overlay" else 0
+        blk = full[:, d * S_sib:(d + 1) * S_sib, c0:c0 + H_sib]
+        got = bx.parse_grft(open(paths[d], "rb").read(), d, "sess", 3 * L, S_sib, H_sib)
+        np.testing.assert_array_equal(np.asarray(got).reshape(blk.shape), bx.round_bf16(blk))
+        want[:, d * S_sib:(d + 1) * S_sib, c0:c0 + H_sib] = bx.round_bf16(blk)
+    a.close()
+    _, b = stack_model(geometry)
+    _lib.check(lib.glt_model_load_stack(b.handle, path_array(paths), N, b"sess"))
+    np.testing.assert_array_equal(b.read_graft("weight").cpu().numpy().reshape(want.shape), want)
+    # refusals leave the graft as it was: siblings out of order (domain ids),
+    # a sibling count that does not divide the slice, another session
+    before = b.read_graft("weight").cpu()
+    for args in ((path_array(paths[::-1]), N, b"sess"), (path_array(paths[:3]), 3, b"sess"),
+                 (path_array(paths), N, b"other")):
+        with pytest.raises(_lib.GltError):
+            _lib.check(lib.glt_model_load_stack(b.handle, *args))
+    assert torch.equal(b.read_graft("weight").cpu(), before)
+    # the stacked graft is live: the loaded model's forward matches a model given the same values
+    c = stack_model(geometry)[1]
+    c.write_graft("weight", torch.from_numpy(want).reshape(-1))
+    ids = torch.randint(0, rc.vocab_size, (2, 128), generator=torch.Generator().manual_seed(1), dtype=torch.int32)
+    assert torch.equal(b.forward(ids.cuda()), c.forward(ids.cuda()))
+    b.close()
+    c.close()

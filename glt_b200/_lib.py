@@ -97,6 +97,7 @@ SIGNATURES: dict[str, tuple] = {
     "glt_model_load_train_state": (_i32, [_vp, C.c_char_p, C.c_char_p, _i32, C.POINTER(_i64)]),
     "glt_model_save_stack": (_i32, [_vp, C.POINTER(C.c_char_p), _i32, C.c_char_p]),
     "glt_model_load_stack": (_i32, [_vp, C.POINTER(C.c_char_p), _i32, C.c_char_p]),
+    "glt_model_step_stats": (_i32, [_vp, _i32, C.c_void_p]),
     "glt_model_memory": (_i32, [_vp, C.POINTER(_i64), C.POINTER(_i64)]),
     "glt_model_mlp_store": (_i32, [_vp, _i32, C.POINTER(_i32), C.POINTER(_i64)]),
     "glt_model_init_random": (_i32, [_vp, _u64, _f32, _f32, _f32]),

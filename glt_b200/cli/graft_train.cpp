@@ -588,13 +588,8 @@ int run(int argc, char** argv) {
   for (int s = 0; s < start_step; ++s)  // the data walk of the steps already taken
     CHECK(glt_batch_step(domain.tokens.data(), domain.num_sequences, ood.tokens.data(), ood.num_sequences, T,
                          batch_size, &dpos, &opos, ids.data(), mask.data()));
-  for (int step = start_step; step < end_step; ++step) {
-    CHECK(glt_batch_step(domain.tokens.data(), domain.num_sequences, ood.tokens.data(), ood.num_sequences, T,
-                         batch_size, &dpos, &opos, ids.data(), mask.data()));
-    GltStepStats st;
-    const auto t0 = std::chrono::steady_clock::now();
-    CHECK(glt_train_step(m, ids.data(), mask.data(), 1, step, steps, &st, nullptr));
-    const double sec = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+  // Logs one finished step (CSV line, parity dump at step 0, console line).
+  auto log_step = [&](int step, const GltStepStats& st, double sec) {
     peak_mb = std::max(peak_mb, used_mb());
     if (step > start_step) steady.push_back(sec);
     // The reference logs the previous step's clip coefficient read back
@@ -630,6 +625,38 @@ int run(int argc, char** argv) {
     if (step % 50 == 0)
       std::cout << "  Step " << step << "/" << steps << " | lm=" << st.lm_loss << " | silence=" << st.silence_loss
                 << " | total=" << st.total_loss << " | lr=" << st.lr << " | grad_norm=" << grad_norm << "\n";
+  };
+  // Steps are enqueued one ahead of the logging: the device runs step k+1
+  // while the host reads and logs step k (glt_model_step_stats), so no host
+  // sync stalls the device between steps; a step's time is the interval
+  // between consecutive step completions.  The parity dump reads step 0's
+  // gradients before step 1 may run, so with it every step is synchronous.
+  const bool pipelined = parity_dump_dir.empty();
+  auto t_prev = std::chrono::steady_clock::now();
+  for (int step = start_step; step < end_step; ++step) {
+    CHECK(glt_batch_step(domain.tokens.data(), domain.num_sequences, ood.tokens.data(), ood.num_sequences, T,
+                         batch_size, &dpos, &opos, ids.data(), mask.data()));
+    GltStepStats st;
+    if (pipelined) {
+      CHECK(glt_train_step(m, ids.data(), mask.data(), 1, step, steps, nullptr, nullptr));
+      if (step > start_step) {
+        CHECK(glt_model_step_stats(m, step - 1, &st));
+        const auto now = std::chrono::steady_clock::now();
+        const double sec = std::chrono::duration<double>(now - t_prev).count();
+        t_prev = now;
+        log_step(step - 1, st, sec);
+      }
+    } else {
+      const auto t0 = std::chrono::steady_clock::now();
+      CHECK(glt_train_step(m, ids.data(), mask.data(), 1, step, steps, &st, nullptr));
+      log_step(step, st, std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count());
+    }
+  }
+  if (pipelined) {
+    GltStepStats st;
+    CHECK(glt_model_step_stats(m, end_step - 1, &st));
+    const double sec = std::chrono::duration<double>(std::chrono::steady_clock::now() - t_prev).count();
+    log_step(end_step - 1, st, sec);
   }
   double p50 = 0.0;
   if (!steady.empty()) {

@@ -212,6 +212,8 @@ Model::~Model() {
   if (graft_mem) cudaFree(graft_mem);
   if (gu_mem) cudaFree(gu_mem);
   if (pinned_stats) cudaFreeHost(pinned_stats);
+  for (auto e : stats_ev)
+    if (e) cudaEventDestroy(e);
   if (eval_mem) cudaFree(eval_mem);
   if (ev_pinned) cudaFreeHost(ev_pinned);
 }
@@ -462,7 +464,8 @@ int Model::allocate() {
     GLT_CUDA_TRY(cudaMemcpy(cos_t, c.data(), c.size() * 4, cudaMemcpyHostToDevice));
     GLT_CUDA_TRY(cudaMemcpy(sin_t, s.data(), s.size() * 4, cudaMemcpyHostToDevice));
   }
-  GLT_CUDA_TRY(cudaMallocHost(&pinned_stats, sizeof(DevStats)));
+  GLT_CUDA_TRY(cudaMallocHost(&pinned_stats, 2 * sizeof(DevStats)));
+  for (auto& e : stats_ev) GLT_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
   GLT_CUDA_TRY(cudaStreamCreateWithFlags(&comm_stream, cudaStreamNonBlocking));
   layer_done.resize(L);
   for (int l = 0; l < L; ++l) GLT_CUDA_TRY(cudaEventCreateWithFlags(&layer_done[l], cudaEventDisableTiming));
@@ -858,19 +861,30 @@ int Model::finish_step(int step, int total_steps, GltStepStats* out, cudaStream_
   MirrorTargets mt = mirror();
   GLT_PROF(GLT_PROF_ADAMW, adamw_step(gw, grad, adam_m, adam_v, L, S, H, lr, cfg.adam_beta1, cfg.adam_beta2,
                      cfg.adam_eps, cfg.adam_weight_decay, step, kinds, stats, &mt, st));
-  if (out) {
-    GLT_CUDA_TRY(cudaMemcpyAsync(pinned_stats, stats, sizeof(DevStats), cudaMemcpyDeviceToHost, st));
-    GLT_CUDA_TRY(cudaStreamSynchronize(st));
-    const DevStats& s = *pinned_stats;
-    out->lm_loss = s.lm_loss;
-    out->silence_loss = s.silence;
-    out->domain_graft_energy = s.domain_energy;
-    out->ood_graft_energy = s.ood_energy;
-    out->domain_ood_energy_ratio = s.ratio;
-    out->total_loss = s.total_loss;
-    out->lr = lr;
-    out->grad_norm = s.grad_norm;
-  }
+  // The step's stats go to a pinned slot without a host sync; the next step
+  // overwrites the device copy, two steps later the slot is reused.
+  const int slot = step & 1;
+  GLT_CUDA_TRY(cudaMemcpyAsync(pinned_stats + slot, stats, sizeof(DevStats), cudaMemcpyDeviceToHost, st));
+  GLT_CUDA_TRY(cudaEventRecord(stats_ev[slot], st));
+  stats_step[slot] = step;
+  stats_lr[slot] = lr;
+  return out ? step_stats(step, out) : GLT_OK;
+}
+
+int Model::step_stats(int step, GltStepStats* out) {
+  const int slot = step & 1;
+  if (step < 0 || stats_step[slot] != step)
+    return fail(GLT_EINVAL, "the stats of step %d are not kept (the last two training steps are)", step);
+  GLT_CUDA_TRY(cudaEventSynchronize(stats_ev[slot]));
+  const DevStats& s = pinned_stats[slot];
+  out->lm_loss = s.lm_loss;
+  out->silence_loss = s.silence;
+  out->domain_graft_energy = s.domain_energy;
+  out->ood_graft_energy = s.ood_energy;
+  out->domain_ood_energy_ratio = s.ratio;
+  out->total_loss = s.total_loss;
+  out->lr = stats_lr[slot];
+  out->grad_norm = s.grad_norm;
   return GLT_OK;
 }
 
@@ -1034,6 +1048,11 @@ extern "C" int glt_train_step(GltModel* m, const int32_t* ids, const int32_t* oo
   if (!m || !ids || !ood_mask) return glt::fail(GLT_EINVAL, "null argument");
   return reinterpret_cast<Model*>(m)->train_step(ids, ood_mask, host_inputs, step, total_steps,
                                                  stats, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int glt_model_step_stats(GltModel* m, int step, GltStepStats* stats) {
+  if (!m || !stats) return glt::fail(GLT_EINVAL, "null argument");
+  return reinterpret_cast<Model*>(m)->step_stats(step, stats);
 }
 
 extern "C" int glt_forward(GltModel* m, const int32_t* ids, int host_inputs, int use_graft,

@@ -102,7 +102,11 @@ struct Model {
   float* cos_t = nullptr;
   float* sin_t = nullptr;
   DevStats* stats = nullptr;
-  DevStats* pinned_stats = nullptr;
+  DevStats* pinned_stats = nullptr;   // [2]: the stats of the last two training steps
+  cudaEvent_t stats_ev[2] = {nullptr, nullptr};
+  int stats_step[2] = {-1, -1};
+  float stats_lr[2] = {0.f, 0.f};
+  int step_stats(int step, GltStepStats* out);
   int* d_enabled = nullptr;
   uint16_t** d_gu_ptrs = nullptr;
   uint16_t** d_wd_ptrs = nullptr;

@@ -178,6 +178,12 @@ class GraftModel:
             return None
         return {f: getattr(st, f) for f, _ in GltStepStats._fields_}
 
+    def step_stats(self, step: int) -> dict:
+        """Stats of an enqueued training step (one of the last two), waiting for that step only."""
+        st = GltStepStats()
+        check(lib.glt_model_step_stats(self.handle, step, C.byref(st)))
+        return {f: getattr(st, f) for f, _ in GltStepStats._fields_}
+
     def forward(self, ids: torch.Tensor, use_graft: bool = True, want_logits: bool = True):
         host = int(ids.device.type == "cpu")
         ids = ids.to(torch.int32).contiguous()

@@ -370,13 +370,20 @@ typedef struct GltStepStats {
 } GltStepStats;
 
 /* One training step (grafting.hip:954-1172): forward with saved activations,
- * CE on domain tokens + OOD silence loss, backward with FFN recompute,
- * global-norm clip, graft-only AdamW.  ids/ood_mask are [B*T] int32; with
- * host_inputs = 1 they are host pointers copied inside the call.  If stats
- * is non-NULL the call synchronises the stream and fills it. */
+ * CE on domain tokens + OOD silence loss, backward (from stored or
+ * recomputed FFN pre-activations, glt_model_mlp_store), global-norm clip,
+ * graft-only AdamW.  ids/ood_mask are [B*T] int32; with host_inputs = 1 they
+ * are host pointers copied inside the call (the host buffers may be reused
+ * as soon as it returns).  If stats is non-NULL the call waits for the step
+ * and fills it; with NULL it only enqueues the step. */
 GLT_API int glt_train_step(GltModel* m, const int32_t* ids, const int32_t* ood_mask,
                            int host_inputs, int step, int total_steps, GltStepStats* stats,
                            void* stream);
+/* The stats of an enqueued training step (one of the last two): waits for
+ * that step only, so a caller can enqueue step k+1 before reading step k's
+ * stats and keep the device busy while it logs (the reference reads them
+ * with .item() host syncs).  GLT_EINVAL for an older step. */
+GLT_API int glt_model_step_stats(GltModel* m, int step, GltStepStats* stats);
 
 /* Forward only; writes bf16 logits [B*T, V] (device) when logits != NULL.
  * use_graft = 0 runs the base model (graft columns skipped). */

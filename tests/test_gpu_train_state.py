@@ -70,3 +70,31 @@ def test_resume_refuses_other_domain_and_baked_model(tmp_path):
     with pytest.raises(GltError):
         load_state(a, p)
     a.close()
+
+
+def test_pipelined_steps_report_the_same_stats():
+    """Steps enqueued without waiting (stats read one step behind through
+    glt_model_step_stats) train exactly like steps that wait for their stats;
+    only the last two steps' stats are kept."""
+    rc = small_cfg(lr_peak=5e-3, lr_warmup_steps=1)
+    B, T = 2, 128
+    w, delta, ids, ood = problem(rc, B, T)
+    a = gpu_model(rc, w, delta, B, T)
+    sync = [a.train_step(ids, ood, s, 5) for s in range(5)]
+    b = gpu_model(rc, w, delta, B, T)
+    piped = []
+    for s in range(5):
+        assert b.train_step(ids, ood, s, 5, want_stats=False) is None   # host ids reused right away
+        if s:
+            piped.append(b.step_stats(s - 1))
+    piped.append(b.step_stats(4))
+    assert b.step_stats(3)["lr"] == sync[3]["lr"]
+    with pytest.raises(GltError):
+        b.step_stats(2)                      # no longer kept
+    for x, y in zip(sync, piped):
+        assert y["lr"] == x["lr"]
+        for k in ("lm_loss", "silence_loss", "total_loss", "grad_norm"):
+            assert y[k] == pytest.approx(x[k], rel=1e-4, abs=1e-7), k
+    torch.testing.assert_close(b.read_graft("weight"), a.read_graft("weight"), rtol=0, atol=1e-5)
+    a.close()
+    b.close()

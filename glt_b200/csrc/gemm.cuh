@@ -254,6 +254,64 @@ struct EpiBF16 {
   }
 };
 
+// The QKV projection with RoPE in its epilogue: C (bf16) = bf16(rope(acc)).
+// Columns [0, rope_cols) hold the q and k heads (hd columns each), rotated
+// half-split at their token's position (row % T) -- the rotation of
+// rope_impl.inc:21-36 that rope_kernel applies to stored bf16 q/k, here on
+// the fp32 accumulator before its one rounding; v columns pass through.  A
+// tile holds whole heads (BN % hd == 0, hd in {64, 128}), so each pair of
+// 32-column chunks (i, i + hd/2) is in the same tile.
+template <int BN>
+struct EpiBF16Rope {
+  uint16_t* C;
+  int64_t ldc;
+  int M, N;
+  int rope_cols, T, hd;
+  const float* cs;   // [T, hd/2]
+  const float* sn;
+  __device__ __forceinline__ void operator()(const tc::EpiCtx<BN>& c) const {
+    const bool row_ok = c.row < M;
+    const int half = hd >> 1;
+    const int pos = c.row % T;
+#pragma unroll 1
+    for (int hb = 0; hb < BN; hb += hd) {
+#pragma unroll 1
+      for (int jj = 0; jj < half; jj += 32) {
+        const int j1 = hb + jj, j2 = j1 + half;
+        float a[32], b[32];
+        c.load(j1, a);   // warp-collective: every lane loads
+        c.load(j2, b);
+        const int col1 = c.n0 + j1;   // the same for the whole warp
+        if (col1 >= N || !row_ok) continue;
+        if (col1 < rope_cols) {
+          const float4* cp = reinterpret_cast<const float4*>(cs + static_cast<int64_t>(pos) * half + jj);
+          const float4* sp = reinterpret_cast<const float4*>(sn + static_cast<int64_t>(pos) * half + jj);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float4 co = __ldg(cp + q), si = __ldg(sp + q);
+            const float cv[4] = {co.x, co.y, co.z, co.w}, sv[4] = {si.x, si.y, si.z, si.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const float x1 = a[4 * q + k], x2 = b[4 * q + k];
+              a[4 * q + k] = x1 * cv[k] - x2 * sv[k];
+              b[4 * q + k] = x2 * cv[k] + x1 * sv[k];
+            }
+          }
+        }
+        uint16_t* d1 = C + static_cast<int64_t>(c.row) * ldc + col1;
+        uint16_t* d2 = d1 + half;
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          *reinterpret_cast<uint4*>(d1 + i) = make_uint4(pack_bf16x2(a[i], a[i + 1]), pack_bf16x2(a[i + 2], a[i + 3]),
+                                                         pack_bf16x2(a[i + 4], a[i + 5]), pack_bf16x2(a[i + 6], a[i + 7]));
+          *reinterpret_cast<uint4*>(d2 + i) = make_uint4(pack_bf16x2(b[i], b[i + 1]), pack_bf16x2(b[i + 2], b[i + 3]),
+                                                         pack_bf16x2(b[i + 4], b[i + 5]), pack_bf16x2(b[i + 6], b[i + 7]));
+        }
+      }
+    }
+  }
+};
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace glt

@@ -661,8 +661,13 @@ int Model::forward_layer(int l, bool use_graft, cudaStream_t st) {
   Layer& y = layers[l];
   AttnShape as{B, T, nh, nkv, hd, QKV, AD, 1.0f / sqrtf(static_cast<float>(hd))};
   GLT_PROF(GLT_PROF_RMSNORM, rmsnorm_fwd(xs[l], y.in_norm, xn, y.var1, M, D, cfg.rms_norm_eps, st));
-  GLT_PROF(GLT_PROF_QKV, g_bf16(kmaj(xn, D), kmaj(y.wqkv, D), M, QKV, D, y.qkv, QKV, nullptr, 0, st));
-  if (rope_on(l)) GLT_PROF(GLT_PROF_ROPE, rope_apply(y.qkv, as, cos_t, sin_t, 0, 1, 1, st));
+  if (rope_on(l)) {
+    // RoPE on q and k in the QKV GEMM's epilogue (no extra pass over qkv)
+    EpiBF16Rope<256> e{y.qkv, QKV, M, QKV, (nh + nkv) * hd, T, hd, cos_t, sin_t};
+    GLT_PROF(GLT_PROF_QKV, (launch_gemm<256, 4, false, false>(kmaj(xn, D), kmaj(y.wqkv, D), M, QKV, D, e, st)));
+  } else {
+    GLT_PROF(GLT_PROF_QKV, g_bf16(kmaj(xn, D), kmaj(y.wqkv, D), M, QKV, D, y.qkv, QKV, nullptr, 0, st));
+  }
   // tcgen05/TMEM kernel for 128-token tiles; the mma.sync kernel covers seq_len % 128 != 0
   if (T % 128 == 0)
     GLT_PROF(GLT_PROF_ATTN_FWD, flash_fwd_tc(y.qkv, y.o, y.lse, as, st));

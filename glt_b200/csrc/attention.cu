@@ -449,6 +449,38 @@ __global__ void dq_convert_kernel(const float* __restrict__ acc, uint16_t* __res
   }
 }
 
+// dq (fp32 accumulator) -> bf16 q columns of dqkv with the inverse RoPE
+// (the transpose of rope_kernel's rotation) applied before the rounding:
+// one thread per (token, head, 4 dims of the first half) and their partners.
+__global__ void dq_convert_rope_kernel(const float* __restrict__ acc, uint16_t* __restrict__ dqkv, int64_t M,
+                                       int nh, int hd, int64_t ld, int T, const float* __restrict__ cs,
+                                       const float* __restrict__ sn) {
+  const int half = hd / 2;
+  const int groups = half / 4;
+  const int64_t total = M * nh * groups;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int g = static_cast<int>(i % groups);
+    const int64_t r = i / groups;
+    const int h = static_cast<int>(r % nh);
+    const int64_t t = r / nh;
+    const int pos = static_cast<int>(t % T);
+    const float* a = acc + t * (static_cast<int64_t>(nh) * hd) + static_cast<int64_t>(h) * hd + g * 4;
+    const float4 x1 = *reinterpret_cast<const float4*>(a);
+    const float4 x2 = *reinterpret_cast<const float4*>(a + half);
+    const float4 co = *reinterpret_cast<const float4*>(cs + static_cast<int64_t>(pos) * half + g * 4);
+    const float4 si = *reinterpret_cast<const float4*>(sn + static_cast<int64_t>(pos) * half + g * 4);
+    uint2 o1, o2;
+    o1.x = pk(x1.x * co.x + x2.x * si.x, x1.y * co.y + x2.y * si.y);
+    o1.y = pk(x1.z * co.z + x2.z * si.z, x1.w * co.w + x2.w * si.w);
+    o2.x = pk(x2.x * co.x - x1.x * si.x, x2.y * co.y - x1.y * si.y);
+    o2.y = pk(x2.z * co.z - x1.z * si.z, x2.w * co.w - x1.w * si.w);
+    uint16_t* d = dqkv + t * ld + static_cast<int64_t>(h) * hd + g * 4;
+    *reinterpret_cast<uint2*>(d) = o1;
+    *reinterpret_cast<uint2*>(d + half) = o2;
+  }
+}
+
 // RoPE: one thread per (token, head, 8 consecutive dims of the first half)
 __global__ void rope_kernel(uint16_t* __restrict__ qkv, AttnShape s, const float* __restrict__ cs,
                             const float* __restrict__ sn, int inverse, int head_begin,
@@ -508,9 +540,10 @@ int fwd_impl(const uint16_t* qkv, uint16_t* o, float* lse, const AttnShape& s, c
 
 template <int HD>
 int bwd_prep_impl(const uint16_t* o, const uint16_t* dout, float* dq_acc, float* dsum,
-                  const AttnShape& s, cudaStream_t st) {
+                  const AttnShape& s, cudaStream_t st, bool dsum_ready = false) {
   const int64_t M = static_cast<int64_t>(s.B) * s.T;
   GLT_CUDA_TRY(cudaMemsetAsync(dq_acc, 0, M * s.nh * HD * sizeof(float), st));
+  if (dsum_ready) return GLT_OK;
   const int64_t warps = M * s.nh;
   const int blocks = static_cast<int>((warps * 32 + 255) / 256);
   bwd_dsum_kernel<HD><<<blocks, 256, 0, st>>>(o, dout, dsum, s);
@@ -518,8 +551,17 @@ int bwd_prep_impl(const uint16_t* o, const uint16_t* dout, float* dq_acc, float*
   return GLT_OK;
 }
 
-int bwd_finish_impl(const float* dq_acc, uint16_t* dqkv, const AttnShape& s, cudaStream_t st) {
+int bwd_finish_impl(const float* dq_acc, uint16_t* dqkv, const AttnShape& s, cudaStream_t st,
+                    const float* rope_cos = nullptr, const float* rope_sin = nullptr) {
   const int64_t M = static_cast<int64_t>(s.B) * s.T;
+  if (rope_cos) {
+    const int64_t n = M * s.nh * (s.hd / 8);
+    int blocks = static_cast<int>((n + 255) / 256);
+    if (blocks > num_sms() * 16) blocks = num_sms() * 16;
+    dq_convert_rope_kernel<<<blocks, 256, 0, st>>>(dq_acc, dqkv, M, s.nh, s.hd, s.ld_qkv, s.T, rope_cos, rope_sin);
+    GLT_LAUNCH_CHECK();
+    return GLT_OK;
+  }
   const int64_t n = M * s.nh * s.hd / 4;
   int blocks = static_cast<int>((n + 255) / 256);
   if (blocks > num_sms() * 16) blocks = num_sms() * 16;
@@ -571,14 +613,16 @@ int flash_fwd(const uint16_t* qkv, uint16_t* o, float* lse, const AttnShape& s, 
 }
 
 int attn_bwd_prep(const uint16_t* o, const uint16_t* dout, float* dq_acc, float* dsum,
-                  const AttnShape& s, cudaStream_t st) {
+                  const AttnShape& s, cudaStream_t st, bool dsum_ready) {
   GLT_TRY(check_shape(s));
-  return s.hd == 128 ? bwd_prep_impl<128>(o, dout, dq_acc, dsum, s, st)
-                     : bwd_prep_impl<64>(o, dout, dq_acc, dsum, s, st);
+  return s.hd == 128 ? bwd_prep_impl<128>(o, dout, dq_acc, dsum, s, st, dsum_ready)
+                     : bwd_prep_impl<64>(o, dout, dq_acc, dsum, s, st, dsum_ready);
 }
 
-int attn_bwd_finish(const float* dq_acc, uint16_t* dqkv, const AttnShape& s, cudaStream_t st) {
-  return bwd_finish_impl(dq_acc, dqkv, s, st);
+int attn_bwd_finish(const float* dq_acc, uint16_t* dqkv, const AttnShape& s, cudaStream_t st,
+                    const float* rope_cos, const float* rope_sin) {
+  if (rope_cos && (s.hd % 8 || !rope_sin)) return fail(GLT_EINVAL, "attn_bwd_finish: rope tables");
+  return bwd_finish_impl(dq_acc, dqkv, s, st, rope_cos, rope_sin);
 }
 
 int flash_bwd(const uint16_t* qkv, const uint16_t* o, const uint16_t* dout, const float* lse,

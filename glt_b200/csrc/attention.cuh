@@ -33,13 +33,19 @@ int flash_fwd_tc(const uint16_t* qkv, uint16_t* o, float* lse, const AttnShape& 
 int flash_bwd(const uint16_t* qkv, const uint16_t* o, const uint16_t* dout, const float* lse,
               uint16_t* dqkv, float* dq_acc, float* dsum, const AttnShape& s, cudaStream_t st);
 // tcgen05/TMEM backward (attention_tc.cu; hd 128, seq_len % 128 == 0); same
-// contract as flash_bwd.
+// contract as flash_bwd.  dsum_ready: dsum was computed by the caller (the
+// dO GEMM's epilogue, EpiBF16Dsum).  rope_cos/sin (nullable, [T, hd/2]):
+// the inverse RoPE of the q columns is applied to dq before its bf16
+// rounding (the k columns are left to rope_apply).
 int flash_bwd_tc(const uint16_t* qkv, const uint16_t* o, const uint16_t* dout, const float* lse,
-                 uint16_t* dqkv, float* dq_acc, float* dsum, const AttnShape& s, cudaStream_t st);
+                 uint16_t* dqkv, float* dq_acc, float* dsum, const AttnShape& s, cudaStream_t st,
+                 bool dsum_ready = false, const float* rope_cos = nullptr, const float* rope_sin = nullptr);
 // Shared pre/post steps of both backward kernels: zero dq_acc and compute
-// dsum = rowsum(dO * O); convert dq_acc (fp32) into the q columns of dqkv.
+// dsum = rowsum(dO * O) (unless dsum_ready); convert dq_acc (fp32) into the
+// q columns of dqkv, with the inverse RoPE when tables are given.
 int attn_bwd_prep(const uint16_t* o, const uint16_t* dout, float* dq_acc, float* dsum,
-                  const AttnShape& s, cudaStream_t st);
-int attn_bwd_finish(const float* dq_acc, uint16_t* dqkv, const AttnShape& s, cudaStream_t st);
+                  const AttnShape& s, cudaStream_t st, bool dsum_ready = false);
+int attn_bwd_finish(const float* dq_acc, uint16_t* dqkv, const AttnShape& s, cudaStream_t st,
+                    const float* rope_cos = nullptr, const float* rope_sin = nullptr);
 
 }  // namespace glt

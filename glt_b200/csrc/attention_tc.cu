@@ -746,12 +746,13 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
 }  // namespace
 
 int flash_bwd_tc(const uint16_t* qkv, const uint16_t* o, const uint16_t* dout, const float* lse,
-                 uint16_t* dqkv, float* dq_acc, float* dsum, const AttnShape& s, cudaStream_t st) {
+                 uint16_t* dqkv, float* dq_acc, float* dsum, const AttnShape& s, cudaStream_t st,
+                 bool dsum_ready, const float* rope_cos, const float* rope_sin) {
   if (s.hd != 128) return fail(GLT_EINVAL, "attention backward (tcgen05): head_dim must be 128");
   if (s.T % BK_KEYS) return fail(GLT_EINVAL, "attention backward (tcgen05): seq_len %% 128 != 0");
   if (s.nkv <= 0 || s.nh % s.nkv) return fail(GLT_EINVAL, "attention: nh %% nkv != 0");
   if (s.ld_qkv % 8 || s.ld_o % 8) return fail(GLT_EINVAL, "attention: strides not 16-byte");
-  GLT_TRY(attn_bwd_prep(o, dout, dq_acc, dsum, s, st));
+  GLT_TRY(attn_bwd_prep(o, dout, dq_acc, dsum, s, st, dsum_ready));
   const int64_t M = static_cast<int64_t>(s.B) * s.T;
   CUtensorMap tk, tq, tdo, tdq;
   GLT_TRY(make_tmap_bf16(&tk, qkv, s.ld_qkv, M, s.ld_qkv, BK_KEYS));
@@ -765,7 +766,7 @@ int flash_bwd_tc(const uint16_t* qkv, const uint16_t* o, const uint16_t* dout, c
   attn_bwd_tc_kernel<<<grid, BWD_THREADS, smem, st>>>(tk, tq, tdo, tdq, lse, dsum, dqkv, s,
                                               device_error_word());
   GLT_LAUNCH_CHECK();
-  return attn_bwd_finish(dq_acc, dqkv, s, st);
+  return attn_bwd_finish(dq_acc, dqkv, s, st, rope_cos, rope_sin);
 }
 
 int flash_fwd_tc(const uint16_t* qkv, uint16_t* o, float* lse, const AttnShape& s,

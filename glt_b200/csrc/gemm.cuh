@@ -312,6 +312,54 @@ struct EpiBF16Rope {
   }
 };
 
+// The dO GEMM with the attention backward's row sums in its epilogue:
+// C (bf16) = bf16(acc) and, per row and head (hd columns, whole heads per
+// tile), dsum[(b * nh + h) * T + t] = sum over the head of bf16(dO) * O --
+// the D_i = rowsum(dO o O) the flash backward needs (bwd_dsum_kernel's
+// value, summed in another order), from the rounded dO it stores.
+template <int BN>
+struct EpiBF16Dsum {
+  uint16_t* C;
+  int64_t ldc;
+  int M, N;
+  const uint16_t* O;
+  int64_t ldo;
+  float* dsum;
+  int T, nh, hd;
+  __device__ __forceinline__ void operator()(const tc::EpiCtx<BN>& c) const {
+    const bool row_ok = c.row < M;
+#pragma unroll 1
+    for (int hb = 0; hb < BN; hb += hd) {
+      float acc = 0.f;
+#pragma unroll 1
+      for (int jj = 0; jj < hd; jj += 32) {
+        float v[32];
+        c.load(hb + jj, v);   // warp-collective: every lane loads
+        const int col = c.n0 + hb + jj;
+        if (col >= N || !row_ok) continue;
+        uint16_t* dst = C + static_cast<int64_t>(c.row) * ldc + col;
+        const uint4* orow = reinterpret_cast<const uint4*>(O + static_cast<int64_t>(c.row) * ldo + col);
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          uint4 w;
+          w.x = pack_bf16x2(v[i], v[i + 1]); w.y = pack_bf16x2(v[i + 2], v[i + 3]);
+          w.z = pack_bf16x2(v[i + 4], v[i + 5]); w.w = pack_bf16x2(v[i + 6], v[i + 7]);
+          *reinterpret_cast<uint4*>(dst + i) = w;
+          const uint4 o = __ldg(orow + i / 8);
+          acc += bf16_lo(w.x) * bf16_lo(o.x) + bf16_hi(w.x) * bf16_hi(o.x) + bf16_lo(w.y) * bf16_lo(o.y) +
+                 bf16_hi(w.y) * bf16_hi(o.y) + bf16_lo(w.z) * bf16_lo(o.z) + bf16_hi(w.z) * bf16_hi(o.z) +
+                 bf16_lo(w.w) * bf16_lo(o.w) + bf16_hi(w.w) * bf16_hi(o.w);
+        }
+      }
+      const int h = (c.n0 + hb) / hd;
+      if (row_ok && c.n0 + hb < N) {
+        const int b = c.row / T, t = c.row - b * T;
+        dsum[(static_cast<int64_t>(b) * nh + h) * T + t] = acc;
+      }
+    }
+  }
+};
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace glt

@@ -753,12 +753,20 @@ int Model::backward_layer(int l, cudaStream_t st) {
   // post-attention RMSNorm backward + residual: dx = grad wrt x_post
   GLT_PROF(GLT_PROF_RMSNORM, rmsnorm_bwd(dtmp, y.x_post, y.post_norm, y.var2, dx, dx, dy_b, M, D, cfg.rms_norm_eps, st));
   // attention: do = dx_post . Wo ; flash backward ; RoPE^T ; dxn = dqkv . Wqkv
-  GLT_PROF(GLT_PROF_DO, g_bf16(kmaj(dy_b, D), mnmaj(y.wo, AD), M, AD, D, dout_b, AD, nullptr, 0, st));
-  if (hd == 128 && T % 128 == 0)
-    GLT_PROF(GLT_PROF_ATTN_BWD, flash_bwd_tc(y.qkv, y.o, dout_b, y.lse, dqkv, dq_acc, dsum, as, st));
-  else
+  if (hd == 128 && T % 128 == 0) {
+    // tcgen05 backward: dsum from the dO GEMM's epilogue, the inverse RoPE
+    // of dq in its fp32 -> bf16 conversion, the one of dk in rope_apply
+    EpiBF16Dsum<256> e{dout_b, AD, M, AD, y.o, AD, dsum, T, nh, hd};
+    GLT_PROF(GLT_PROF_DO, (launch_gemm<256, 4, false, true>(kmaj(dy_b, D), mnmaj(y.wo, AD), M, AD, D, e, st)));
+    const bool rope = rope_on(l);
+    GLT_PROF(GLT_PROF_ATTN_BWD, flash_bwd_tc(y.qkv, y.o, dout_b, y.lse, dqkv, dq_acc, dsum, as, st, true,
+                                             rope ? cos_t : nullptr, rope ? sin_t : nullptr));
+    if (rope) GLT_PROF(GLT_PROF_ROPE, rope_apply(dqkv, as, cos_t, sin_t, 1, 0, 1, st));
+  } else {
+    GLT_PROF(GLT_PROF_DO, g_bf16(kmaj(dy_b, D), mnmaj(y.wo, AD), M, AD, D, dout_b, AD, nullptr, 0, st));
     GLT_PROF(GLT_PROF_ATTN_BWD, flash_bwd(y.qkv, y.o, dout_b, y.lse, dqkv, dq_acc, dsum, as, st));
-  if (rope_on(l)) GLT_PROF(GLT_PROF_ROPE, rope_apply(dqkv, as, cos_t, sin_t, 1, 1, 1, st));
+    if (rope_on(l)) GLT_PROF(GLT_PROF_ROPE, rope_apply(dqkv, as, cos_t, sin_t, 1, 1, 1, st));
+  }
   GLT_PROF(GLT_PROF_DX_QKV, g_f32(kmaj(dqkv, QKV), mnmaj(y.wqkv, D), M, D, QKV, dtmp, D, st));
   GLT_PROF(GLT_PROF_RMSNORM, rmsnorm_bwd(dtmp, xs[l], y.in_norm, y.var1, dx, dx, nullptr, M, D, cfg.rms_norm_eps, st));
   return GLT_OK;

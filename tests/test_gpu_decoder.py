@@ -158,3 +158,26 @@ def test_train_step_with_any_ood_mask_matches_oracle(mask):
         assert_close_bf16(grad_gpu, grad_ref, f"graft grads ({mask} mask)")
     else:
         assert float(grad_gpu.abs().max()) == 0.0
+
+
+@pytest.mark.parametrize("no_rope", [[], [1, 0]])
+def test_train_step_head_dim_128_matches_oracle(no_rope):
+    """head_dim 128 runs the tcgen05 attention backward with the row sums
+    D = rowsum(dO o O) from the dO GEMM's epilogue and the inverse RoPE of dq
+    in its fp32 -> bf16 conversion (RoPE on layer 0 only with [1, 0])."""
+    rc = small_cfg(hidden_dim=512, intermediate_dim=1024, num_heads=4, num_kv_heads=2, no_rope_layers=no_rope)
+    assert rc.head_dim == 128
+    B, T = 2, 256
+    w, delta, ids, ood = problem(rc, B, T, std=0.05, graft_std=0.05)
+    m = gpu_model(rc, w, delta, B, T)
+    st = m.train_step(ids, ood, step=0, total_steps=10)
+    grad_gpu = m.read_graft("grad").cpu()
+    m.close()
+    grad_ref, stats, _ = rm.compute_grads(ids, ood, w, delta.clone(), rc)
+    assert st["lm_loss"] == pytest.approx(stats["lm_loss"], rel=1e-2)
+    assert st["total_loss"] == pytest.approx(stats["total_loss"], rel=1e-2)
+    SH = rc.slice_dim * rc.h_slice_dim
+    for l in range(rc.num_layers):
+        for p, name in enumerate(("gate", "up", "down")):
+            sl = slice((3 * l + p) * SH, (3 * l + p + 1) * SH)
+            assert_close_bf16(grad_gpu[sl], grad_ref[sl], f"hd128 grad L{l} {name}")

@@ -43,17 +43,20 @@ def run_point(M: int, S: int, steps: int, warmup: int, D: int = 4096, F: int = 1
     torch.cuda.synchronize()
     m.profile(False)
     kms, kn = m.profile_read()
+    store_on, _ = m.mlp_store()
     m.close()
     ms = e0.elapsed_time(e1) / steps
     Fp = F + S
     alg = M * (12.0 * D * Fp + 6.0 * D * S)   # fwd 6DF' + input grad 6DF' + graft dW 6DS
-    gemm_kinds = [0, 1, 2, 6, 7, 8, 9, 10]
+    gemm_kinds = [0, 1, 2, 6, 7, 8, 9, 10]   # the recompute kind (7) is zero with the MLP store
     gemm_ms = sum(kms[k] for k in gemm_kinds) / steps
     kernels = {G.PROF_NAMES[k]: round(kms[k] / steps, 4) for k in gemm_kinds}
     return {"tokens": M, "slice": S, "hidden": D, "ffn": F, "ms_per_step": ms,
             "block_tflops": alg / (ms / 1e3) / 1e12,
             "gemm_tflops_algorithmic": alg / (gemm_ms / 1e3) / 1e12,
-            "gemm_tflops_executed": (alg + M * (4.0 * D * Fp + 2.0 * D * S)) / (gemm_ms / 1e3) / 1e12,
+            "gemm_tflops_executed": (alg + M * ((0.0 if store_on else 4.0 * D * Fp) + 2.0 * D * S))
+                                    / (gemm_ms / 1e3) / 1e12,
+            "mlp_activations": "stored" if store_on else "recomputed",
             "gemm_ms": gemm_ms, "non_gemm_ms": ms - gemm_ms, "kernel_ms": kernels}
 
 

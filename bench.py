@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""Graft-train throughput at the Llama-3-8B shape (BASELINE config 3).
+"""Graft-train throughput at the Llama-3-8B shape.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -39,12 +39,12 @@ WORKLOADS = {
     "c3": dict(num_layers=32, hidden_dim=4096, intermediate_dim=14336, slice_dim=1024, num_heads=32,
                num_kv_heads=8, head_dim=128, vocab_size=128256, rope_theta=500000.0,
                tie_embeddings=0, batch=16, seq=2048,
-               label="llama3-8b graft-train (BASELINE config 3): 32L d4096 ffn14336 + graft 1024, "
+               label="llama3-8b graft-train: 32L d4096 ffn14336 + graft 1024, "
                      "32q/8kv hd128, vocab 128256, 16x2048 tokens/GPU"),
     "c2": dict(num_layers=24, hidden_dim=896, intermediate_dim=4864, slice_dim=512, num_heads=14,
                num_kv_heads=2, head_dim=64, vocab_size=151936, rope_theta=1000000.0,
                tie_embeddings=1, batch=8, seq=1024,
-               label="qwen2.5-0.5b graft-train (BASELINE config 2): 24L d896 ffn4864 + graft 512, "
+               label="qwen2.5-0.5b graft-train: 24L d896 ffn4864 + graft 512, "
                      "14q/2kv hd64, vocab 151936, 8x1024 tokens/GPU"),
 }
 METRIC = "graft-train tokens/s at Llama-3-8B shape, 1-8 B200; MLP GEMM % of bf16 peak"
@@ -187,14 +187,20 @@ def run_reference_arm(args, wl):
         "impl": "reference", "metric": METRIC, "value": tok_s, "unit": "tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": wl["batch"] * wl["seq"] / tok_s * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "extrapolated": True,
+        "sample_ms_per_step": sec_layer * 1e3,
+        "higher_is_better": True, "scaling": "none: one host's cores, the same line at every --gpus",
+        "vs_baseline": None, "dtype": "f32",
         "data": "synthetic: N(0,0.02) weights, N(0,1) activations",
         "config": {"workload": wl["label"], "global_batch": wl["batch"], "seq_len": wl["seq"],
                    "parallelism": "cpu"},
         "cpu_baseline": {"value": tok_s, "unit": "tokens/s", "cores": cores, "kind": "port",
                          "sample": f"fp32 CPU oracle: one grafted decoder layer forward+backward on "
-                                   f"1x{tokens} tokens per step, extrapolated to "
-                                   f"{wl['num_layers']} layers (LM head excluded)"},
+                                   f"1x{tokens} tokens per step ({sec_layer * 1e3:.0f} ms measured), "
+                                   f"extrapolated linearly to {wl['num_layers']} layers and "
+                                   f"{wl['batch']}x{wl['seq']} tokens (LM head excluded); "
+                                   f"ms_per_step is that extrapolation",
+                         "sampled_layers": 1, "sampled_tokens": tokens, "extrapolated": True},
         "e2e": {"value": tok_s, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -214,6 +220,12 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=512)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--mlp-store", choices=["0", "1", "auto"], default="auto",
+                    help="FFN pre-activations in the timed steps: 1 stored by the forward, "
+                         "0 recomputed in the backward (recompute_ffn), auto as the library decides")
+    ap.add_argument("--recompute-steps", type=int, default=None,
+                    help="steps of the extra recompute-mode timing after the main one "
+                         "(default: --steps; 0 skips it)")
     args = ap.parse_args()
     wl = WORKLOADS[args.workload]
     if args.impl == "reference":
@@ -244,6 +256,8 @@ def main():
         graft_layer_end=wl["num_layers"] - 1, graft_proj_gate=1, graft_proj_up=1, graft_proj_down=1,
         allow_expansion_trap=1, lambda_silence=5.0, lr_peak=2e-4, lr_warmup_steps=20)
     model = G.GraftModel(cfg, B, T)
+    if args.mlp_store != "auto":
+        model.mlp_store(int(args.mlp_store))
     # replicas start identical; graft down N(0,0.02) so no zero-skipping shortcut exists
     model.init_random(seed=1234, std=0.02, graft_std=0.02, graft_down_std=0.02)
     if world > 1:
@@ -352,6 +366,29 @@ def main():
         e2e_s = max_over_ranks((time.perf_counter() - t0) / args.steps)
         e2e = {"value": tokens_per_step / e2e_s, "unit": "tokens/s",
                "h2d_bytes_per_step": 2 * M * 4, "d2h_bytes_per_step": 32}
+
+    # The same step with the reference's FFN recompute (recompute_ffn) instead
+    # of stored pre-activations, timed the same way after the main region.
+    extra = {}
+    rsteps = args.steps if args.recompute_steps is None else args.recompute_steps
+    if store_on and rsteps > 0:
+        model.mlp_store(0)
+        model.train_step(ids, ood, step, total_steps + 2 * args.steps + rsteps + 1, want_stats=False)
+        step += 1
+        barrier()
+        r0 = torch.cuda.Event(enable_timing=True)
+        r1 = torch.cuda.Event(enable_timing=True)
+        r0.record(stream)
+        for _ in range(rsteps):
+            model.train_step(ids, ood, step, total_steps + 2 * args.steps + rsteps + 1, want_stats=False)
+            step += 1
+        r1.record(stream)
+        torch.cuda.synchronize()
+        rms = max_over_ranks(r0.elapsed_time(r1) / rsteps)
+        extra = {"recompute_ms_per_step": rms, "recompute_tokens_per_s": tokens_per_step / (rms / 1e3),
+                 "recompute_steps": rsteps,
+                 "recompute_note": "same step with the FFN gate/up recomputed in the backward "
+                                   "(recompute_ffn) instead of stored, timed after the main region"}
     if world > 1:
         model.dp_finalize()
 
@@ -359,7 +396,7 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         sec, cores = cpu_oracle_sample(wl, args.cpu_tokens)
         cpu = {"value": args.cpu_tokens / (sec * L), "unit": "tokens/s", "cores": cores,
-               "kind": "port",
+               "kind": "port", "extrapolated": True,
                "sample": f"fp32 CPU oracle: one grafted decoder layer forward+backward on "
                          f"1x{args.cpu_tokens} tokens (median of 2 after 1 warm-up), extrapolated "
                          f"to {L} layers (LM head excluded)"}
@@ -380,7 +417,7 @@ def main():
                                            if store_on else "recomputed in the backward (recompute_ffn)"),
                        "l2": f"no flush: the step streams {w_bytes / 1e9:.1f} GB of weights, and its "
                              f"activations, through the 126 MB L2"},
-            "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu,
+            "e2e": e2e, "roofline": roofline, "cpu_baseline": cpu, "extra": extra,
             "clocks": clk.summary(),
             "gpu_launches": int(launches1.value - launches0.value),
             "kernels": kernels,

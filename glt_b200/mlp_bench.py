@@ -1,4 +1,4 @@
-"""Grafted-MLP microbench.
+"""Grafted-MLP microbench sweep (hidden 4096, base intermediate 14336).
 
     python -m glt_b200.mlp_bench [--tokens 4096,16384,65536] [--slice 256,1024,4096]
                                  [--steps 5] [--warmup 3]

@@ -1,4 +1,4 @@
-"""Stacked-graft inference: four independently seeded
+"""Stacked-graft inference at the Llama-3-8B shape: four independently seeded
 sibling grafts of width 512 active at once on the Llama-3-8B shape, prefill
 forward of batch 8 x seq 4096 uniform-random tokens, explicit stack versus
 the same grafts shadow-baked into the base MLP weights.
@@ -149,7 +149,7 @@ def run(geometry: str, a, world: int, rank: int, dist) -> dict:
     del logits_base
     m.close()
     tok = world * B * T
-    return {"config": "stacked-graft inference (BASELINE config 4)", "geometry": geometry,
+    return {"config": "stacked-graft inference, llama3-8b shape, 4 x 512 sibling grafts, prefill 8 x 4096", "geometry": geometry,
             "stack": f"{N} sibling grafts x {S_each}", "model": f"llama3-8b shape, {L} layers",
             "batch": B, "seq": T, "n_gpus": world, "dtype": "bf16", "data": "synthetic",
             "stack_ms": ms_stack, "stack_tokens_per_s": tok / (ms_stack / 1e3),

@@ -296,7 +296,7 @@ GLT_API int glt_apply_graft_to_shadow(const GltModelConfig* cfg, uint16_t* const
 /* allocate_arena/VramArena (src/arena_impl.inc:14-126) and                 */
 /* allocate_graft_weights/GraftWeights (src/graft_weights_impl.inc:6-62).   */
 /* kind: GLT_MODEL_DECODER runs the full decoder step; GLT_MODEL_MLP_BLOCK  */
-/* runs one pre-RMSNorm grafted MLP block with residual. */
+/* runs one pre-RMSNorm grafted MLP block with residual.                   */
 /* ------------------------------------------------------------------------ */
 #define GLT_MODEL_DECODER 0
 #define GLT_MODEL_MLP_BLOCK 1
@@ -421,7 +421,7 @@ GLT_API int glt_model_eval(GltModel* m, const int32_t* ids, int64_t num_sequence
  * use_graft = 1 forwards fail afterwards.  Synchronises the stream. */
 GLT_API int glt_model_shadow_bake(GltModel* m, void* stream);
 
-/* MLP-block step (BASELINE config 1): out = x + MLP(rms_norm(x)),
+/* MLP-block step: out = x + MLP(rms_norm(x)),
  * loss = mean((out - y)^2), backward to the graft, AdamW with lr.
  * x: bf16 [M, D] device; y: fp32 [M, D] device.  Optional outputs: out (bf16),
  * dx (fp32 grad wrt x), loss (host float, synchronises). */

@@ -416,12 +416,16 @@ def adamw(weight, grad, m, v, step: int, lr: float, cfg: GraftConfig):
         w.sub_(upd)
 
 
-def compute_grads(ids, ood, weights, delta, cfg: GraftConfig):
+def compute_grads(ids, ood, weights, delta, cfg: GraftConfig, keep=None):
     """Forward, loss, silence and the explicit backward of one step (grafting.hip:997-1146).
 
-    Returns (grad [flat, pre-clip], stats dict, logits).
+    Returns (grad [flat, pre-clip], stats dict, logits).  `keep`, a dict, if
+    given receives per layer the forward's x_post and x_ffn ([M*D] each).
     """
     logits, x_last, var_f, saves = model_forward(ids, weights, delta, cfg)
+    if keep is not None:
+        keep["acts"] = [dict(x_post=s["x_post"].detach().reshape(-1).clone(),
+                             x_ffn=s["x_ffn"].detach().reshape(-1).clone()) for s in saves]
     loss, dlogits, _ = lm_loss_and_grad(logits, ids, ood, cfg)
     sil = silence_terms(saves, ood, cfg)
     dx = dlogits @ weights["lm_head"]
@@ -449,7 +453,7 @@ def train_step(ids, ood, weights, delta, m, v, cfg: GraftConfig, step: int, tota
 
 
 # ---------------------------------------------------------------------------
-# Single grafted MLP block
+# Single grafted MLP block (hidden 256, base 688 + graft 64 workload)
 # ---------------------------------------------------------------------------
 def mlp_block_step(x, y, lw, delta, m, v, cfg: GraftConfig, lr: float, step: int = 0):
     """Pre-RMSNorm grafted MLP block with residual, MSE loss, graft-only AdamW.
@@ -473,7 +477,7 @@ def mlp_block_step(x, y, lw, delta, m, v, cfg: GraftConfig, lr: float, step: int
 
 
 # ---------------------------------------------------------------------------
-# Seeded synthetic inputs (N(0, 0.02) weights, as BASELINE specifies)
+# Seeded synthetic inputs (N(0, 0.02) weights)
 # ---------------------------------------------------------------------------
 def init_weights(cfg: GraftConfig, seed: int = 0, std: float = 0.02):
     g = torch.Generator().manual_seed(seed)

@@ -48,7 +48,8 @@ def fwd(qkv, B, T, nh, nkv, hd, impl):
 
 @pytest.mark.parametrize("impl", [TC, MMA])
 @pytest.mark.parametrize("B,T,nh,nkv,hd", [(2, 256, 4, 2, 128), (1, 512, 8, 2, 128),
-                                           (2, 256, 4, 4, 64), (1, 384, 6, 2, 64)])
+                                           (2, 256, 4, 4, 64), (1, 384, 6, 2, 64),
+                                           (2, 256, 14, 2, 64), (1, 1024, 32, 8, 128)])
 def test_forward_matches_fp32_reference(impl, B, T, nh, nkv, hd):
     qkv = make_qkv(B, T, nh, nkv, hd, seed=T + nh + hd)
     q = qkv[:, :nh * hd]
@@ -71,8 +72,9 @@ def test_tcgen05_and_mma_sync_agree_on_large_scores():
 
 
 @pytest.mark.parametrize("impl,B,T,nh,nkv,hd", [(MMA, 2, 128, 4, 2, 128), (MMA, 1, 256, 4, 4, 64),
+                                                (MMA, 2, 256, 14, 2, 64), (MMA, 1, 192, 14, 2, 64),
                                                 (TC, 2, 128, 4, 2, 128), (TC, 1, 384, 8, 2, 128),
-                                                (TC, 2, 256, 4, 4, 128)])
+                                                (TC, 2, 256, 4, 4, 128), (TC, 1, 512, 32, 8, 128)])
 def test_backward_matches_autograd(impl, B, T, nh, nkv, hd):
     qkv = make_qkv(B, T, nh, nkv, hd, seed=11)
     o, lse = fwd(qkv, B, T, nh, nkv, hd, MMA)

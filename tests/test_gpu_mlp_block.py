@@ -1,4 +1,4 @@
-"""BASELINE config 1 on the GPU: one pre-RMSNorm grafted MLP block
+"""The single-block workload on the GPU: one pre-RMSNorm grafted MLP block
 (hidden 256, base intermediate 688 + graft 64 concatenated), MSE loss,
 backward to the graft only, one AdamW step -- against the fp32 oracle."""
 import pytest

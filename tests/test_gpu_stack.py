@@ -1,4 +1,4 @@
-"""Graft stacks (BASELINE config 4 at test size): N sibling grafts of one
+"""Graft stacks (the stacked-inference workload at test size): N sibling grafts of one
 session active at once, explicitly injected versus shadow-baked.
 
 Overlay geometry (the reference's): domain d's graft sits at intermediate rows

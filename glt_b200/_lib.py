@@ -76,6 +76,7 @@ SIGNATURES: dict[str, tuple] = {
     "glt_last_error": (C.c_char_p, []),
     "glt_version": (C.c_char_p, []),
     "glt_device_error": (_i32, [C.POINTER(_u32)]),
+    "glt_selftest_wait_timeout": (_i32, [_i32, _i32, _vp]),
     "glt_gemm": (_i32, [_vp, _i64, _i32, _vp, _i64, _i32, _vp, _i64, _i32,
                         _i32, _i32, _i32, _f32, _f32, _vp]),
     "glt_config_default": (_i32, [_cfgp]),

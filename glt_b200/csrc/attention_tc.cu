@@ -27,7 +27,9 @@
 // is rare; p = exp2(s - m) stays <= 256, well inside fp32/bf16 range, and the
 // final normalisation uses the same m for O and the row sum.
 // All mbarrier waits are bounded (tc::mbar_wait); a timeout sets the device
-// error word and the CTA drains instead of hanging.
+// error word and the CTA's abort flag, the other roles give up their waits,
+// and the CTA waits (bounded) for its loads in flight and its issued MMAs
+// before it frees TMEM and exits, instead of hanging.
 #include <math.h>
 
 #include "attention.cuh"
@@ -163,6 +165,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 2)
   const uint32_t sQ = smem_u32(sm + L::OFF_Q);
   const uint32_t sK = smem_u32(sm + L::OFF_K);
   const uint32_t sV = smem_u32(sm + L::OFF_V);
+  int nk = 0, nv = 0;   // K and V tiles the producer issued (read on the abort path)
 
   if (warp == 0) {
     // ------------------------------ producer ------------------------------
@@ -174,18 +177,20 @@ __global__ void __launch_bounds__(FWD_THREADS, 2)
         tma_load_2d(sm + L::OFF_Q + c * (AQ * 128), &tm_q, q_full, qcol + 64 * c, row_base + qt * AQ);
       for (int j = 0; j < n_kv && !s_abort; ++j) {
         const int ks = j % K_STAGES, vs = j % V_STAGES;
-        if (!mbar_wait(&k_empty[ks], ((j / K_STAGES) & 1) ^ 1, err)) { s_abort = 1; break; }
+        if (!mbar_wait(&k_empty[ks], ((j / K_STAGES) & 1) ^ 1, err, &s_abort)) { s_abort = 1; break; }
         mbar_arrive_expect_tx(&k_full[ks], L::K_BYTES);
         uint8_t* kb = sm + L::OFF_K + ks * L::K_BYTES;
 #pragma unroll
         for (int c = 0; c < HD / 64; ++c)
           tma_load_2d(kb + c * (AK * 128), &tm_kv, &k_full[ks], kcol + 64 * c, row_base + j * AK);
-        if (!mbar_wait(&v_empty[vs], ((j / V_STAGES) & 1) ^ 1, err)) { s_abort = 1; break; }
+        nk = j + 1;
+        if (!mbar_wait(&v_empty[vs], ((j / V_STAGES) & 1) ^ 1, err, &s_abort)) { s_abort = 1; break; }
         mbar_arrive_expect_tx(&v_full[vs], L::V_BYTES);
         uint8_t* vb = sm + L::OFF_V + vs * L::V_BYTES;
 #pragma unroll
         for (int c = 0; c < HD / 64; ++c)
           tma_load_2d(vb + c * (AK * 128), &tm_kv, &v_full[vs], vcol + 64 * c, row_base + j * AK);
+        nv = j + 1;
       }
     }
   } else if (warp == 1) {
@@ -193,9 +198,9 @@ __global__ void __launch_bounds__(FWD_THREADS, 2)
     if (lane == 0) {
       auto issue_s = [&](int j) -> bool {
         const int ks = j % K_STAGES, sb = j & 1;
-        if (!mbar_wait(&k_full[ks], (j / K_STAGES) & 1, err)) return false;
+        if (!mbar_wait(&k_full[ks], (j / K_STAGES) & 1, err, &s_abort)) return false;
         // buffer sb last held P_{j-2}: wait until PV_{j-2} has read it
-        if (!mbar_wait(&p_free[sb], ((j >> 1) & 1) ^ 1, err)) return false;
+        if (!mbar_wait(&p_free[sb], ((j >> 1) & 1) ^ 1, err, &s_abort)) return false;
         tc_fence_after();
         const uint32_t kb = sK + ks * L::K_BYTES;
 #pragma unroll
@@ -208,13 +213,13 @@ __global__ void __launch_bounds__(FWD_THREADS, 2)
         umma_commit(&k_empty[ks]);
         return true;
       };
-      bool ok = mbar_wait(q_full, 0, err);
+      bool ok = mbar_wait(q_full, 0, err, &s_abort);
       if (ok) { tc_fence_after(); ok = issue_s(0); }
       for (int j = 0; ok && j < n_kv; ++j) {
         if (j + 1 < n_kv && !issue_s(j + 1)) { ok = false; break; }
         const int sb = j & 1, vs = j % V_STAGES;
-        if (!mbar_wait(&v_full[vs], (j / V_STAGES) & 1, err)) { ok = false; break; }
-        if (!mbar_wait(&p_full[sb], (j >> 1) & 1, err)) { ok = false; break; }
+        if (!mbar_wait(&v_full[vs], (j / V_STAGES) & 1, err, &s_abort)) { ok = false; break; }
+        if (!mbar_wait(&p_full[sb], (j >> 1) & 1, err, &s_abort)) { ok = false; break; }
         tc_fence_after();
         const uint32_t vb = sV + vs * L::V_BYTES;
 #pragma unroll
@@ -236,7 +241,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 2)
     float m_run = -INFINITY, l_run = 0.f;
     for (int j = 0; j < n_kv; ++j) {
       const int sb = j & 1;
-      if (!mbar_wait(&s_full[sb], (j >> 1) & 1, err)) { s_abort = 1; break; }
+      if (!mbar_wait(&s_full[sb], (j >> 1) & 1, err, &s_abort)) { s_abort = 1; break; }
       tc_fence_after();
       float sv[AK];
       {
@@ -266,7 +271,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 2)
       const float alpha = (m_run == -INFINITY) ? 0.f : ex2_approx(m_run - m_new);
       if (__any_sync(0xffffffffu, need) && j > 0) {
         // O (TMEM) must be quiescent: wait for the PV product of tile j-1
-        if (!mbar_wait(&p_free[(j - 1) & 1], ((j - 1) >> 1) & 1, err)) { s_abort = 1; break; }
+        if (!mbar_wait(&p_free[(j - 1) & 1], ((j - 1) >> 1) & 1, err, &s_abort)) { s_abort = 1; break; }
         tc_fence_after();
         const float f = need ? alpha : 1.f;
 #pragma unroll 1
@@ -303,7 +308,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 2)
       if (lane == 0) mbar_arrive(&p_full[sb]);
     }
     // epilogue: O / l -> bf16, lse
-    if (!s_abort && mbar_wait(&p_free[(n_kv - 1) & 1], ((n_kv - 1) >> 1) & 1, err)) {
+    if (!s_abort && mbar_wait(&p_free[(n_kv - 1) & 1], ((n_kv - 1) >> 1) & 1, err, &s_abort)) {
       tc_fence_after();
       const float inv = 1.f / l_run;
       uint16_t* orow = o + static_cast<int64_t>(row_base + qrow) * s.ld_o + h * HD;
@@ -329,12 +334,21 @@ __global__ void __launch_bounds__(FWD_THREADS, 2)
 
   tc_fence_before();
   __syncthreads();
+  if (warp == 0 && lane == 0 && s_abort) {
+    // loads still in flight land before the CTA exits (bounded waits on the
+    // last arming of every buffer)
+    mbar_wait(q_full, 0, err, nullptr);
+    for (int d = 0; d < K_STAGES && d < nk; ++d)
+      mbar_wait(&k_full[(nk - 1 - d) % K_STAGES], ((nk - 1 - d) / K_STAGES) & 1, err, nullptr);
+    for (int d = 0; d < V_STAGES && d < nv; ++d)
+      mbar_wait(&v_full[(nv - 1 - d) % V_STAGES], ((nv - 1 - d) / V_STAGES) & 1, err, nullptr);
+  }
   if (warp == 1) {
     tc_fence_after();
     if (s_abort) {
       if (lane == 0) {
         umma_commit(drain);
-        mbar_wait(drain, 0, err);
+        mbar_wait(drain, 0, err, nullptr);
       }
       __syncwarp();
     }
@@ -505,6 +519,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   const uint32_t sK = smem_u32(sm + L::OFF_K), sV = smem_u32(sm + L::OFF_V);
   const uint32_t sQ = smem_u32(sm + L::OFF_Q), sDO = smem_u32(sm + L::OFF_DO);
   const uint32_t sP = smem_u32(sm + L::OFF_P), sDS = smem_u32(sm + L::OFF_DS);
+  int issued = 0;   // Q/dO items the producer issued (read on the abort path)
 
   if (warp == 0) {
     // ------------------------------ producer ------------------------------
@@ -518,7 +533,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       for (int i = 0; i < n_items && !s_abort; ++i) {
         const int st = i % QD_STAGES;
         const int h = kvh * rep + i / per_head, qt = q_first + i % per_head;
-        if (!mbar_wait(&qd_empty[st], ((i / QD_STAGES) & 1) ^ 1, err)) { s_abort = 1; break; }
+        if (!mbar_wait(&qd_empty[st], ((i / QD_STAGES) & 1) ^ 1, err, &s_abort)) { s_abort = 1; break; }
         mbar_arrive_expect_tx(&qd_full[st], 2 * L::QD_BYTES);
         for (int c = 0; c < 2; ++c) {
           tma_load_2d(sm + L::OFF_Q + st * L::QD_BYTES + c * (BQ * 128), &tm_q, &qd_full[st],
@@ -526,6 +541,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
           tma_load_2d(sm + L::OFF_DO + st * L::QD_BYTES + c * (BQ * 128), &tm_do, &qd_full[st],
                       h * HD + 64 * c, row0 + qt * BQ);
         }
+        issued = i + 1;
       }
     }
   } else if (warp == 1) {
@@ -535,8 +551,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       // once the warps have loaded item j-1's S/dP
       auto issue_sdp = [&](int j) -> bool {
         const int st = j % QD_STAGES;
-        if (!mbar_wait(&qd_full[st], (j / QD_STAGES) & 1, err)) return false;
-        if (j > 0 && !mbar_wait(sdp_free, (j - 1) & 1, err)) return false;
+        if (!mbar_wait(&qd_full[st], (j / QD_STAGES) & 1, err, &s_abort)) return false;
+        if (j > 0 && !mbar_wait(sdp_free, (j - 1) & 1, err, &s_abort)) return false;
         tc_fence_after();
         const uint32_t qb = sQ + st * L::QD_BYTES, db = sDO + st * L::QD_BYTES;
 #pragma unroll
@@ -550,12 +566,12 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         umma_commit(sdp_full);
         return true;
       };
-      bool ok = mbar_wait(kv_full, 0, err);
+      bool ok = mbar_wait(kv_full, 0, err, &s_abort);
       if (ok && n_items > 0) { tc_fence_after(); ok = issue_sdp(0); }
       for (int i = 0; ok && i < n_items; ++i) {
         if (i + 1 < n_items && !issue_sdp(i + 1)) { ok = false; break; }
         const int st = i % QD_STAGES;
-        if (!mbar_wait(p_full, i & 1, err)) { ok = false; break; }
+        if (!mbar_wait(p_full, i & 1, err, &s_abort)) { ok = false; break; }
         tc_fence_after();
         const uint32_t qb = sQ + st * L::QD_BYTES, db = sDO + st * L::QD_BYTES;
 #pragma unroll
@@ -566,7 +582,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         // dQ^T = K^T . dS^T into dQ buffer i & 1, drained (item i-2) by now:
         // A = K tile read MN-major (d contiguous, 16 KB between d blocks),
         // B = dS^T tile read MN-major (q contiguous)
-        if (!mbar_wait(&dq_free[i & 1], ((i >> 1) & 1) ^ 1, err)) { ok = false; break; }
+        if (!mbar_wait(&dq_free[i & 1], ((i >> 1) & 1) ^ 1, err, &s_abort)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int k = 0; k < BK_KEYS / 16; ++k)
@@ -629,7 +645,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         pl = lse[lse_index(i + 1)];
         pd = dsum[lse_index(i + 1)];
       }
-      if (!mbar_wait(sdp_full, i & 1, err)) { ok = false; break; }
+      if (!mbar_wait(sdp_full, i & 1, err, &s_abort)) { ok = false; break; }
       tc_fence_after();
       uint32_t pw[16], dw[16];   // P^T and dS^T row segments, packed bf16 pairs
       {
@@ -667,7 +683,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       }
       // the P^T / dS^T tiles are free once item i-1's products are done
       if (i > 0) {
-        if (!mbar_wait(mm_done, (i - 1) & 1, err)) { ok = false; break; }
+        if (!mbar_wait(mm_done, (i - 1) & 1, err, &s_abort)) { ok = false; break; }
         tc_fence_after();
       }
       // P^T and dS^T row segments -> 128-byte swizzled smem rows (16-byte
@@ -690,7 +706,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       if (i > 0) flush_dq(i - 1);
     }
     if (ok && n_items > 0) {
-      ok = mbar_wait(mm_done, (n_items - 1) & 1, err);
+      ok = mbar_wait(mm_done, (n_items - 1) & 1, err, &s_abort);
       if (ok) {
         tc_fence_after();
         flush_dq(n_items - 1);
@@ -730,12 +746,18 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
+  if (warp == 0 && lane == 0 && s_abort) {
+    // loads still in flight land before the CTA exits
+    mbar_wait(kv_full, 0, err, nullptr);
+    for (int d = 0; d < QD_STAGES && d < issued; ++d)
+      mbar_wait(&qd_full[(issued - 1 - d) % QD_STAGES], ((issued - 1 - d) / QD_STAGES) & 1, err, nullptr);
+  }
   if (warp == 1) {
     tc_fence_after();
     if (s_abort) {
       if (lane == 0) {
         umma_commit(drain);
-        mbar_wait(drain, 0, err);
+        mbar_wait(drain, 0, err, nullptr);
       }
       __syncwarp();
     }

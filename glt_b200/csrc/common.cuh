@@ -133,6 +133,14 @@ __device__ __forceinline__ float warp_max(float v) {
 // glt_device_error().  Allocated lazily once per device.
 namespace glt {
 unsigned int* device_error_word();
+// GLT_OK for code 0, else GLT_ETIMEOUT (a bounded wait ran out) or
+// GLT_EINVAL (a kernel rejected its shape), with a message naming `where`.
+int status_from_device_error(unsigned int code, const char* where);
+// Reads and clears the error word of the allocation-free graft op on the
+// current device (graft_ops_noalloc.cu); noalloc_error_word gives its device
+// address (for the failure-path self-test).
+int noalloc_error_take(unsigned int* code);
+int noalloc_error_word(unsigned int** word);
 }
 #define GLT_DEVERR_MBAR_TIMEOUT 1u
 #define GLT_DEVERR_BAD_SHAPE 2u

@@ -245,9 +245,11 @@ int Model::eval(const int32_t* ids_in, int64_t n_seq, int host, int use_graft, G
       if (use_graft) graft_calls += L;
     }
   }
+  GLT_TRY(collect_device_error(device_error_word(), d_err, &ev_acc->dev_err, st));
   GLT_CUDA_TRY(cudaMemcpyAsync(ev_pinned, ev_acc, sizeof(EvalAccum), cudaMemcpyDeviceToHost, st));
   GLT_CUDA_TRY(cudaStreamSynchronize(st));
   const EvalAccum& a = *ev_pinned;
+  GLT_TRY(status_from_device_error(a.dev_err, "glt_model_eval"));
   out->tokens = tokens;
   out->total_nll = a.nll;
   out->mean_ce = a.nll / static_cast<double>(tokens);

@@ -39,12 +39,15 @@ struct ScopedTileCounter {
   explicit ScopedTileCounter(int* c) : prev(gemm_tile_counter()) { gemm_tile_counter() = c; }
   ~ScopedTileCounter() { gemm_tile_counter() = prev; }
 };
-// Sets the dynamic-smem attribute of `func` to `bytes` once per process.
+// Sets the dynamic-smem attribute of `func` to `bytes` once per (device, function).
 int ensure_smem_attr(const void* func, int bytes);
 
 // ---------------------------------------------------------------------------
 // Launcher
 // ---------------------------------------------------------------------------
+// err: the launch's error word (default: this device's, device_error_word());
+// timeout_ns bounds every mbarrier wait; selftest_skip_first_load is the
+// failure-path self-test switch of GemmShape (0 in every product launch).
 // group_m: m-tiles per raster group.  32 keeps a 32-tile block of A (32 MB
 // at K = 4096) resident in L2 while the 148 persistent CTAs sweep N, so a
 // K = 4096 weight such as W_gu (252 MB) streams from HBM once per 32 m-tiles
@@ -54,7 +57,8 @@ template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi>
 int launch_gemm(const Operand& A, const Operand& B, int M, int N, int K, const Epi& epi,
                 cudaStream_t stream, int k_splits = 1, const Operand* A2 = nullptr,
                 int a2_n_tile = INT_MAX, int group_m = 32, const int* m_dev = nullptr,
-                int m_off = 0) {
+                int m_off = 0, unsigned int* err = nullptr, uint64_t timeout_ns = tc::GLT_MBAR_TIMEOUT_NS,
+                int selftest_skip_first_load = 0) {
   using namespace tc;
   if (M <= 0 || N <= 0 || K <= 0) return GLT_OK;
   if (A.mn_major != A_MN || B.mn_major != B_MN)
@@ -91,8 +95,10 @@ int launch_gemm(const Operand& A, const Operand& B, int M, int N, int K, const E
   shape.m_dev = m_dev;
   shape.m_off = m_off;
   shape.tile_ctr = gemm_tile_counter();
-  shape.err = device_error_word();
+  shape.err = err ? err : device_error_word();
   if (!shape.err) return fail(GLT_ECUDA, "device error word unavailable");
+  shape.timeout_ns = timeout_ns;
+  shape.selftest_skip_first_load = selftest_skip_first_load;
   auto kern = tc_gemm_kernel<BN, STAGES, A_MN, B_MN, Epi>;
   constexpr int smem = gemm_smem_bytes<BN, STAGES, Epi>();
   GLT_TRY(ensure_smem_attr(reinterpret_cast<const void*>(kern), smem));

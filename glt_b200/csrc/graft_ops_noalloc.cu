@@ -90,34 +90,34 @@ int stage(const void* src, int is_f32, int64_t ld, int rows, int cols, uint8_t* 
 template <bool AMN, bool BMN>
 int gemm_f32(const Operand& a, const Operand& b, int M, int N, int K, float* C, int64_t ldc,
              float alpha, float beta, unsigned int* err, cudaStream_t st) {
-  using namespace tc;
-  constexpr int BN = 128, STAGES = 6;
-  CUtensorMap ta, tb;
-  if (!AMN) GLT_TRY(make_tmap_bf16(&ta, a.ptr, K, M, a.ld, BM));
-  else GLT_TRY(make_tmap_bf16(&ta, a.ptr, M, K, a.ld, 64));
-  if (!BMN) GLT_TRY(make_tmap_bf16(&tb, b.ptr, K, N, b.ld, BN));
-  else GLT_TRY(make_tmap_bf16(&tb, b.ptr, N, K, b.ld, 64));
+  // the launcher shared with every other GEMM, with this entry point's own
+  // error word (launch_gemm allocates nothing when it is given one)
   const bool vec = aligned16(C) && ldc % 4 == 0 && N % 4 == 0;
-  EpiF32<BN> epi{C, ldc, M, N, alpha, beta, 0, vec ? 1 : 0};
-  GemmShape shape;
-  shape.M = M;
-  shape.N = N;
-  shape.K = K;
-  shape.k_splits = 1;
-  shape.a2_n_tile = INT_MAX;
-  shape.group_m = 8;
-  shape.err = err;
-  auto kern = tc_gemm_kernel<BN, STAGES, AMN, BMN, EpiF32<BN>>;
-  constexpr int smem = gemm_smem_bytes<BN, STAGES, EpiF32<BN>>();
-  GLT_TRY(ensure_smem_attr(reinterpret_cast<const void*>(kern), smem));
-  const int units = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-  const int grid = units < num_sms() ? units : num_sms();
-  kern<<<grid, gemm_threads<EpiF32<BN>>(), smem, st>>>(ta, ta, tb, shape, epi);
-  GLT_LAUNCH_CHECK();
-  return GLT_OK;
+  EpiF32<128> epi{C, ldc, M, N, alpha, beta, 0, vec ? 1 : 0};
+  return launch_gemm<128, 6, AMN, BMN>(a, b, M, N, K, epi, st, 1, nullptr, INT_MAX, 32, nullptr, 0, err);
 }
 
 }  // namespace
+
+int noalloc_error_word(unsigned int** word) {
+  Slots slots;
+  GLT_TRY(device_slots(&slots));
+  *word = slots.err;
+  return GLT_OK;
+}
+
+int noalloc_error_take(unsigned int* code) {
+  // a symbol copy allocates nothing; the word is this file's, per device
+  unsigned int v = 0;
+  GLT_CUDA_TRY(cudaMemcpyFromSymbol(&v, g_noalloc_err, sizeof(v)));
+  if (v) {
+    const unsigned int zero = 0;
+    GLT_CUDA_TRY(cudaMemcpyToSymbol(g_noalloc_err, &zero, sizeof(zero)));
+  }
+  *code = v;
+  return GLT_OK;
+}
+
 }  // namespace glt
 
 extern "C" int glt_graft_op_noalloc(int op, int M, int S, int H, const float* w_f32,

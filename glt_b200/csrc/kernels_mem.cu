@@ -791,6 +791,24 @@ int grad_clip_scale(const float* grad, int64_t n, float clip_norm, float gscale,
   return GLT_OK;
 }
 
+__global__ void collect_error_kernel(unsigned int* word, unsigned int* accum, unsigned int* dst) {
+  const unsigned int v = *word | *accum;
+  *word = 0u;
+  if (dst) {
+    *dst = v;
+    *accum = 0u;
+  } else {
+    *accum = v;
+  }
+}
+
+int collect_device_error(unsigned int* word, unsigned int* accum, unsigned int* dst, cudaStream_t st) {
+  if (!word || !accum) return fail(GLT_ECUDA, "device error word unavailable");
+  collect_error_kernel<<<1, 1, 0, st>>>(word, accum, dst);
+  GLT_LAUNCH_CHECK();
+  return GLT_OK;
+}
+
 int set_clip_scale(DevStats* stats, float v, cudaStream_t st) {
   set_scalar_kernel<<<1, 1, 0, st>>>(&stats->clip_scale, v);
   GLT_LAUNCH_CHECK();

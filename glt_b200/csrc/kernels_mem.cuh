@@ -34,7 +34,8 @@ struct DevStats {
   float lambda_eff;         // lambda / (ood_count * active_grafts) or 0
   float clip_scale;         // global-norm clip factor
   float lm_loss, silence, domain_energy, ood_energy, ratio, total_loss, grad_norm;
-  float pad[3];
+  unsigned int dev_err;     // device error word collected at the end of the step
+  float pad[2];
 };
 
 // Counts domain label positions and OOD tokens.
@@ -62,6 +63,10 @@ int silence_stats(const float* esq, const int* proj_enabled /*[L*3] dev*/, int L
 int mse_grad(const uint16_t* out, const float* y, float* dx, DevStats* stats, int M, int D,
              cudaStream_t st);
 int set_clip_scale(DevStats* stats, float v, cudaStream_t st);
+// Stream-ordered collection of the device error word (kernels that give up a
+// bounded wait set it): v = *word | *accum, then *word = 0; with dst, *dst = v
+// and *accum = 0, else *accum = v.  No host synchronisation.
+int collect_device_error(unsigned int* word, unsigned int* accum, unsigned int* dst, cudaStream_t st);
 // Finalises losses and lambda_eff on the device (grafting.hip:1097-1117).
 int finalize_loss(DevStats* stats, float lambda_silence, int active_grafts, float lm_loss_scale,
                   cudaStream_t st);

@@ -406,6 +406,7 @@ int Model::allocate() {
     add(reinterpret_cast<void**>(&dys), b2 * M * 2 * static_cast<size_t>(S));
   }
   add(reinterpret_cast<void**>(&stats), sizeof(DevStats));
+  add(reinterpret_cast<void**>(&d_err), sizeof(unsigned int));   // zeroed with the arena
   add(reinterpret_cast<void**>(&tile_ctr), 2 * sizeof(int));   // zeroed with the arena
   add(reinterpret_cast<void**>(&d_enabled), sizeof(int) * 3 * L);
   add(reinterpret_cast<void**>(&d_gu_ptrs), sizeof(void*) * L);
@@ -875,7 +876,10 @@ int Model::finish_step(int step, int total_steps, GltStepStats* out, cudaStream_
   GLT_PROF(GLT_PROF_ADAMW, adamw_step(gw, grad, adam_m, adam_v, L, S, H, lr, cfg.adam_beta1, cfg.adam_beta2,
                      cfg.adam_eps, cfg.adam_weight_decay, step, kinds, stats, &mt, st));
   // The step's stats go to a pinned slot without a host sync; the next step
-  // overwrites the device copy, two steps later the slot is reused.
+  // overwrites the device copy, two steps later the slot is reused.  The
+  // device error word travels with them (any kernel of this step, or of an
+  // earlier forward, that gave up a bounded wait).
+  GLT_TRY(collect_device_error(device_error_word(), d_err, &stats->dev_err, st));
   const int slot = step & 1;
   GLT_CUDA_TRY(cudaMemcpyAsync(pinned_stats + slot, stats, sizeof(DevStats), cudaMemcpyDeviceToHost, st));
   GLT_CUDA_TRY(cudaEventRecord(stats_ev[slot], st));
@@ -898,7 +902,7 @@ int Model::step_stats(int step, GltStepStats* out) {
   out->total_loss = s.total_loss;
   out->lr = stats_lr[slot];
   out->grad_norm = s.grad_norm;
-  return GLT_OK;
+  return status_from_device_error(s.dev_err, "glt_train_step");
 }
 
 int Model::forward_logits(const int32_t* ids_in, int host, int use_graft, uint16_t* out,
@@ -911,7 +915,9 @@ int Model::forward_logits(const int32_t* ids_in, int host, int use_graft, uint16
   GLT_TRY(forward_all(use_graft != 0, st));
   if (out)
     GLT_TRY(g_bf16(kmaj(xf, D), kmaj(lm_head, D), M, V, D, out, V, nullptr, 0, st));
-  return GLT_OK;
+  // no host sync here: a timeout is reported by the model's next call that
+  // reads results back
+  return collect_device_error(device_error_word(), d_err, nullptr, st);
 }
 
 int Model::block_step(const uint16_t* x, const float* y_t, float lr, int step, float* loss,
@@ -940,11 +946,13 @@ int Model::block_step(const uint16_t* x, const float* y_t, float lr, int step, f
   GLT_PROF(GLT_PROF_ADAMW, adamw_step(gw, grad, adam_m, adam_v, L, S, H, lr, cfg.adam_beta1, cfg.adam_beta2,
                      cfg.adam_eps, cfg.adam_weight_decay, step, kinds, stats, &mt, st));
   if (loss) {
+    GLT_TRY(collect_device_error(device_error_word(), d_err, &stats->dev_err, st));
     GLT_CUDA_TRY(cudaMemcpyAsync(pinned_stats, stats, sizeof(DevStats), cudaMemcpyDeviceToHost, st));
     GLT_CUDA_TRY(cudaStreamSynchronize(st));
     *loss = static_cast<float>(pinned_stats->ce_sum / (static_cast<double>(M) * D));
+    return status_from_device_error(pinned_stats->dev_err, "glt_block_step");
   }
-  return GLT_OK;
+  return collect_device_error(device_error_word(), d_err, nullptr, st);
 }
 
 int Model::activation(int which, int layer, void** ptr, int64_t* numel) {

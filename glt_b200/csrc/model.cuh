@@ -41,6 +41,8 @@ struct Layer {
 struct EvalAccum {
   double nll, sum, sumsq;
   uint64_t hash;
+  unsigned int dev_err;   // device error word collected at the end of the eval
+  unsigned int pad;
 };
 
 struct Model {
@@ -113,6 +115,11 @@ struct Model {
   int32_t* ids = nullptr;
   int32_t* ood = nullptr;
   float last_lr = 0.f;
+  // Device error codes of this model's calls that return without a host
+  // sync (glt_forward, a pipelined glt_train_step), held until the next call
+  // that reads its results back reports them (glt_model_step_stats, eval, a
+  // block step with its loss).
+  unsigned int* d_err = nullptr;
   // GEMM tile-claim counter of this model's stream, used with
   // GLT_GEMM_SCHEDULE=dynamic (default static: round-robin units)
   int* tile_ctr = nullptr;

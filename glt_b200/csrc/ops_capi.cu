@@ -3,7 +3,6 @@
 #include <math.h>
 
 #include <mutex>
-#include <unordered_map>
 #include <vector>
 
 #include "attention.cuh"
@@ -14,31 +13,37 @@ namespace glt {
 int flash_fwd_tc(const uint16_t* qkv, uint16_t* o, float* lse, const AttnShape& s, cudaStream_t st);
 
 namespace {
-// RoPE cos/sin tables cached per (device, T, hd, theta).
-struct RopeKey {
+// RoPE cos/sin tables cached per (device, T, hd, theta), at most kRopeCache
+// entries per process: the oldest is freed when a new one is needed
+// (cudaFree waits for the device, so no kernel still reads it).
+constexpr size_t kRopeCache = 8;
+struct RopeEntry {
   int dev, T, hd;
   float theta;
-  bool operator==(const RopeKey& o) const { return dev == o.dev && T == o.T && hd == o.hd && theta == o.theta; }
-};
-struct RopeHash {
-  size_t operator()(const RopeKey& k) const {
-    return std::hash<long long>()(((long long)k.dev << 48) ^ ((long long)k.T << 20) ^ k.hd) ^
-           std::hash<float>()(k.theta);
-  }
+  float* c;
+  float* s;
 };
 std::mutex g_rope_mu;
-std::unordered_map<RopeKey, std::pair<float*, float*>, RopeHash> g_rope;
+std::vector<RopeEntry> g_rope;   // oldest first
 
 int rope_tables(int T, int hd, float theta, float** c, float** s) {
   int dev = 0;
-  cudaGetDevice(&dev);
+  GLT_CUDA_TRY(cudaGetDevice(&dev));
   std::lock_guard<std::mutex> lk(g_rope_mu);
-  RopeKey k{dev, T, hd, theta};
-  auto it = g_rope.find(k);
-  if (it != g_rope.end()) {
-    *c = it->second.first;
-    *s = it->second.second;
-    return GLT_OK;
+  for (const RopeEntry& e : g_rope)
+    if (e.dev == dev && e.T == T && e.hd == hd && e.theta == theta) {
+      *c = e.c;
+      *s = e.s;
+      return GLT_OK;
+    }
+  if (g_rope.size() >= kRopeCache) {
+    const RopeEntry& old = g_rope.front();
+    int cur = dev;
+    GLT_CUDA_TRY(cudaSetDevice(old.dev));
+    cudaFree(old.c);
+    cudaFree(old.s);
+    GLT_CUDA_TRY(cudaSetDevice(cur));
+    g_rope.erase(g_rope.begin());
   }
   const int half = hd / 2;
   std::vector<float> hc(static_cast<size_t>(T) * half), hs(hc.size());
@@ -51,10 +56,13 @@ int rope_tables(int T, int hd, float theta, float** c, float** s) {
   }
   float *dc = nullptr, *ds = nullptr;
   GLT_CUDA_TRY(cudaMalloc(&dc, hc.size() * 4));
-  GLT_CUDA_TRY(cudaMalloc(&ds, hs.size() * 4));
+  if (cudaMalloc(&ds, hs.size() * 4) != cudaSuccess) {
+    cudaFree(dc);
+    return fail(GLT_ENOMEM, "glt_rope: table allocation failed");
+  }
   GLT_CUDA_TRY(cudaMemcpy(dc, hc.data(), hc.size() * 4, cudaMemcpyHostToDevice));
   GLT_CUDA_TRY(cudaMemcpy(ds, hs.data(), hs.size() * 4, cudaMemcpyHostToDevice));
-  g_rope[k] = {dc, ds};
+  g_rope.push_back(RopeEntry{dev, T, hd, theta, dc, ds});
   *c = dc;
   *s = ds;
   return GLT_OK;

@@ -9,8 +9,10 @@
 #include <string.h>
 
 #include <atomic>
+#include <map>
 #include <mutex>
 #include <unordered_map>
+#include <utility>
 
 #include "common.cuh"
 #include "gemm.cuh"
@@ -67,15 +69,27 @@ int num_sms() {
 }
 
 int ensure_smem_attr(const void* func, int bytes) {
-  static std::unordered_map<const void*, int> done;
+  // cudaFuncSetAttribute applies to the current device only: key by both
+  int dev = 0;
+  GLT_CUDA_TRY(cudaGetDevice(&dev));
+  static std::map<std::pair<int, const void*>, int> done;
   std::lock_guard<std::mutex> lk(g_mu);
-  auto it = done.find(func);
+  const auto key = std::make_pair(dev, func);
+  auto it = done.find(key);
   if (it != done.end() && it->second >= bytes) return GLT_OK;
   cudaError_t e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   if (e != cudaSuccess)
     return fail(GLT_ECUDA, "cudaFuncSetAttribute(smem=%d): %s", bytes, cudaGetErrorString(e));
-  done[func] = bytes;
+  done[key] = bytes;
   return GLT_OK;
+}
+
+int status_from_device_error(unsigned int code, const char* where) {
+  if (code == 0) return GLT_OK;
+  if (code & GLT_DEVERR_MBAR_TIMEOUT)
+    return fail(GLT_ETIMEOUT, "%s: a kernel gave up a bounded device wait (device error word 0x%x); "
+                "its outputs are incomplete", where, code);
+  return fail(GLT_EINVAL, "%s: a kernel rejected its shape (device error word 0x%x)", where, code);
 }
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
@@ -154,8 +168,49 @@ extern "C" int glt_device_error(unsigned int* out_code) {
   unsigned int v = 0;
   GLT_CUDA_TRY(cudaMemcpy(&v, w, sizeof(v), cudaMemcpyDeviceToHost));
   GLT_CUDA_TRY(cudaMemset(w, 0, sizeof(v)));
-  if (out_code) *out_code = v;
+  // the allocation-free graft op keeps its own word (it may not allocate one)
+  unsigned int v2 = 0;
+  GLT_TRY(noalloc_error_take(&v2));
+  if (out_code) *out_code = v | v2;
   return GLT_OK;
+}
+
+// Failure-path self-test: a small GEMM whose CTA 0 never receives its first
+// k-block, so that CTA's bounded waits run out after timeout_ms; nothing else
+// is skipped.  mode 0 reads and clears the device word like any call; mode 1
+// leaves the code pending in it; mode 2 writes it to the allocation-free graft
+// op's own word instead (left pending for glt_device_error).
+extern "C" int glt_selftest_wait_timeout(int timeout_ms, int mode, void* stream) {
+  if (timeout_ms < 1 || timeout_ms > 2000) return fail(GLT_EINVAL, "selftest: timeout_ms in [1, 2000]");
+  if (mode < 0 || mode > 2) return fail(GLT_EINVAL, "selftest: mode 0, 1 or 2");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  unsigned int* w = nullptr;
+  if (mode == 2) {
+    GLT_TRY(noalloc_error_word(&w));
+  } else {
+    w = device_error_word();
+    if (!w) return fail(GLT_ECUDA, "no device error word");
+  }
+  constexpr int n = 256;
+  void* buf = nullptr;
+  GLT_CUDA_TRY(cudaMalloc(&buf, 3 * n * n * 4));
+  uint16_t* a = static_cast<uint16_t*>(buf);
+  uint16_t* b = a + n * n;
+  float* c = reinterpret_cast<float*>(b + n * n);
+  int rc = GLT_OK;
+  if (cudaMemsetAsync(buf, 0, 3 * n * n * 4, st) != cudaSuccess) rc = fail(GLT_ECUDA, "selftest: memset failed");
+  if (rc == GLT_OK) {
+    EpiF32<128> e{c, n, n, n, 1.f, 0.f, 0, 1};
+    rc = launch_gemm<128, 6, false, false>(Operand{a, n, false}, Operand{b, n, false}, n, n, n, e, st, 1,
+                                            nullptr, INT_MAX, 32, nullptr, 0, w,
+                                            static_cast<uint64_t>(timeout_ms) * 1000000ull, 1);
+  }
+  if (cudaStreamSynchronize(st) != cudaSuccess && rc == GLT_OK) rc = fail(GLT_ECUDA, "selftest: sync failed");
+  cudaFree(buf);
+  if (rc != GLT_OK || mode != 0) return rc;
+  unsigned int v = 0;
+  GLT_TRY(glt_device_error(&v));
+  return status_from_device_error(v, "glt_selftest_wait_timeout");
 }
 
 extern "C" int glt_launch_count(uint64_t* out) {

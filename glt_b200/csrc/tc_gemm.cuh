@@ -31,9 +31,12 @@
 // collective) takes fewer tiles instead of finishing last.  Every TMA load is a plain per-CTA load into
 // the CTA's own shared memory, so the kernel is safe in multi-GPU jobs.
 //
-// Every mbarrier wait is bounded (GLT_MBAR_TIMEOUT_NS of %globaltimer);
-// a timed-out wait records GLT_DEVERR_MBAR_TIMEOUT in the device error word
-// and the CTA drains out instead of hanging the GPU.
+// Every mbarrier wait is bounded (GemmShape::timeout_ns of %globaltimer,
+// GLT_MBAR_TIMEOUT_NS by default); a timed-out wait records
+// GLT_DEVERR_MBAR_TIMEOUT in the launch's error word and sets the CTA's abort
+// flag, on which every other role of the CTA gives up its own wait; the CTA
+// then waits (bounded) for its loads in flight and its issued MMAs, frees its
+// TMEM and exits, instead of hanging the GPU.
 #pragma once
 
 #include <cuda.h>
@@ -88,8 +91,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait.  Returns false (and records the error) after the timeout.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int* err) {
+// Bounded wait.  Returns false after `timeout_ns` of %globaltimer (and
+// records GLT_DEVERR_MBAR_TIMEOUT in *err), or as soon as *abort (a flag in
+// the CTA's own shared memory, nullable) is set by another role of the same
+// CTA that gave up first.  Nothing outside the CTA is consulted, so a timeout
+// in one launch never shortens the waits of a later one.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int* err,
+                                          const volatile int* abort = nullptr,
+                                          uint64_t timeout_ns = GLT_MBAR_TIMEOUT_NS) {
   const uint32_t addr = smem_u32(bar);
   if (mbar_try_wait(addr, parity)) return true;
   const uint64_t t0 = globaltimer();
@@ -97,12 +106,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
 #pragma unroll 1
     for (int i = 0; i < 256; ++i)
       if (mbar_try_wait(addr, parity)) return true;
-    if (globaltimer() - t0 > GLT_MBAR_TIMEOUT_NS) {
+    if (globaltimer() - t0 > timeout_ns) {
       if (err) atomicOr(err, GLT_DEVERR_MBAR_TIMEOUT);
       return false;
     }
-    // Another role may already have given up.
-    if (err && *(volatile unsigned int*)err != 0u) return false;
+    if (abort && *abort != 0) return false;
   }
 }
 
@@ -243,6 +251,12 @@ struct GemmShape {
   // last CTA to finish sets them back to zero for the next launch on the
   // stream.  One counter pair per stream (launches on it must not overlap).
   int* tile_ctr = nullptr;
+  // Bound of every mbarrier wait of the launch.
+  uint64_t timeout_ns = GLT_MBAR_TIMEOUT_NS;
+  // Failure-path self-test only (glt_selftest_wait_timeout): CTA 0's
+  // producer never arms or loads its first k-block, so that CTA's MMA wait
+  // runs out and the CTA takes the abort path.  0 in every product launch.
+  int selftest_skip_first_load = 0;
 };
 
 constexpr int UNIT_RING = 4;   // work units in flight between the producer and the consumers
@@ -398,6 +412,10 @@ __global__ void __launch_bounds__(gemm_threads<Epi>(), 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // producer state read again on the abort path: k-blocks issued, and the one
+  // never armed by the failure-path self-test (-1: none)
+  int p_issued = 0;
+  const int skip_it = (shape.selftest_skip_first_load && blockIdx.x == 0) ? 0 : -1;
 
   if (warp == 0) {
     // ------------------------------ TMA producer ------------------------------
@@ -413,7 +431,10 @@ __global__ void __launch_bounds__(gemm_threads<Epi>(), 1)
       for (int t = 0; !s_abort; ++t) {
         // publish this CTA's next unit (-1: none left) to the MMA and epilogue warps
         const int slot = t % UNIT_RING;
-        if (!mbar_wait(&uempty_bar[slot], ((t / UNIT_RING) & 1) ^ 1, shape.err)) { s_abort = 1; break; }
+        if (!mbar_wait(&uempty_bar[slot], ((t / UNIT_RING) & 1) ^ 1, shape.err, &s_abort, shape.timeout_ns)) {
+          s_abort = 1;
+          break;
+        }
         const int unit = claim < units ? claim : -1;
         unit_ring[slot] = unit;
         mbar_arrive(&ufull_bar[slot]);
@@ -429,7 +450,8 @@ __global__ void __launch_bounds__(gemm_threads<Epi>(), 1)
         for (int k0 = k_begin; k0 < k_end; k0 += BK, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
-          if (!mbar_wait(&empty_bar[s], ph ^ 1, shape.err)) { s_abort = 1; break; }
+          if (!mbar_wait(&empty_bar[s], ph ^ 1, shape.err, &s_abort, shape.timeout_ns)) { s_abort = 1; break; }
+          if (it == skip_it) continue;
           uint8_t* a_tile = tiles + s * L::STAGE_BYTES;
           uint8_t* b_tile = a_tile + L::A_BYTES;
           mbar_arrive_expect_tx(&full_bar[s], L::STAGE_BYTES);
@@ -449,6 +471,7 @@ __global__ void __launch_bounds__(gemm_threads<Epi>(), 1)
           }
         }
       }
+      p_issued = it;
       if (ctr) {
         // every claim of this CTA is done; the last CTA out re-arms the counter
         __threadfence();
@@ -464,7 +487,10 @@ __global__ void __launch_bounds__(gemm_threads<Epi>(), 1)
       int it = 0;
       for (int local = 0; !s_abort; ++local) {
         const int slot = local % UNIT_RING;
-        if (!mbar_wait(&ufull_bar[slot], (local / UNIT_RING) & 1, shape.err)) { s_abort = 1; break; }
+        if (!mbar_wait(&ufull_bar[slot], (local / UNIT_RING) & 1, shape.err, &s_abort, shape.timeout_ns)) {
+          s_abort = 1;
+          break;
+        }
         const int unit = unit_ring[slot];
         mbar_arrive(&uempty_bar[slot]);
         if (unit < 0) break;
@@ -473,7 +499,10 @@ __global__ void __launch_bounds__(gemm_threads<Epi>(), 1)
         const int k_begin = split * k_chunk;
         const int k_end = min(shape.K, k_begin + k_chunk);
         const int buf = local & 1;
-        if (!mbar_wait(&tempty_bar[buf], ((local >> 1) & 1) ^ 1, shape.err)) { s_abort = 1; break; }
+        if (!mbar_wait(&tempty_bar[buf], ((local >> 1) & 1) ^ 1, shape.err, &s_abort, shape.timeout_ns)) {
+          s_abort = 1;
+          break;
+        }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * BN);
         uint32_t acc = 0;
@@ -481,7 +510,7 @@ __global__ void __launch_bounds__(gemm_threads<Epi>(), 1)
         for (int k0 = k_begin; k0 < k_end; k0 += BK, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
-          if (!mbar_wait(&full_bar[s], ph, shape.err)) { ok = false; break; }
+          if (!mbar_wait(&full_bar[s], ph, shape.err, &s_abort, shape.timeout_ns)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a_addr = smem_u32(tiles + s * L::STAGE_BYTES);
           const uint32_t b_addr = a_addr + L::A_BYTES;
@@ -507,7 +536,8 @@ __global__ void __launch_bounds__(gemm_threads<Epi>(), 1)
     for (int local = 0;; ++local) {
       if (__shfl_sync(0xffffffffu, static_cast<int>(s_abort), 0)) break;
       const int slot = local % UNIT_RING;
-      if (!__all_sync(0xffffffffu, mbar_wait(&ufull_bar[slot], (local / UNIT_RING) & 1, shape.err))) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&ufull_bar[slot], (local / UNIT_RING) & 1, shape.err, &s_abort,
+                                             shape.timeout_ns))) {
         s_abort = 1;
         break;
       }
@@ -518,7 +548,8 @@ __global__ void __launch_bounds__(gemm_threads<Epi>(), 1)
       int mt, nt, split;
       unit_coords(unit, shape, num_m, num_n, mt, nt, split);
       const int buf = local & 1;
-      if (!__all_sync(0xffffffffu, mbar_wait(&tfull_bar[buf], (local >> 1) & 1, shape.err))) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull_bar[buf], (local >> 1) & 1, shape.err, &s_abort,
+                                             shape.timeout_ns))) {
         s_abort = 1;
         break;
       }
@@ -542,13 +573,25 @@ __global__ void __launch_bounds__(gemm_threads<Epi>(), 1)
 
   tc_fence_before();
   __syncthreads();
+  if (warp == 0 && lane == 0 && s_abort) {
+    // Abort path: loads this thread issued may still be landing in shared
+    // memory.  Wait (bounded) for the last arming of every stage -- k-block
+    // p_issued - 1 - d filled stage (p_issued - 1 - d) % STAGES -- before
+    // the CTA exits.
+    for (int d = 0; d < STAGES && d < p_issued; ++d) {
+      const int j = p_issued - 1 - d;
+      if (j == skip_it) continue;
+      mbar_wait(&full_bar[j % STAGES], (j / STAGES) & 1, shape.err, nullptr, shape.timeout_ns);
+    }
+  }
   if (warp == 1) {
     tc_fence_after();
     if (s_abort) {
-      // Abort path: make sure no issued MMA still writes TMEM before freeing it.
+      // Abort path: make sure no issued MMA still writes TMEM before freeing it
+      // (a bounded wait that ignores the abort flag).
       if (lane == 0) {
         umma_commit(drain_bar);
-        mbar_wait(drain_bar, 0, shape.err);
+        mbar_wait(drain_bar, 0, shape.err, nullptr, shape.timeout_ns);
       }
       __syncwarp();
     }

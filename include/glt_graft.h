@@ -45,7 +45,7 @@ typedef enum GltStatus {
   GLT_ECUDA = 2,    /* CUDA runtime or driver error                       */
   GLT_ENCCL = 3,    /* NCCL error                                         */
   GLT_EIO = 4,      /* file I/O or format error                           */
-  GLT_ETIMEOUT = 5, /* a bounded device wait gave up (see glt_device_error) */
+  GLT_ETIMEOUT = 5, /* a kernel gave up a bounded device wait (glt_device_error) */
   GLT_ESTATE = 6,   /* call not legal in the current state (e.g. double bake) */
   GLT_ENOMEM = 7    /* allocation failed                                  */
 } GltStatus;
@@ -54,9 +54,29 @@ typedef enum GltStatus {
 GLT_API const char* glt_last_error(void);
 /* Library version string. */
 GLT_API const char* glt_version(void);
-/* Reads and clears the device error word of the current device
- * (1 = mbarrier wait timed out, 2 = bad shape seen by a kernel). */
+/* Reads and clears the device error words of the current device (the one
+ * every kernel uses and the one of glt_graft_op_noalloc): 1 = a bounded
+ * mbarrier wait ran out, 2 = a kernel saw a bad shape.  Synchronises.
+ * The model calls report these codes themselves: glt_model_step_stats (and
+ * glt_train_step with stats), glt_model_eval and glt_block_step with a loss
+ * collect the word on their stream at the end of the work they read back
+ * (also covering the model's earlier glt_forward calls and pipelined steps)
+ * and return GLT_ETIMEOUT (code 1) or GLT_EINVAL (code 2) with the results.
+ * A kernel that gives up a wait leaves its outputs incomplete, writes the
+ * code, waits for its own copies and tensor-core work in flight, frees its
+ * tensor memory and exits; the next launch starts clean (no code is
+ * consulted by later launches).  The reference throws from its CHECK macros
+ * (src/checks.hpp:10-44). */
 GLT_API int glt_device_error(unsigned int* out_code);
+/* Failure-path self-test (no counterpart in the reference): runs one small
+ * GEMM in which CTA 0 never receives its first k-block, so that CTA's waits
+ * run out after timeout_ms (1..2000) and it takes the abort path above; the
+ * other CTAs finish normally.  mode 0: reads and clears the device word and
+ * returns GLT_ETIMEOUT (the expected result); mode 1: returns GLT_OK and
+ * leaves the code in the device word for the next model call to report;
+ * mode 2: the same with the word of glt_graft_op_noalloc, which
+ * glt_device_error reports.  Synchronises. */
+GLT_API int glt_selftest_wait_timeout(int timeout_ms, int mode, void* stream);
 /* Copies `bytes` between any host/device pointers on `stream` (cudaMemcpyDefault);
  * synchronises the stream when sync != 0.  Lets bindings move data in and out
  * of library-owned buffers without their own CUDA runtime binding. */

@@ -6,7 +6,10 @@ Through the C ABI, each op is run twice in a row with different inputs and
 compared with glt_graft_op (which stages in a caller-allocated GltArena):
 the same kernel on the same operands, so the results agree within the
 graft-op tolerance of tests/test_gpu_graft_ops.py.  Also checks that a
-request beyond the fixed 16 MiB workspace is refused with a clear error.
+request beyond the fixed 16 MiB workspace is refused with a clear error,
+that repeated calls leave the device memory in use unchanged (the property
+the entry point exists for), and that a timeout recorded in its own error
+word is reported once by glt_device_error and then cleared.
 This file needs no fixture from other test files; it runs alone or last."""
 import ctypes as C
 
@@ -72,3 +75,40 @@ def test_noalloc_rejects_oversize_workspace():
                                   1.0, 0.0, None)
     assert st == 1
     assert "16777216-byte workspace" in _lib.last_error()
+
+
+def used_bytes():
+    used = C.c_int64()
+    _lib.check(lib.glt_device_memory(C.byref(used), None))
+    return used.value
+
+
+def test_noalloc_calls_leave_device_memory_unchanged():
+    M, S, H = 513, 256, 1024        # fp32 weight and fp32 dy: both staged in the workspace
+    cases = [operands(code, M, S, H, seed=7 + code) for code in OPS]
+    outs = [base.clone() for (_, _, _, base) in cases]
+    for code in OPS:   # first calls: symbol lookup and lazy loading of each kernel variant
+        _lib.check(call("noalloc", code, M, S, H, *cases[code][:3], outs[code]))
+    torch.cuda.synchronize()
+    before = used_bytes()
+    for rep in range(3):
+        for code in OPS:
+            W, x, dy, _ = cases[code]
+            _lib.check(call("noalloc", code, M, S, H, W, x, dy, outs[code]))
+    torch.cuda.synchronize()
+    assert used_bytes() == before
+
+
+def test_noalloc_error_word_is_reported_then_cleared():
+    s = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    v = C.c_uint()
+    _lib.check(lib.glt_device_error(C.byref(v)))
+    assert v.value == 0
+    # a GEMM that times out against this entry point's own word (mode 2)
+    _lib.check(lib.glt_selftest_wait_timeout(20, 2, s))
+    _lib.check(lib.glt_device_error(C.byref(v)))
+    assert v.value == 1
+    _lib.check(lib.glt_device_error(C.byref(v)))
+    assert v.value == 0
+    # the word is not sticky: the next calls wait their full bound and agree
+    test_noalloc_matches_arena_op_twice(1, 257, 96, 136)

@@ -1,4 +1,4 @@
-"""Causal GQA attention microbench (the attention of the config-3 decoder layer).
+"""Causal GQA attention microbench (default: the attention of the Llama-3-8B decoder layer).
 
     python -m glt_b200.attn_bench [--batch 16] [--seq 2048] [--heads 32] [--kv-heads 8]
                                   [--head-dim 128] [--impl tc|mma] [--steps 10] [--warmup 3]
@@ -34,7 +34,7 @@ def run(B: int, T: int, nh: int, nkv: int, hd: int, impl: int, steps: int, warmu
     lse = torch.empty(B, nh, T, device=dev)
     dout = torch.randn(B * T, nh * hd, device=dev, generator=g).to(torch.bfloat16)
     dqkv = torch.zeros_like(qkv)
-    dq_acc = torch.empty(B * T, nh * hd, device=dev)
+    dq_acc = torch.empty(B * T * (nh + 2 * nkv) * hd, device=dev)   # dQ (+ dK/dV at hd 64, tcgen05)
     dsum = torch.empty(B * nh * T, device=dev)
     stream = torch.cuda.current_stream()
     sp = C.c_void_p(stream.cuda_stream)
@@ -73,7 +73,8 @@ def run(B: int, T: int, nh: int, nkv: int, hd: int, impl: int, steps: int, warmu
             "impl": "tcgen05" if impl == 0 else "mma.sync",
             "fwd_ms": ms_f, "fwd_tflops": flops_f / (ms_f / 1e3) / 1e12,
             "bwd_ms": ms_b, "bwd_tflops": flops_b / (ms_b / 1e3) / 1e12,
-            "bwd_includes": "dsum prep + fp32 dQ reduce + dQ convert", "device_error": dev_err.value}
+            "bwd_includes": "dsum prep + fp32 dQ (hd 64: and dK/dV) reduce + bf16 convert",
+            "device_error": dev_err.value}
 
 
 def main(argv=None) -> int:

@@ -40,6 +40,14 @@ int flash_bwd(const uint16_t* qkv, const uint16_t* o, const uint16_t* dout, cons
 int flash_bwd_tc(const uint16_t* qkv, const uint16_t* o, const uint16_t* dout, const float* lse,
                  uint16_t* dqkv, float* dq_acc, float* dsum, const AttnShape& s, cudaStream_t st,
                  bool dsum_ready = false, const float* rope_cos = nullptr, const float* rope_sin = nullptr);
+// tcgen05/TMEM backward for head_dim 64 (attention_tc.cu; seq_len % 128 == 0):
+// same outputs as flash_bwd.  acc is an fp32 workspace of
+// B*T*(nh + 2*nkv)*hd floats (dQ, then dK and dV accumulated over the GQA
+// heads).  rope_cos/sin (nullable, [T, hd/2]): the inverse RoPE of the q and
+// k columns is applied before their bf16 rounding (no separate RoPE pass).
+int flash_bwd_tc64(const uint16_t* qkv, const uint16_t* o, const uint16_t* dout, const float* lse,
+                   uint16_t* dqkv, float* acc, float* dsum, const AttnShape& s, cudaStream_t st,
+                   bool dsum_ready = false, const float* rope_cos = nullptr, const float* rope_sin = nullptr);
 // Shared pre/post steps of both backward kernels: zero dq_acc and compute
 // dsum = rowsum(dO * O) (unless dsum_ready); convert dq_acc (fp32) into the
 // q columns of dqkv, with the inverse RoPE when tables are given.

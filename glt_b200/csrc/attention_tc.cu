@@ -765,6 +765,388 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Backward for head_dim 64.  The head_dim-128 plan above would give the dQ^T
+// product M = hd = 64, below the 128 rows a single-CTA tcgen05.mma needs;
+// here items are 128 queries, so every product has M = 128 and dQ itself
+// (not its transpose) comes out of the tensor core:
+//   S^T  = K . Q^T      dP^T = V . dO^T        (M=128 keys, N=128 q, K=64 d)
+//   compute warps (thread = key row): P^T, dS^T as above, bf16 to smem
+//   dV  += P^T . dO     dK  += dS^T . Q        (M=128 keys, N=64 d,  K=128 q)
+//   dQ   = dS  . K                             (M=128 q,    N=64 d,  K=128 keys;
+//                                               A = the dS^T tile read MN-major)
+// One CTA per (query head, batch, 128-key tile), grid z = key tile so the
+// CTAs with the most causal items (key tile 0) start first.  Each CTA covers
+// one query head only, so the GQA heads of a KV head run in parallel and
+// their dK/dV are added into an fp32 accumulator [B*T, 2 * nkv * 64] with
+// TMA reduce-adds (as dQ is), then converted to bf16 with the inverse RoPE
+// of dq and dk applied before the rounding.
+// TMEM: S^T [0, 128), dP^T [128, 256), dQ buffers [256, 320) and [320, 384),
+// dV [384, 448), dK [448, 512).  Eight compute warps: warp (quarter, half)
+// owns TMEM lanes [32 quarter, +32) and query columns [64 half, +64) of
+// S/dP, and d columns [32 half, +32) of dQ/dK/dV.  Staging tiles for the
+// reduce-adds are [32 rows][32 fp32] in the 128-byte swizzle (16-byte chunk
+// c of row r at chunk c ^ (r & 7): conflict-free row-per-lane stores).
+// ---------------------------------------------------------------------------
+constexpr int B64_ROWS = 128;      // keys per CTA and queries per item
+constexpr int B64_STAGES = 3;      // Q/dO ring depth
+
+struct Bwd64Smem {
+  static constexpr uint32_t TILE = B64_ROWS * 64 * 2;        // [128 rows][64 bf16] = 16 KB
+  static constexpr uint32_t OFF_K = 0;
+  static constexpr uint32_t OFF_V = OFF_K + TILE;
+  static constexpr uint32_t OFF_Q = OFF_V + TILE;                  // [B64_STAGES]
+  static constexpr uint32_t OFF_DO = OFF_Q + B64_STAGES * TILE;    // [B64_STAGES]
+  static constexpr uint32_t OFF_P = OFF_DO + B64_STAGES * TILE;    // 2 blocks [128 keys][64 q]
+  static constexpr uint32_t OFF_DS = OFF_P + 2 * TILE;
+  static constexpr uint32_t STG_BYTES = 32 * 32 * 4;               // per compute warp
+  static constexpr uint32_t OFF_STG = OFF_DS + 2 * TILE;
+  static constexpr uint32_t OFF_BAR = OFF_STG + 8 * STG_BYTES;
+  static constexpr uint32_t NUM_BARS = 1 + 2 * B64_STAGES + 1 + 1 + 1 + 1 + 2 + 1;
+  static constexpr uint32_t TOTAL = 1024 + OFF_BAR + NUM_BARS * 8 + 16;
+};
+static_assert(Bwd64Smem::TOTAL <= 232448, "attention backward (hd 64): shared memory over 227 KB");
+static_assert(Bwd64Smem::OFF_STG % 1024 == 0 && Bwd64Smem::OFF_P % 1024 == 0, "swizzle alignment");
+
+// Row-per-lane [32 rows][32 fp32] tile (this lane = row) into a 128-byte
+// swizzled staging tile, scaled.
+__device__ __forceinline__ void stage_row32(float* stg, int lane, const float (&t)[32], float scale) {
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+    *reinterpret_cast<float4*>(stg + lane * 32 + ((c ^ (lane & 7)) << 2)) =
+        make_float4(t[4 * c] * scale, t[4 * c + 1] * scale, t[4 * c + 2] * scale, t[4 * c + 3] * scale);
+}
+
+__global__ void __launch_bounds__(BWD_THREADS, 1)
+    attn_bwd_tc64_kernel(const __grid_constant__ CUtensorMap tm_qkv,
+                         const __grid_constant__ CUtensorMap tm_do,
+                         const __grid_constant__ CUtensorMap tm_dq,
+                         const __grid_constant__ CUtensorMap tm_dkv, const float* __restrict__ lse,
+                         const float* __restrict__ dsum, AttnShape s, unsigned int* err) {
+  using L = Bwd64Smem;
+  constexpr int HD = 64;
+  constexpr uint32_t TMEM_COLS = 512;
+  constexpr uint32_t COL_S = 0, COL_DP = 128, COL_DQ = 256, COL_DV = 384, COL_DK = 448;
+  constexpr uint32_t ID_SDP = make_idesc(128, false, false);   // N = 128 q, both K-major
+  constexpr uint32_t ID_DVK = make_idesc(HD, false, true);     // N = 64 d, A K-major, B MN-major
+  constexpr uint32_t ID_DQ = make_idesc(HD, true, true);       // N = 64 d, A and B MN-major
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + L::OFF_BAR);
+  uint64_t* kv_full = bars;
+  uint64_t* qd_full = kv_full + 1;             // [B64_STAGES]
+  uint64_t* qd_empty = qd_full + B64_STAGES;   // [B64_STAGES]
+  uint64_t* sdp_full = qd_empty + B64_STAGES;
+  uint64_t* sdp_free = sdp_full + 1;
+  uint64_t* p_full = sdp_free + 1;
+  uint64_t* mm_done = p_full + 1;
+  uint64_t* dq_free = mm_done + 1;             // [2]
+  uint64_t* drain = dq_free + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  __shared__ int abort_flag;
+  volatile int& s_abort = abort_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.x, b = blockIdx.y, kt = blockIdx.z;
+  const int kvh = h / (s.nh / s.nkv);
+  const int n_items = s.T / B64_ROWS - kt;     // causal query tiles kt .. T/128 - 1
+  const int row0 = b * s.T;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int i = 0; i < B64_STAGES; ++i) {
+      mbar_init(&qd_full[i], 1);
+      mbar_init(&qd_empty[i], 1);
+    }
+    mbar_init(sdp_full, 1);
+    mbar_init(sdp_free, 8);
+    mbar_init(p_full, 8);
+    mbar_init(mm_done, 1);
+    for (int i = 0; i < 2; ++i) mbar_init(&dq_free[i], 8);
+    mbar_init(drain, 1);
+    s_abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_qkv);
+    tma_prefetch_desc(&tm_do);
+    tma_prefetch_desc(&tm_dq);
+    tma_prefetch_desc(&tm_dkv);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t sK = smem_u32(sm + L::OFF_K), sV = smem_u32(sm + L::OFF_V);
+  const uint32_t sQ = smem_u32(sm + L::OFF_Q), sDO = smem_u32(sm + L::OFF_DO);
+  const uint32_t sP = smem_u32(sm + L::OFF_P), sDS = smem_u32(sm + L::OFF_DS);
+  int issued = 0;   // Q/dO items the producer issued (read on the abort path)
+
+  if (warp == 0) {
+    // ------------------------------ producer ------------------------------
+    if (lane == 0) {
+      const int kcol = (s.nh + kvh) * HD, vcol = (s.nh + s.nkv + kvh) * HD;
+      mbar_arrive_expect_tx(kv_full, 2 * L::TILE);
+      tma_load_2d(sm + L::OFF_K, &tm_qkv, kv_full, kcol, row0 + kt * B64_ROWS);
+      tma_load_2d(sm + L::OFF_V, &tm_qkv, kv_full, vcol, row0 + kt * B64_ROWS);
+      for (int i = 0; i < n_items && !s_abort; ++i) {
+        const int st = i % B64_STAGES;
+        const int qrow = row0 + (kt + i) * B64_ROWS;
+        if (!mbar_wait(&qd_empty[st], ((i / B64_STAGES) & 1) ^ 1, err, &s_abort)) { s_abort = 1; break; }
+        mbar_arrive_expect_tx(&qd_full[st], 2 * L::TILE);
+        tma_load_2d(sm + L::OFF_Q + st * L::TILE, &tm_qkv, &qd_full[st], h * HD, qrow);
+        tma_load_2d(sm + L::OFF_DO + st * L::TILE, &tm_do, &qd_full[st], h * HD, qrow);
+        issued = i + 1;
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer ----------------------------
+    if (lane == 0) {
+      auto issue_sdp = [&](int j) -> bool {
+        const int st = j % B64_STAGES;
+        if (!mbar_wait(&qd_full[st], (j / B64_STAGES) & 1, err, &s_abort)) return false;
+        if (j > 0 && !mbar_wait(sdp_free, (j - 1) & 1, err, &s_abort)) return false;
+        tc_fence_after();
+        const uint32_t qb = sQ + st * L::TILE, db = sDO + st * L::TILE;
+#pragma unroll
+        for (int k = 0; k < HD / 16; ++k)
+          umma_bf16(tmem + COL_S, desc_kmajor(sK, k), desc_kmajor(qb, k), ID_SDP, k > 0);
+#pragma unroll
+        for (int k = 0; k < HD / 16; ++k)
+          umma_bf16(tmem + COL_DP, desc_kmajor(sV, k), desc_kmajor(db, k), ID_SDP, k > 0);
+        umma_commit(sdp_full);
+        return true;
+      };
+      bool ok = mbar_wait(kv_full, 0, err, &s_abort);
+      if (ok && n_items > 0) { tc_fence_after(); ok = issue_sdp(0); }
+      for (int i = 0; ok && i < n_items; ++i) {
+        if (i + 1 < n_items && !issue_sdp(i + 1)) { ok = false; break; }
+        const int st = i % B64_STAGES;
+        if (!mbar_wait(p_full, i & 1, err, &s_abort)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t qb = sQ + st * L::TILE, db = sDO + st * L::TILE;
+        // dV += P^T . dO, dK += dS^T . Q: K = 128 queries, the P^T / dS^T
+        // tiles in two 64-query K-major blocks; dO / Q read MN-major
+#pragma unroll
+        for (int k = 0; k < B64_ROWS / 16; ++k) {
+          umma_bf16(tmem + COL_DV, desc_kmajor(sP + (k >> 2) * L::TILE, k & 3), desc_mnmajor(db, k), ID_DVK,
+                    (i > 0 || k > 0));
+          umma_bf16(tmem + COL_DK, desc_kmajor(sDS + (k >> 2) * L::TILE, k & 3), desc_mnmajor(qb, k), ID_DVK,
+                    (i > 0 || k > 0));
+        }
+        // dQ = dS . K into buffer i & 1 (drained for item i-2 by now): A = the
+        // dS^T tile read MN-major (its two 64-query blocks are the M chunks,
+        // 16 KB apart), B = the K tile read MN-major (d contiguous)
+        if (!mbar_wait(&dq_free[i & 1], ((i >> 1) & 1) ^ 1, err, &s_abort)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < B64_ROWS / 16; ++k)
+          umma_bf16(tmem + COL_DQ + 64u * (i & 1), make_sdesc(sDS + k * (UMMA_K * 128), L::TILE, 1024),
+                    make_sdesc(sK + k * (UMMA_K * 128), 8192, 1024), ID_DQ, k > 0);
+        umma_commit(mm_done);
+        umma_commit(&qd_empty[st]);
+      }
+      if (!ok) s_abort = 1;
+    }
+  } else {
+    // ------------------------------- compute ------------------------------
+    const int sub = warp & 3;                 // TMEM lane quarter
+    const int half = (warp - 2) >> 2;         // S/dP query columns [64 half, +64); d columns [32 half, +32)
+    const int r = sub * 32 + lane;            // key row of S/dP/dK/dV, query row of dQ
+    const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
+    const float sl2 = s.scale * LOG2E_F;
+    float* stg = reinterpret_cast<float*>(sm + L::OFF_STG + (warp - 2) * L::STG_BYTES);
+    const uint32_t sSTG = smem_u32(stg);
+    // lse / dsum of this warp's 64 query columns of item i: lane holds
+    // columns lane and 32 + lane, broadcast by shuffle; prefetched one item ahead
+    auto lse_base = [&](int i) -> int64_t {
+      return (static_cast<int64_t>(b) * s.nh + h) * s.T + (kt + i) * B64_ROWS + 64 * half;
+    };
+    float pl0 = lse[lse_base(0) + lane], pl1 = lse[lse_base(0) + 32 + lane];
+    float pd0 = dsum[lse_base(0) + lane], pd1 = dsum[lse_base(0) + 32 + lane];
+    auto flush_dq = [&](int j) {
+      float t[32];
+      tmem_ld32(tmem + lane_off + COL_DQ + 64u * (j & 1) + 32 * half, t);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&dq_free[j & 1]);
+        bulk_wait_read0();                    // this warp's previous reduce has read its tile
+      }
+      __syncwarp();
+      stage_row32(stg, lane, t, s.scale);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_reduce_add_2d(&tm_dq, sSTG, h * HD + 32 * half, row0 + (kt + j) * B64_ROWS + 32 * sub);
+        bulk_commit();
+      }
+    };
+    bool ok = true;
+    for (int i = 0; i < n_items; ++i) {
+      const float cl0 = pl0 * LOG2E_F, cl1 = pl1 * LOG2E_F, cd0 = pd0, cd1 = pd1;
+      if (i + 1 < n_items) {
+        const int64_t nb = lse_base(i + 1);
+        pl0 = lse[nb + lane];
+        pl1 = lse[nb + 32 + lane];
+        pd0 = dsum[nb + lane];
+        pd1 = dsum[nb + 32 + lane];
+      }
+      if (!mbar_wait(sdp_full, i & 1, err, &s_abort)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t pw[32], dw[32];   // P^T and dS^T row segments, packed bf16 pairs
+      {
+        float sv[64], dv[64];
+        tmem_ld32(tmem + lane_off + COL_S + 64 * half, *reinterpret_cast<float(*)[32]>(sv));
+        tmem_ld32(tmem + lane_off + COL_S + 64 * half + 32, *reinterpret_cast<float(*)[32]>(sv + 32));
+        tmem_ld32(tmem + lane_off + COL_DP + 64 * half, *reinterpret_cast<float(*)[32]>(dv));
+        tmem_ld32(tmem + lane_off + COL_DP + 64 * half + 32, *reinterpret_cast<float(*)[32]>(dv + 32));
+        // S/dP are in registers: the MMA thread may overwrite them with item i+1
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(sdp_free);
+        // causal (diagonal item only): query column c sees key r iff 64 half + c >= r
+        const bool diag = i == 0;
+        const int lim = r - 64 * half;
+#pragma unroll
+        for (int c = 0; c < 64; c += 2) {
+          const float lc = c < 32 ? cl0 : cl1, dc = c < 32 ? cd0 : cd1;
+          const float l0 = __shfl_sync(0xffffffffu, lc, c & 31), l1 = __shfl_sync(0xffffffffu, lc, (c + 1) & 31);
+          const float d0 = __shfl_sync(0xffffffffu, dc, c & 31), d1 = __shfl_sync(0xffffffffu, dc, (c + 1) & 31);
+          float p0 = ex2_approx(fmaf(sv[c], sl2, -l0));
+          float p1 = ex2_approx(fmaf(sv[c + 1], sl2, -l1));
+          if (diag) {
+            if (c < lim) p0 = 0.f;
+            if (c + 1 < lim) p1 = 0.f;
+          }
+          pw[c >> 1] = pack_bf16x2_rn(p0, p1);
+          dw[c >> 1] = pack_bf16x2_rn(p0 * (dv[c] - d0), p1 * (dv[c + 1] - d1));
+        }
+      }
+      // the P^T / dS^T tiles are free once item i-1's products are done
+      if (i > 0) {
+        if (!mbar_wait(mm_done, (i - 1) & 1, err, &s_abort)) { ok = false; break; }
+        tc_fence_after();
+      }
+      // row r of block `half` (query columns [64 half, +64)), 128-byte swizzle
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint32_t off = half * L::TILE + r * 128 + ((c ^ (r & 7)) << 4);
+        asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(sP + off), "r"(pw[4 * c]),
+                     "r"(pw[4 * c + 1]), "r"(pw[4 * c + 2]), "r"(pw[4 * c + 3])
+                     : "memory");
+        asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(sDS + off), "r"(dw[4 * c]),
+                     "r"(dw[4 * c + 1]), "r"(dw[4 * c + 2]), "r"(dw[4 * c + 3])
+                     : "memory");
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+      if (i > 0) flush_dq(i - 1);
+    }
+    if (ok && n_items > 0) {
+      ok = mbar_wait(mm_done, (n_items - 1) & 1, err, &s_abort);
+      if (ok) {
+        tc_fence_after();
+        flush_dq(n_items - 1);
+        // dV, then dK (scaled), of this CTA's keys and query head into the
+        // shared fp32 accumulator (the GQA heads of the KV head add up there)
+        const int krow = row0 + kt * B64_ROWS + 32 * sub;
+#pragma unroll 1
+        for (int which = 0; which < 2; ++which) {
+          float t[32];
+          tmem_ld32(tmem + lane_off + (which == 0 ? COL_DV : COL_DK) + 32 * half, t);
+          if (lane == 0) bulk_wait_read0();
+          __syncwarp();
+          stage_row32(stg, lane, t, which == 0 ? 1.0f : s.scale);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            const int col = (which == 0 ? s.nkv * HD : 0) + kvh * HD + 32 * half;
+            tma_reduce_add_2d(&tm_dkv, sSTG, col, krow);
+            bulk_commit();
+          }
+        }
+      }
+    }
+    if (!ok) s_abort = 1;
+    if (lane == 0) bulk_wait0();   // this warp's reduce-adds complete before the CTA exits
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0 && lane == 0 && s_abort) {
+    // loads still in flight land before the CTA exits
+    mbar_wait(kv_full, 0, err, nullptr);
+    for (int d = 0; d < B64_STAGES && d < issued; ++d)
+      mbar_wait(&qd_full[(issued - 1 - d) % B64_STAGES], ((issued - 1 - d) / B64_STAGES) & 1, err, nullptr);
+  }
+  if (warp == 1) {
+    tc_fence_after();
+    if (s_abort) {
+      if (lane == 0) {
+        umma_commit(drain);
+        mbar_wait(drain, 0, err, nullptr);
+      }
+      __syncwarp();
+    }
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// fp32 accumulator [M, acc_ld] (heads x hd columns) -> bf16 columns of dst
+// (dst_ld), with the inverse half-split RoPE (the transpose of the forward
+// rotation, rope_impl.inc:21-36) applied before the rounding when cs is given:
+// one thread per (token, head, 4 dims of the first half) and their partners.
+__global__ void acc_to_bf16_kernel(const float* __restrict__ acc, int64_t acc_ld, int heads, int hd,
+                                   uint16_t* __restrict__ dst, int64_t dst_ld, int64_t M, int T,
+                                   const float* __restrict__ cs, const float* __restrict__ sn) {
+  const int half = hd / 2;
+  const int groups = half / 4;
+  const int64_t total = M * heads * groups;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int g = static_cast<int>(i % groups);
+    const int64_t rr = i / groups;
+    const int hh = static_cast<int>(rr % heads);
+    const int64_t t = rr / heads;
+    const float* a = acc + t * acc_ld + static_cast<int64_t>(hh) * hd + g * 4;
+    float4 x1 = *reinterpret_cast<const float4*>(a);
+    float4 x2 = *reinterpret_cast<const float4*>(a + half);
+    if (cs) {
+      const int pos = static_cast<int>(t % T);
+      const float4 co = *reinterpret_cast<const float4*>(cs + static_cast<int64_t>(pos) * half + g * 4);
+      const float4 si = *reinterpret_cast<const float4*>(sn + static_cast<int64_t>(pos) * half + g * 4);
+      const float4 y1 = make_float4(x1.x * co.x + x2.x * si.x, x1.y * co.y + x2.y * si.y,
+                                    x1.z * co.z + x2.z * si.z, x1.w * co.w + x2.w * si.w);
+      const float4 y2 = make_float4(x2.x * co.x - x1.x * si.x, x2.y * co.y - x1.y * si.y,
+                                    x2.z * co.z - x1.z * si.z, x2.w * co.w - x1.w * si.w);
+      x1 = y1;
+      x2 = y2;
+    }
+    uint16_t* d = dst + t * dst_ld + static_cast<int64_t>(hh) * hd + g * 4;
+    *reinterpret_cast<uint2*>(d) = make_uint2(pack_bf16x2(x1.x, x1.y), pack_bf16x2(x1.z, x1.w));
+    *reinterpret_cast<uint2*>(d + half) = make_uint2(pack_bf16x2(x2.x, x2.y), pack_bf16x2(x2.z, x2.w));
+  }
+}
+
+int acc_to_bf16(const float* acc, int64_t acc_ld, int heads, int hd, uint16_t* dst, int64_t dst_ld,
+                int64_t M, int T, const float* cs, const float* sn, cudaStream_t st) {
+  const int64_t n = M * heads * (hd / 8);
+  int blocks = static_cast<int>((n + 255) / 256);
+  if (blocks > num_sms() * 16) blocks = num_sms() * 16;
+  if (blocks < 1) return GLT_OK;
+  acc_to_bf16_kernel<<<blocks, 256, 0, st>>>(acc, acc_ld, heads, hd, dst, dst_ld, M, T, cs, sn);
+  GLT_LAUNCH_CHECK();
+  return GLT_OK;
+}
+
 }  // namespace
 
 int flash_bwd_tc(const uint16_t* qkv, const uint16_t* o, const uint16_t* dout, const float* lse,
@@ -789,6 +1171,36 @@ int flash_bwd_tc(const uint16_t* qkv, const uint16_t* o, const uint16_t* dout, c
                                               device_error_word());
   GLT_LAUNCH_CHECK();
   return attn_bwd_finish(dq_acc, dqkv, s, st, rope_cos, rope_sin);
+}
+
+int flash_bwd_tc64(const uint16_t* qkv, const uint16_t* o, const uint16_t* dout, const float* lse,
+                   uint16_t* dqkv, float* acc, float* dsum, const AttnShape& s, cudaStream_t st,
+                   bool dsum_ready, const float* rope_cos, const float* rope_sin) {
+  if (s.hd != 64) return fail(GLT_EINVAL, "attention backward (tcgen05, hd 64): head_dim must be 64");
+  if (s.T % B64_ROWS) return fail(GLT_EINVAL, "attention backward (tcgen05): seq_len %% 128 != 0");
+  if (s.nkv <= 0 || s.nh % s.nkv) return fail(GLT_EINVAL, "attention: nh %% nkv != 0");
+  if (s.ld_qkv % 8 || s.ld_o % 8) return fail(GLT_EINVAL, "attention: strides not 16-byte");
+  if (rope_cos && !rope_sin) return fail(GLT_EINVAL, "attention backward: rope tables");
+  GLT_TRY(attn_bwd_prep(o, dout, acc, dsum, s, st, dsum_ready));   // zeroes dq, computes dsum
+  const int64_t M = static_cast<int64_t>(s.B) * s.T;
+  const int64_t qcols = static_cast<int64_t>(s.nh) * s.hd, kvcols = 2 * static_cast<int64_t>(s.nkv) * s.hd;
+  float* dkv = acc + M * qcols;
+  GLT_CUDA_TRY(cudaMemsetAsync(dkv, 0, static_cast<size_t>(M * kvcols) * sizeof(float), st));
+  CUtensorMap tqkv, tdo, tdq, tdkv;
+  GLT_TRY(make_tmap_bf16(&tqkv, qkv, s.ld_qkv, M, s.ld_qkv, B64_ROWS));
+  GLT_TRY(make_tmap_bf16(&tdo, dout, s.ld_o, M, s.ld_o, B64_ROWS));
+  GLT_TRY(make_tmap_f32_swz128(&tdq, acc, qcols, M, qcols, 32));
+  GLT_TRY(make_tmap_f32_swz128(&tdkv, dkv, kvcols, M, kvcols, 32));
+  constexpr int smem = Bwd64Smem::TOTAL;
+  GLT_TRY(ensure_smem_attr(reinterpret_cast<const void*>(attn_bwd_tc64_kernel), smem));
+  dim3 grid(s.nh, s.B, s.T / B64_ROWS);
+  attn_bwd_tc64_kernel<<<grid, BWD_THREADS, smem, st>>>(tqkv, tdo, tdq, tdkv, lse, dsum, s,
+                                                         device_error_word());
+  GLT_LAUNCH_CHECK();
+  GLT_TRY(acc_to_bf16(acc, qcols, s.nh, s.hd, dqkv, s.ld_qkv, M, s.T, rope_cos, rope_sin, st));
+  GLT_TRY(acc_to_bf16(dkv, kvcols, s.nkv, s.hd, dqkv + qcols, s.ld_qkv, M, s.T, rope_cos, rope_sin, st));
+  return acc_to_bf16(dkv + static_cast<int64_t>(s.nkv) * s.hd, kvcols, s.nkv, s.hd,
+                     dqkv + qcols + static_cast<int64_t>(s.nkv) * s.hd, s.ld_qkv, M, s.T, nullptr, nullptr, st);
 }
 
 int flash_fwd_tc(const uint16_t* qkv, uint16_t* o, float* lse, const AttnShape& s,

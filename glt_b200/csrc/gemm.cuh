@@ -23,6 +23,11 @@ int make_tmap_bf16(CUtensorMap* tm, const void* base, uint64_t inner, uint64_t o
 // elements, box {box_inner, box_outer}); used for TMA reduce-add stores.
 int make_tmap_f32_plain(CUtensorMap* tm, const void* base, uint64_t inner, uint64_t outer,
                         uint64_t ld, uint32_t box_inner, uint32_t box_outer);
+// 2-D fp32 tensor map with 128-byte swizzle: box {32, box_outer} (one 128-byte
+// row of 32 floats per box row; 16-byte chunk c of row r at chunk c ^ (r & 7)
+// in shared memory, which must be 1024-byte aligned).
+int make_tmap_f32_swz128(CUtensorMap* tm, const void* base, uint64_t inner, uint64_t outer,
+                         uint64_t ld, uint32_t box_outer);
 
 int num_sms();
 

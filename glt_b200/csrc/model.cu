@@ -417,7 +417,9 @@ int Model::allocate() {
     add(reinterpret_cast<void**>(&xn), b2 * M * D);
     add(reinterpret_cast<void**>(&dqkv), b2 * M * QKV);
     add(reinterpret_cast<void**>(&dout_b), b2 * M * AD);
-    add(reinterpret_cast<void**>(&dq_acc), b4 * M * AD);
+    // fp32 dQ accumulator; with head_dim 64 also the dK/dV accumulators of
+    // the tcgen05 backward (flash_bwd_tc64)
+    add(reinterpret_cast<void**>(&dq_acc), b4 * M * (AD + (hd == 64 ? 2 * nkv * hd : 0)));
     add(reinterpret_cast<void**>(&dsum), b4 * B * nh * T);
     add(reinterpret_cast<void**>(&xf), b2 * M * D);
     add(reinterpret_cast<void**>(&varf), b4 * M);
@@ -754,15 +756,21 @@ int Model::backward_layer(int l, cudaStream_t st) {
   // post-attention RMSNorm backward + residual: dx = grad wrt x_post
   GLT_PROF(GLT_PROF_RMSNORM, rmsnorm_bwd(dtmp, y.x_post, y.post_norm, y.var2, dx, dx, dy_b, M, D, cfg.rms_norm_eps, st));
   // attention: do = dx_post . Wo ; flash backward ; RoPE^T ; dxn = dqkv . Wqkv
-  if (hd == 128 && T % 128 == 0) {
-    // tcgen05 backward: dsum from the dO GEMM's epilogue, the inverse RoPE
-    // of dq in its fp32 -> bf16 conversion, the one of dk in rope_apply
+  if (T % 128 == 0 && (hd == 128 || hd == 64)) {
+    // tcgen05 backward: dsum from the dO GEMM's epilogue; the inverse RoPE of
+    // dq (and, head_dim 64, of dk) in the fp32 -> bf16 conversion, that of dk
+    // at head_dim 128 in rope_apply
     EpiBF16Dsum<256> e{dout_b, AD, M, AD, y.o, AD, dsum, T, nh, hd};
     GLT_PROF(GLT_PROF_DO, (launch_gemm<256, 4, false, true>(kmaj(dy_b, D), mnmaj(y.wo, AD), M, AD, D, e, st)));
     const bool rope = rope_on(l);
-    GLT_PROF(GLT_PROF_ATTN_BWD, flash_bwd_tc(y.qkv, y.o, dout_b, y.lse, dqkv, dq_acc, dsum, as, st, true,
-                                             rope ? cos_t : nullptr, rope ? sin_t : nullptr));
-    if (rope) GLT_PROF(GLT_PROF_ROPE, rope_apply(dqkv, as, cos_t, sin_t, 1, 0, 1, st));
+    if (hd == 64) {
+      GLT_PROF(GLT_PROF_ATTN_BWD, flash_bwd_tc64(y.qkv, y.o, dout_b, y.lse, dqkv, dq_acc, dsum, as, st, true,
+                                                 rope ? cos_t : nullptr, rope ? sin_t : nullptr));
+    } else {
+      GLT_PROF(GLT_PROF_ATTN_BWD, flash_bwd_tc(y.qkv, y.o, dout_b, y.lse, dqkv, dq_acc, dsum, as, st, true,
+                                               rope ? cos_t : nullptr, rope ? sin_t : nullptr));
+      if (rope) GLT_PROF(GLT_PROF_ROPE, rope_apply(dqkv, as, cos_t, sin_t, 1, 0, 1, st));
+    }
   } else {
     GLT_PROF(GLT_PROF_DO, g_bf16(kmaj(dy_b, D), mnmaj(y.wo, AD), M, AD, D, dout_b, AD, nullptr, 0, st));
     GLT_PROF(GLT_PROF_ATTN_BWD, flash_bwd(y.qkv, y.o, dout_b, y.lse, dqkv, dq_acc, dsum, as, st));

@@ -95,7 +95,10 @@ extern "C" int glt_attention_bwd(const uint16_t* qkv, int64_t ld_qkv, const uint
     return glt::fail(GLT_EINVAL, "null argument");
   const AttnShape s = make_shape(B, T, nh, nkv, hd, ld_qkv, ld_o);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (impl == GLT_ATTN_TCGEN05) return glt::flash_bwd_tc(qkv, o, dout, lse, dqkv, dq_acc, dsum, s, st);
+  if (impl == GLT_ATTN_TCGEN05) {
+    if (hd == 64) return glt::flash_bwd_tc64(qkv, o, dout, lse, dqkv, dq_acc, dsum, s, st);
+    return glt::flash_bwd_tc(qkv, o, dout, lse, dqkv, dq_acc, dsum, s, st);
+  }
   if (impl == GLT_ATTN_MMA_SYNC) return glt::flash_bwd(qkv, o, dout, lse, dqkv, dq_acc, dsum, s, st);
   return glt::fail(GLT_EINVAL, "unknown attention implementation %d", impl);
 }

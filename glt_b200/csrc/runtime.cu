@@ -130,6 +130,23 @@ int make_tmap_f32_plain(CUtensorMap* tm, const void* base, uint64_t inner, uint6
   return GLT_OK;
 }
 
+int make_tmap_f32_swz128(CUtensorMap* tm, const void* base, uint64_t inner, uint64_t outer,
+                         uint64_t ld, uint32_t box_outer) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return fail(GLT_ECUDA, "cuTensorMapEncodeTiled unavailable");
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (ld * 4) % 16 != 0)
+    return fail(GLT_EINVAL, "fp32 tensor map: base/stride not 16-byte aligned");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld * 4};
+  cuuint32_t box[2] = {32, box_outer};   // 32 fp32 = one 128-byte swizzle row
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(GLT_ECUDA, "cuTensorMapEncodeTiled (fp32, swizzled) failed (%d)", (int)r);
+  return GLT_OK;
+}
+
 int make_tmap_bf16(CUtensorMap* tm, const void* base, uint64_t inner, uint64_t outer,
                    uint64_t ld, uint32_t box_outer) {
   EncodeTiledFn enc = get_encode_fn();

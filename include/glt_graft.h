@@ -205,10 +205,11 @@ GLT_API int glt_swiglu_bwd(float* grad_gate_pre, float* grad_up, const float* gr
 /* Attention = causal GQA SDPA (layer_forward_impl.inc:41-49; K/V heads     */
 /* indexed, not repeat_interleave'd); backward = attention_bwd_autograd's  */
 /* gradient (attention_autograd_impl.inc:1-39) into dqkv (same packing),   */
-/* with fp32 workspaces dq_acc [B*T, nh*hd] and dsum [B*nh*T].             */
-/* impl: GLT_ATTN_TCGEN05 (tcgen05/TMEM kernels, seq_len % 128 == 0; the   */
-/* backward needs hd 128) or GLT_ATTN_MMA_SYNC (seq_len % 64 == 0).         */
-/* hd: 64 or 128.                                                          */
+/* with fp32 workspaces dq_acc [B*T, nh*hd] and dsum [B*nh*T]; the        */
+/* tcgen05 backward at hd 64 needs dq_acc of B*T*(nh + 2*nkv)*hd floats     */
+/* (its dK/dV accumulators follow dQ).                                      */
+/* impl: GLT_ATTN_TCGEN05 (tcgen05/TMEM kernels, seq_len % 128 == 0) or     */
+/* GLT_ATTN_MMA_SYNC (seq_len % 64 == 0).  hd: 64 or 128.                   */
 /* RoPE: half-split rotation in place on q and k (rope_impl.inc:8-64);      */
 /* inverse = 1 applies the transpose (its backward).                        */
 /* RMSNorm: rms_norm_fwd_kernel / rms_norm_bwd_kernel                       */

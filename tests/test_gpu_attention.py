@@ -2,7 +2,9 @@
 same op (the reference computes it with at::scaled_dot_product_attention on
 repeat_interleave'd K/V, layer_forward_impl.inc:41-49): forward output and
 log-sum-exp of the tcgen05/TMEM kernel and of the mma.sync kernel, and the
-backward (dq, dk, dv) against torch autograd."""
+backward (dq, dk, dv) against torch autograd: the tcgen05 kernels at head_dim
+128 (64-query items) and 64 (128-query items, one CTA per query head, dK/dV
+summed over the GQA heads), and the mma.sync kernels."""
 import ctypes as C
 import math
 
@@ -74,14 +76,16 @@ def test_tcgen05_and_mma_sync_agree_on_large_scores():
 @pytest.mark.parametrize("impl,B,T,nh,nkv,hd", [(MMA, 2, 128, 4, 2, 128), (MMA, 1, 256, 4, 4, 64),
                                                 (MMA, 2, 256, 14, 2, 64), (MMA, 1, 192, 14, 2, 64),
                                                 (TC, 2, 128, 4, 2, 128), (TC, 1, 384, 8, 2, 128),
-                                                (TC, 2, 256, 4, 4, 128), (TC, 1, 512, 32, 8, 128)])
+                                                (TC, 2, 256, 4, 4, 128), (TC, 1, 512, 32, 8, 128),
+                                                (TC, 2, 128, 4, 2, 64), (TC, 1, 384, 4, 4, 64),
+                                                (TC, 2, 256, 14, 2, 64), (TC, 1, 1024, 14, 2, 64)])
 def test_backward_matches_autograd(impl, B, T, nh, nkv, hd):
     qkv = make_qkv(B, T, nh, nkv, hd, seed=11)
     o, lse = fwd(qkv, B, T, nh, nkv, hd, MMA)
     g = torch.Generator(device="cuda").manual_seed(12)
     dout = torch.randn(B * T, nh * hd, device="cuda", generator=g).to(torch.bfloat16)
     dqkv = torch.zeros_like(qkv)
-    dq_acc = torch.empty(B * T, nh * hd, device="cuda")
+    dq_acc = torch.empty(B * T * (nh + 2 * nkv) * hd, device="cuda")   # dQ (+ dK/dV: tcgen05, hd 64)
     dsum = torch.empty(B * nh * T, device="cuda")
     _lib.check(lib.glt_attention_bwd(vp(qkv), qkv.shape[1], vp(o), vp(dout), nh * hd, vp(lse),
                                      vp(dqkv), vp(dq_acc), vp(dsum), B, T, nh, nkv, hd, impl,

@@ -67,7 +67,20 @@ class GltEvalStats(C.Structure):
                 ("logits_hash", C.c_uint64), ("graft_forward_calls", C.c_int64)]
 
 
+class GltGraftWeights(C.Structure):
+    """ctypes mirror of GltGraftWeights (include/glt_graft.h)."""
+    _fields_ = [("weight", _vp), ("weight_bf16", _vp), ("weight_elems", C.c_int64), ("domain_id", _i32),
+                ("allocated", _i32), ("active", _i32)]
+
+
+class GltMlpSaved(C.Structure):
+    """ctypes mirror of GltMlpSaved (include/glt_graft.h)."""
+    _fields_ = [("x_ffn", _vp), ("variance", _vp), ("energy_sq", _vp), ("delta_down", _vp)]
+
+
 _cfgp = C.POINTER(GltModelConfig)
+_gwp = C.POINTER(GltGraftWeights)
+_svp = C.POINTER(GltMlpSaved)
 _fp = C.POINTER(C.c_void_p)
 
 # (name, restype, argtypes) for every exported symbol; tests check that each
@@ -89,6 +102,16 @@ SIGNATURES: dict[str, tuple] = {
     "glt_swiglu_bwd": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _vp]),
     "glt_stack_grafts": (_i32, [C.POINTER(_vp), _i32, _i32, _i32, _i32, _vp, _vp]),
     "glt_model_create": (_i32, [_cfgp, _i32, _i32, _i32, C.POINTER(_vp)]),
+    "glt_graft_weights_alloc": (_i32, [_cfgp, _i32, _i32, _gwp]),
+    "glt_graft_weights_free": (_i32, [_gwp]),
+    "glt_mlp_create": (_i32, [_cfgp, _i32, C.POINTER(_vp)]),
+    "glt_mlp_destroy": (_i32, [_vp]),
+    "glt_mlp_set_weight": (_i32, [_vp, _i32, _i32, _vp, _i64, _i32, _vp]),
+    "glt_mlp_set_graft": (_i32, [_vp, _gwp, _vp]),
+    "glt_mlp_recompute_bytes": (_i32, [_vp, C.POINTER(_i64)]),
+    "glt_mlp_fwd": (_i32, [_vp, _i32, _vp, _vp, _svp, _i32, _vp]),
+    "glt_mlp_recompute": (_i32, [_vp, _i32, _svp, _vp, _vp]),
+    "glt_mlp_bwd": (_i32, [_vp, _i32, _vp, _vp, _svp, _vp, _vp, _f32, _vp, _vp]),
     "glt_model_destroy": (_i32, [_vp]),
     "glt_train_state_save": (_i32, [C.c_char_p, _vp, _vp, _vp, _i64, _i32, C.c_char_p, _i32, _i32, _i32,
                                     _i32, _i32, _i64]),

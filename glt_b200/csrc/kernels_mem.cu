@@ -815,6 +815,12 @@ int set_clip_scale(DevStats* stats, float v, cudaStream_t st) {
   return GLT_OK;
 }
 
+int set_lambda_eff(DevStats* stats, float v, cudaStream_t st) {
+  set_scalar_kernel<<<1, 1, 0, st>>>(&stats->lambda_eff, v);
+  GLT_LAUNCH_CHECK();
+  return GLT_OK;
+}
+
 int mse_grad(const uint16_t* out, const float* y, float* dx, DevStats* stats, int M, int D,
              cudaStream_t st) {
   if (M <= 0) return GLT_OK;

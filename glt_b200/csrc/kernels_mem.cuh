@@ -63,6 +63,8 @@ int silence_stats(const float* esq, const int* proj_enabled /*[L*3] dev*/, int L
 int mse_grad(const uint16_t* out, const float* y, float* dx, DevStats* stats, int M, int D,
              cudaStream_t st);
 int set_clip_scale(DevStats* stats, float v, cudaStream_t st);
+// stats->lambda_eff = v (a caller-supplied silence weight for a layer-level backward).
+int set_lambda_eff(DevStats* stats, float v, cudaStream_t st);
 // Stream-ordered collection of the device error word (kernels that give up a
 // bounded wait set it): v = *word | *accum, then *word = 0; with dst, *dst = v
 // and *accum = 0, else *accum = v.  No host synchronisation.

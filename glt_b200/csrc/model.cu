@@ -345,7 +345,7 @@ int Model::ensure_mlp_store() {
 int Model::allocate() {
   // ---- graft parameters (outside the arena, like GraftWeights) ----
   graft_numel = static_cast<int64_t>(3) * L * S * H;
-  {
+  if (!external_acts) {
     const size_t bytes = static_cast<size_t>(graft_numel) * 4 * 4;
     GLT_CUDA_TRY(cudaMalloc(&graft_mem, bytes));
     GLT_CUDA_TRY(cudaMemset(graft_mem, 0, bytes));
@@ -377,6 +377,7 @@ int Model::allocate() {
     add(reinterpret_cast<void**>(&y.post_norm), b2 * D);
     add(reinterpret_cast<void**>(&y.w_gu), b2 * 2 * FF * D);
     add(reinterpret_cast<void**>(&y.w_d), b2 * D * FF);
+    if (external_acts) continue;   // saved activations belong to the caller
     // saved activations
     add(reinterpret_cast<void**>(&y.x_post), b2 * M * D);
     add(reinterpret_cast<void**>(&y.x_ffn), b2 * M * D);
@@ -389,9 +390,11 @@ int Model::allocate() {
       add(reinterpret_cast<void**>(&y.lse), b4 * B * nh * T);
     }
   }
-  add(reinterpret_cast<void**>(&esq_all), b4 * 3 * static_cast<size_t>(L) * M);
-  xs.resize(L + 1);
-  for (int l = 0; l <= L; ++l) add(reinterpret_cast<void**>(&xs[l]), b2 * M * D);
+  if (!external_acts) {
+    add(reinterpret_cast<void**>(&esq_all), b4 * 3 * static_cast<size_t>(L) * M);
+    xs.resize(L + 1);
+    for (int l = 0; l <= L; ++l) add(reinterpret_cast<void**>(&xs[l]), b2 * M * D);
+  }
   add(reinterpret_cast<void**>(&h), b2 * M * FF);
   add(reinterpret_cast<void**>(&dx), b4 * M * D);
   add(reinterpret_cast<void**>(&dtmp), b4 * M * D);
@@ -445,7 +448,8 @@ int Model::allocate() {
     off += rup(static_cast<int64_t>(r.bytes), 256);
   }
   if (dec && cfg.tie_embeddings) lm_head = embed;
-  for (int l = 0; l < L; ++l) layers[l].esq = esq_all + static_cast<int64_t>(3) * M * l;
+  if (esq_all)
+    for (int l = 0; l < L; ++l) layers[l].esq = esq_all + static_cast<int64_t>(3) * M * l;
   // device-side tables
   GLT_CUDA_TRY(cudaMemcpy(d_enabled, enabled.data(), sizeof(int) * 3 * L, cudaMemcpyHostToDevice));
   std::vector<uint16_t*> gup(L), wdp(L);
@@ -657,6 +661,29 @@ int Model::ffn_forward(int l, const uint16_t* x_in, uint16_t* x_out, float* var_
       GLT_PROF(GLT_PROF_DELTA_DOWN, (launch_gemm<128, 6, false, false>(kmaj(h + F_pad, FF), kmaj(y.w_d + F_pad, FF), M, D, S, e, st)));
     }
   }
+  return GLT_OK;
+}
+
+// recompute_ffn (layer_recompute_impl.inc:8-91): the gate/up GEMM of layer l
+// from its saved x_ffn, with the graft deltas injected, writing only the
+// bf16 gate_pre/up store (layers[l].gu) that the fused backward reads.
+int Model::ffn_recompute(int l, cudaStream_t st) {
+  Layer& y = layers[l];
+  if (!y.gu || !y.x_ffn) return fail(GLT_EINVAL, "recompute: no store or no x_ffn for layer %d", l);
+  const bool g = enabled[3 * l], u = enabled[3 * l + 1];
+  const bool grafted = g || u || enabled[3 * l + 2];
+  if (overlay) {
+    if (g || u) GLT_TRY(expand_deltas(l, g, u, nullptr, nullptr, st));
+    EpiSwiGLUFwdOv e{h, FF, M, g ? dlt : nullptr, u ? dlt + S : nullptr, 2 * static_cast<int64_t>(S),
+                     i0, i0 + S, y.gu, 2 * static_cast<int64_t>(FF) / 8};
+    GLT_PROF(GLT_PROF_RECOMPUTE,
+             (launch_gemm<256, 4, false, false>(kmaj(y.x_ffn, D), kmaj(y.w_gu, D), M, 2 * FF, D, e, st)));
+    return GLT_OK;
+  }
+  const int ff = grafted ? FF : F_pad;
+  EpiSwiGLUFwd e{h, FF, M, F_pad, F_pad + S, nullptr, nullptr, y.gu, 2 * static_cast<int64_t>(FF) / 8};
+  GLT_PROF(GLT_PROF_RECOMPUTE,
+           (launch_gemm<256, 4, false, false>(kmaj(y.x_ffn, D), kmaj(y.w_gu, D), M, 2 * ff, D, e, st)));
   return GLT_OK;
 }
 

@@ -147,6 +147,13 @@ struct Model {
   cudaEvent_t comm_done = nullptr;
   bool own_stream_events = false;
 
+  // Layer-level use (glt_mlp_*, mlp_layers.cu): the caller owns the saved
+  // activations, the graft weights and their gradients; the model holds only
+  // the fused weights and the scratch of one layer at a time.  The per-layer
+  // saved pointers, dx, grad and ood are set by each call.
+  bool external_acts = false;
+  int ffn_recompute(int l, cudaStream_t st);   // gate_pre/up of layer l into layers[l].gu
+
   ~Model();
   int setup(const GltModelConfig& c, int batch, int seq, int kind);
   int allocate();

@@ -490,6 +490,82 @@ GLT_API int glt_model_profile(GltModel* m, int enable);
 GLT_API int glt_model_profile_read(GltModel* m, double* ms, int64_t* launches, int reset);
 
 /* ------------------------------------------------------------------------ */
+/* Graft weights outside any arena: allocate_graft_weights /                */
+/* free_graft_weights_noexcept (src/graft_weights_impl.inc:6-62).          */
+/* alloc: the fp32 master [3L, S, H] (delta_offset layout; H = hidden for   */
+/* the concat layout, hidden / max_domains for overlay) and, with           */
+/* with_bf16_mirror, its bf16 mirror, both zeroed; active = 0 (the caller   */
+/* sets it once a checkpoint, init or training load is applied).  A struct */
+/* still allocated is freed first.  free: releases both buffers and resets  */
+/* every field (safe on a freed or zeroed struct).                          */
+/* ------------------------------------------------------------------------ */
+typedef struct GltGraftWeights {
+  float* weight;          /* device fp32 [3L, S, H]         (d_weight)      */
+  uint16_t* weight_bf16;  /* device bf16 mirror, or NULL    (d_weight_bf16) */
+  int64_t weight_elems;
+  int domain_id;
+  int allocated;
+  int active;
+} GltGraftWeights;
+GLT_API int glt_graft_weights_alloc(const GltModelConfig* cfg, int domain_id, int with_bf16_mirror,
+                                    GltGraftWeights* g);
+GLT_API int glt_graft_weights_free(GltGraftWeights* g);
+
+/* ------------------------------------------------------------------------ */
+/* Layer-level grafted MLP, for callers that keep the reference's own layer */
+/* loop: the MLP halves of forward_layer (src/layer_forward_impl.inc:53-218), */
+/* recompute_ffn (src/layer_recompute_impl.inc:8-91) and backward_layer     */
+/* (src/layer_backward_impl.inc:36-368), in the same fused tcgen05 GEMMs as */
+/* glt_train_step.  A GltMlp holds, for cfg.num_layers layers, the frozen   */
+/* bf16 post-attention norm and gate/up/down weights in the fused layout    */
+/* with the graft's bf16 image inside, and the scratch of one layer for     */
+/* `tokens` rows (M = batch * seq).  The caller owns the activations, the   */
+/* saved tensors (GltMlpSaved, the MLP fields of LayerActivations), the     */
+/* graft weights (GltGraftWeights) and their gradients.  All device         */
+/* pointers 16-byte aligned; calls are stream-ordered and do not            */
+/* synchronise (a device timeout is reported by glt_device_error).          */
+/* ------------------------------------------------------------------------ */
+typedef struct GltMlp GltMlp;
+typedef struct GltMlpSaved {
+  uint16_t* x_ffn;       /* [M, D] bf16 post-attention RMSNorm output (x_ffn_input)   */
+  float* variance;       /* [M] fp32 mean square of x_post (rms_norm_variance)        */
+  float* energy_sq;      /* [3, M] fp32 per-token sums of squares of the gate, up and */
+                         /* down delta outputs (energy = sqrt(esq + 1e-8) / sqrt(width)) */
+  uint16_t* delta_down;  /* [M, H] bf16 delta_down_out (needed when down is grafted)  */
+} GltMlpSaved;
+GLT_API int glt_mlp_create(const GltModelConfig* cfg, int tokens, GltMlp** out);
+GLT_API int glt_mlp_destroy(GltMlp* m);
+/* which: GLT_W_POST_NORM [D], GLT_W_GATE / GLT_W_UP [F, D], GLT_W_DOWN [D, F], bf16. */
+GLT_API int glt_mlp_set_weight(GltMlp* m, int layer, int which, const void* src_bf16, int64_t numel,
+                               int src_is_host, void* stream);
+/* Copies the bf16 image (reference rounding) of g->weight into the fused    */
+/* weights the GEMMs read, and into g->weight_bf16 when present: after a    */
+/* load or an optimizer step (refresh_graft_weight_bf16).                   */
+GLT_API int glt_mlp_set_graft(GltMlp* m, const GltGraftWeights* g, void* stream);
+/* Forward of layer `layer`: x_out = x_post + MLP(rms_norm(x_post)) with the */
+/* graft's expand deltas injected into gate/up and its contract delta into   */
+/* the output (use_graft = 0: base only), bf16 [M, D]; fills saved.          */
+GLT_API int glt_mlp_fwd(GltMlp* m, int layer, const uint16_t* x_post, uint16_t* x_out,
+                        const GltMlpSaved* saved, int use_graft, void* stream);
+/* recompute_ffn: the layer's bf16 gate_pre/up (deltas injected) from       */
+/* saved->x_ffn into gate_up, a private blocked layout of                   */
+/* glt_mlp_recompute_bytes bytes that glt_mlp_bwd reads.                    */
+GLT_API int glt_mlp_recompute_bytes(const GltMlp* m, int64_t* bytes);
+GLT_API int glt_mlp_recompute(GltMlp* m, int layer, const GltMlpSaved* saved, void* gate_up,
+                              void* stream);
+/* Backward of layer `layer`'s MLP half and post-attention RMSNorm: dx (fp32 */
+/* [M, D], in/out) enters as the gradient of x_out and leaves as that of     */
+/* x_post (the residual included); x_post is the forward's input.  The       */
+/* layer's three [S, H] slices of grad ([3L, S, H] fp32) are overwritten     */
+/* with the graft gradients, the OOD silence term included (ood_mask [M]     */
+/* int32 device, lambda_effective = lambda / (ood_count * active_grafts) as  */
+/* grafting.hip:1104).  gate_up: this layer's glt_mlp_recompute output, or   */
+/* NULL to recompute gate/up inside the backward's own GEMM.                 */
+GLT_API int glt_mlp_bwd(GltMlp* m, int layer, float* dx, const uint16_t* x_post,
+                        const GltMlpSaved* saved, const void* gate_up, const int32_t* ood_mask,
+                        float lambda_effective, float* grad, void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* GRFT checkpoint (src/checkpoint_impl.inc).  Bytes: u32 "GRFT" LE | u8 4  */
 /* | u64 header size (JSON NUL-padded to 8) | safetensors JSON | bf16      */
 /* delta_weights [3L,S,H] (bias-trick rounding, checkpoint_impl.inc:49-57). */

@@ -12,10 +12,13 @@ overlay: the reference's geometry -- domain d's graft at intermediate rows
   assembled by glt_stack_grafts into one block-diagonal graft.
 concat:  the four slices side by side, [base | s0 | s1 | s2 | s3].
 
-Prints one JSON line per geometry: prefill tokens/s of the stacked and of the
-baked forward (CUDA events on the launching stream, whole forward including
-the LM head, max over ranks, summed over ranks for the aggregate), and the
-logits agreement over every logit (max |stack - baked| / max |stack| and the
+Under torchrun every rank holds the same base model and stack and runs its
+own prefill batch (weak scaling, no collective on the data path); the only
+exchange is one reduce of the metrics at the end.  Prints one JSON line per
+geometry: prefill tokens/s of the stacked and of the baked forward (CUDA
+events on the launching stream, whole forward including the LM head, max
+over ranks, summed over ranks for the aggregate), and the logits agreement
+over every logit (worst over the ranks) (max |stack - baked| / max |stack| and the
 cosine), checked against the bf16 gate (<= 2e-2, >= 0.999), and the mean
 next-token CE of both models over the batch against the reference's own bake
 acceptance gate (|CE_shadow - CE_explicit| < 0.02).  Base weights are
@@ -90,7 +93,8 @@ def run(geometry: str, a, world: int, rank: int, dist) -> dict:
         cfg = G.GraftConfig(slice_dim=N * S_each, max_domains=4, domain_id=0, layout=G.LAYOUT_CONCAT,
                             **common)
     m = G.GraftModel(cfg, B, T, kind=G.MODEL_DECODER)
-    m.init_random(seed=1234 + rank, std=0.02, graft_std=0.0, graft_down_std=0.0)
+    # replicas: the same base weights and grafts on every rank, each rank its own prefill batch
+    m.init_random(seed=1234, std=0.02, graft_std=0.0, graft_down_std=0.0)
     stream = torch.cuda.current_stream()
     gen = [torch.Generator(device="cuda").manual_seed(100 + d) for d in range(N)]
     if geometry == "overlay":
@@ -148,10 +152,20 @@ def run(geometry: str, a, world: int, rank: int, dist) -> dict:
     effect = l2_rel(logits_base, logits_stack)
     del logits_base
     m.close()
+    if dist:
+        # the one exchange of the replicas: their metrics, reduced once at the end
+        # (worst agreement over the ranks, mean CE over the ranks' batches)
+        t = torch.tensor([rel, -cos, l2, effect, ce_stack, ce_baked], device="cuda", dtype=torch.float64)
+        tmax = t.clone()
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        rel, cos, l2, effect = float(tmax[0]), -float(tmax[1]), float(tmax[2]), float(tmax[3])
+        ce_stack, ce_baked = float(t[4]) / world, float(t[5]) / world
     tok = world * B * T
     return {"config": "stacked-graft inference, llama3-8b shape, 4 x 512 sibling grafts, prefill 8 x 4096", "geometry": geometry,
             "stack": f"{N} sibling grafts x {S_each}", "model": f"llama3-8b shape, {L} layers",
-            "batch": B, "seq": T, "n_gpus": world, "dtype": "bf16", "data": "synthetic",
+            "batch": B, "seq": T, "n_gpus": world, "parallelism": f"dp{world} (replicas, one metrics reduce)",
+            "scaling": "weak", "dtype": "bf16", "data": "synthetic",
             "stack_ms": ms_stack, "stack_tokens_per_s": tok / (ms_stack / 1e3),
             "baked_ms": ms_baked, "baked_tokens_per_s": tok / (ms_baked / 1e3),
             "graft_std": a.graft_std, "logits_max_rel": rel, "logits_cos": cos, "logits_l2_rel": l2,

@@ -7,12 +7,12 @@
 //   refresh of the bf16 graft copy the GEMMs read (delta_bf16_mirror)
 //                                            -> glt_mlp_set_graft
 //   forward_layer, MLP half (post-attention RMSNorm, gate/up + deltas,
-//       SiLU*mul, down + delta, residual)   src/layer_forward_impl.inc:53-218
+//       SiLU*mul, down + delta, residual)   src/layer_forward_impl.inc:53-285
 //                                            -> glt_mlp_fwd
 //   recompute_ffn                            src/layer_recompute_impl.inc:8-91
 //                                            -> glt_mlp_recompute
 //   backward_layer, MLP half + post-attention RMSNorm backward
-//                                            src/layer_backward_impl.inc:36-368
+//                                            src/layer_backward_impl.inc:36-367
 //                                            -> glt_mlp_bwd
 // The MLP runs in the same fused tcgen05 GEMMs as the whole-model step
 // (Model::ffn_forward / ffn_backward); the handle is a Model that holds only

@@ -513,9 +513,9 @@ GLT_API int glt_graft_weights_free(GltGraftWeights* g);
 
 /* ------------------------------------------------------------------------ */
 /* Layer-level grafted MLP, for callers that keep the reference's own layer */
-/* loop: the MLP halves of forward_layer (src/layer_forward_impl.inc:53-218), */
+/* loop: the MLP halves of forward_layer (src/layer_forward_impl.inc:53-285), */
 /* recompute_ffn (src/layer_recompute_impl.inc:8-91) and backward_layer     */
-/* (src/layer_backward_impl.inc:36-368), in the same fused tcgen05 GEMMs as */
+/* (src/layer_backward_impl.inc:36-367), in the same fused tcgen05 GEMMs as */
 /* glt_train_step.  A GltMlp holds, for cfg.num_layers layers, the frozen   */
 /* bf16 post-attention norm and gate/up/down weights in the fused layout    */
 /* with the graft's bf16 image inside, and the scratch of one layer for     */

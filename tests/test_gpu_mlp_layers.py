@@ -2,9 +2,9 @@
 weights (glt_graft_weights_alloc / _free), against the fp32 oracle.
 
 A caller that keeps the reference's own layer loop replaces the MLP half of
-forward_layer (src/layer_forward_impl.inc:53-218), recompute_ffn
+forward_layer (src/layer_forward_impl.inc:53-285), recompute_ffn
 (src/layer_recompute_impl.inc:8-91) and the MLP half of backward_layer with
-the post-attention RMSNorm backward (src/layer_backward_impl.inc:36-368)
+the post-attention RMSNorm backward (src/layer_backward_impl.inc:36-367)
 call for call.  For each layer of a two-layer stack, in both graft
 geometries: the forward output and the saved tensors, then the backward's
 input gradient and the layer's graft gradients, with the gate_pre/up store

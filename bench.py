@@ -16,7 +16,11 @@ value  tokens/s of the whole job with the token ids already on the device
 e2e    the same metric through glt_train_step with pinned-host inputs copied
        in and the step statistics read back every step;
 roofline  the dominant kernel (the gate/up GEMM with fused SwiGLU) timed live
-       with CUDA events around each of its launches inside the timed region;
+       with CUDA events around each of its launches, in a second pass of the
+       same steps right after the timed region (the events cost ~0.3% of a
+       step at this shape, so the timed region itself runs without them);
+extra  the same step recomputing the FFN (recompute_ffn) instead of keeping
+       the forward's gate_pre/up;
 cpu_baseline  the fp32 CPU oracle on this host's cores, one decoder layer on
        a bounded token sample, extrapolated per token.
 """
@@ -207,6 +211,30 @@ def run_reference_arm(args, wl):
     return 0
 
 
+NCCL_ALGOS = {0: "Tree", 1: "Ring", 2: "CollNetDirect", 3: "CollNetChain", 4: "NVLS", 5: "NVLSTree", 6: "PAT"}
+NCCL_PROTOS = {0: "LL", 1: "LL128", 2: "Simple"}
+
+
+def nccl_summary(path):
+    """The algorithm/protocol NCCL chose for each all-reduce size (its TUNING
+    lines, 'AllReduce: <bytes> Bytes -> Algo <a> proto <p> ...'), and the
+    communicators it built."""
+    import re
+    try:
+        text = open(path).read()
+    except OSError:
+        return {"log": "unavailable"}
+    picks = {}
+    for m in re.finditer(r"AllReduce: (\d+) Bytes -> Algo (\d+) proto (\d+)", text):
+        key = f"{int(m.group(1))} B"
+        picks.setdefault(key, {"algo": NCCL_ALGOS.get(int(m.group(2)), m.group(2)),
+                               "proto": NCCL_PROTOS.get(int(m.group(3)), m.group(3)), "calls": 0})
+        picks[key]["calls"] += 1
+    nvls = [ln.split("NCCL INFO")[-1].strip() for ln in text.splitlines() if "NVLS" in ln][:4]
+    tuning = [ln.split("NCCL INFO")[-1].strip() for ln in text.splitlines() if " Algo " in ln][:3]
+    return {"allreduce": picks, "nvls_lines": nvls, "tuning_lines": tuning, "version": (re.findall(r"NCCL version [^\s]+", text) or [None])[0]}
+
+
 # ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
@@ -240,10 +268,19 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dist = None
+    nccl_log = None
     if world > 1:
         import datetime
 
         import torch.distributed as dist
+        if "NCCL_DEBUG_FILE" not in os.environ:
+            # NCCL's own record of the algorithm and protocol it picks for each
+            # all-reduce (TUNING lines), one file per rank, summarised in the line
+            nccl_log = os.path.join("/tmp", f"glt_bench_nccl.{os.getpid()}.log")
+            if os.environ.get("NCCL_DEBUG", "").upper() not in ("INFO", "TRACE"):
+                os.environ["NCCL_DEBUG"] = "INFO"
+            os.environ.update(NCCL_DEBUG_SUBSYS=os.environ.get("NCCL_DEBUG_SUBSYS", "INIT,TUNING"),
+                              NCCL_DEBUG_FILE=nccl_log)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
 
@@ -299,7 +336,6 @@ def main():
             pass
     launches0 = C.c_uint64()
     _lib.check(_lib.lib.glt_launch_count(C.byref(launches0)))
-    _lib.check(_lib.lib.glt_model_profile(model.handle, 1))
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     with ClockSampler(smi_index) as clk:
@@ -309,15 +345,28 @@ def main():
             step += 1
         e1.record(stream)
         torch.cuda.synchronize()
-    _lib.check(_lib.lib.glt_model_profile(model.handle, 0))
     launches1 = C.c_uint64()
     _lib.check(_lib.lib.glt_launch_count(C.byref(launches1)))
     barrier()
     ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
     tokens_per_step = world * B * T
-    value = tokens_per_step / (ms / 1e3)
 
-    # per-kind kernel times over the timed region
+    # per-kind kernel times: the same steps again with CUDA events recorded on
+    # the launching stream around every launch (kept out of the main region,
+    # whose value they would lower by their own cost)
+    _lib.check(_lib.lib.glt_model_profile(model.handle, 1))
+    p0 = torch.cuda.Event(enable_timing=True)
+    p1 = torch.cuda.Event(enable_timing=True)
+    p0.record(stream)
+    for _ in range(args.steps):
+        model.train_step(ids, ood, step, total_steps + args.steps, want_stats=False)
+        step += 1
+    p1.record(stream)
+    torch.cuda.synchronize()
+    _lib.check(_lib.lib.glt_model_profile(model.handle, 0))
+    barrier()
+    profiled_ms = max_over_ranks(p0.elapsed_time(p1) / args.steps)
+    value = tokens_per_step / (ms / 1e3)
     kms, kn = model.profile_read(reset=True)   # sized by the library's GLT_PROF_KINDS
     M = B * T
     D, F, S, L = wl["hidden_dim"], wl["intermediate_dim"], wl["slice_dim"], wl["num_layers"]
@@ -338,6 +387,8 @@ def main():
         "peak_note": f"{pk['src']} bf16_tflops_sustained (kernel timed inside a long step)",
         "traffic": GATE_UP_TRAFFIC_BYTES[store_on],
         "algorithmic_flops_per_launch": gu_flops, "avg_launch_ms": gu_ms,
+        "timing": "CUDA events around every launch on its stream, over a second pass of the "
+                  f"same {args.steps} steps ({profiled_ms:.1f} ms per step with the events)",
         "mlp_gemm": {
             "pct_of_peak_algorithmic": 100.0 * mlp_alg / (mlp_ms / 1e3) / 1e12 / pk["tf_sus"],
             "pct_of_burst_peak_algorithmic": 100.0 * mlp_alg / (mlp_ms / 1e3) / 1e12 / pk["tf"],
@@ -360,7 +411,7 @@ def main():
         barrier()
         t0 = time.perf_counter()
         for _ in range(args.steps):
-            model.train_step(h_ids, h_ood, step, total_steps + args.steps, want_stats=True)
+            model.train_step(h_ids, h_ood, step, total_steps + 2 * args.steps, want_stats=True)
             step += 1
         torch.cuda.synchronize()
         e2e_s = max_over_ranks((time.perf_counter() - t0) / args.steps)
@@ -405,6 +456,7 @@ def main():
     Dm, nhm, nkvm, hdm = wl["hidden_dim"], wl["num_heads"], wl["num_kv_heads"], wl["head_dim"]
     w_layer = Dm * (nhm + 2 * nkvm) * hdm + nhm * hdm * Dm + 3 * Dm * (wl["intermediate_dim"] + wl["slice_dim"])
     w_bytes = 2 * (L * w_layer + (1 if wl["tie_embeddings"] else 2) * wl["vocab_size"] * Dm)
+    nccl = nccl_summary(nccl_log) if (nccl_log and rank == 0) else None
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
@@ -422,6 +474,11 @@ def main():
             "gpu_launches": int(launches1.value - launches0.value),
             "kernels": kernels,
         }
+        if world > 1:
+            line["nccl"] = nccl
+            line["dp"] = {"bucket_layers": int(os.environ.get("GLT_DP_BUCKET_LAYERS", "4")),
+                          "comm_priority": os.environ.get("GLT_DP_COMM_PRIORITY", "default"),
+                          "gemm_schedule": os.environ.get("GLT_GEMM_SCHEDULE", "static")}
         print(json.dumps(line), flush=True)
     model.close()
     if dist:

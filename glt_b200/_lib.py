@@ -143,6 +143,8 @@ SIGNATURES: dict[str, tuple] = {
     "glt_dp_unique_id": (_i32, [_vp, _i32]),
     "glt_dp_init": (_i32, [_vp, _vp, _i32, _i32]),
     "glt_dp_finalize": (_i32, [_vp]),
+    "glt_dp_async_error": (_i32, [_vp, C.POINTER(_i32)]),
+    "glt_dp_abort": (_i32, [_vp]),
     "glt_memcpy": (_i32, [_vp, _vp, _i64, _vp, _i32]),
     "glt_launch_count": (_i32, [C.POINTER(_u64)]),
     "glt_model_profile": (_i32, [_vp, _i32]),

@@ -366,12 +366,8 @@ int launch_fwd_tc(const uint16_t* qkv, uint16_t* o, float* lse, const AttnShape&
   auto k = attn_fwd_tc_kernel<HD>;
   constexpr int smem = FwdSmem<HD>::TOTAL;
   GLT_TRY(ensure_smem_attr(reinterpret_cast<const void*>(k), smem));
-  static bool carveout_set = false;   // two CTAs per SM need the full shared-memory carveout
-  if (!carveout_set) {
-    GLT_CUDA_TRY(cudaFuncSetAttribute(reinterpret_cast<const void*>(k),
-                                      cudaFuncAttributePreferredSharedMemoryCarveout, 100));
-    carveout_set = true;
-  }
+  // two CTAs per SM need the full shared-memory carveout (a per-device setting)
+  GLT_TRY(ensure_smem_carveout_max(reinterpret_cast<const void*>(k)));
   dim3 grid(s.T / AQ, s.nh, s.B);
   k<<<grid, FWD_THREADS, smem, st>>>(tq, tkv, o, lse, s, device_error_word());
   GLT_LAUNCH_CHECK();

@@ -26,6 +26,7 @@ struct NcclApi {
                             cudaStream_t) = nullptr;
   ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
   ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+  ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
   const char* (*GetErrorString)(ncclResult_t) = nullptr;
 };
 
@@ -45,6 +46,8 @@ int load_nccl() {
   g_nccl.AllReduce = reinterpret_cast<decltype(g_nccl.AllReduce)>(dlsym(h, "ncclAllReduce"));
   g_nccl.CommDestroy = reinterpret_cast<decltype(g_nccl.CommDestroy)>(dlsym(h, "ncclCommDestroy"));
   g_nccl.CommAbort = reinterpret_cast<decltype(g_nccl.CommAbort)>(dlsym(h, "ncclCommAbort"));
+  g_nccl.CommGetAsyncError =
+      reinterpret_cast<decltype(g_nccl.CommGetAsyncError)>(dlsym(h, "ncclCommGetAsyncError"));
   g_nccl.GetErrorString =
       reinterpret_cast<decltype(g_nccl.GetErrorString)>(dlsym(h, "ncclGetErrorString"));
   if (!g_nccl.GetUniqueId || !g_nccl.CommInitRank || !g_nccl.AllReduce || !g_nccl.CommDestroy)
@@ -87,6 +90,22 @@ int Model::dp_init(const void* unique_id, int rank, int world) {
     const int v = atoi(e);
     dp_bucket = v < 1 ? 1 : (v > L ? L : v);
   }
+  // GLT_DP_COMM_PRIORITY=high puts the all-reduce stream at the device's
+  // highest stream priority, so that at each kernel boundary of the backward
+  // the block scheduler starts the collective's CTAs before the next GEMM's.
+  if (const char* e = getenv("GLT_DP_COMM_PRIORITY")) {
+    if (strcmp(e, "high") == 0) {
+      int least = 0, greatest = 0;
+      GLT_CUDA_TRY(cudaDeviceGetStreamPriorityRange(&least, &greatest));
+      cudaStream_t hp = nullptr;
+      GLT_CUDA_TRY(cudaStreamCreateWithPriority(&hp, cudaStreamNonBlocking, greatest));
+      cudaStreamSynchronize(comm_stream);
+      cudaStreamDestroy(comm_stream);
+      comm_stream = hp;
+    } else if (strcmp(e, "default") != 0) {
+      return fail(GLT_EINVAL, "GLT_DP_COMM_PRIORITY=%s (high or default)", e);
+    }
+  }
   return GLT_OK;
 }
 
@@ -98,6 +117,37 @@ int Model::dp_allreduce_layers(int l0, int l1) {
   ncclResult_t r = g_nccl.AllReduce(buf, buf, n, ncclFloat32, ncclSum,
                                     static_cast<ncclComm_t>(nccl_comm), comm_stream);
   if (r != ncclSuccess) return fail(GLT_ENCCL, "ncclAllReduce: %s", nccl_err(r));
+  return GLT_OK;
+}
+
+// Asynchronous communicator state (ncclCommGetAsyncError): ncclSuccess, or
+// the error a collective of this communicator ran into.
+int Model::dp_async_error(int* nccl_result) {
+  *nccl_result = 0;
+  if (!nccl_comm || !g_nccl.CommGetAsyncError) return GLT_OK;
+  ncclResult_t r = ncclSuccess;
+  ncclResult_t q = g_nccl.CommGetAsyncError(static_cast<ncclComm_t>(nccl_comm), &r);
+  if (q != ncclSuccess) return fail(GLT_ENCCL, "ncclCommGetAsyncError: %s", nccl_err(q));
+  *nccl_result = static_cast<int>(r);
+  if (r != ncclSuccess) return fail(GLT_ENCCL, "data-parallel communicator error: %s", nccl_err(r));
+  return GLT_OK;
+}
+
+// Tears the communicator down without waiting for the other ranks
+// (ncclCommAbort): for a rank that learned on the host that a peer has left,
+// so that it neither waits in ncclCommDestroy nor starts another collective.
+// The model stays usable for one-GPU training.
+int Model::dp_abort() {
+  if (!nccl_comm) {
+    dp_world = 1;
+    return GLT_OK;
+  }
+  ncclResult_t r = ncclSuccess;
+  if (g_nccl.CommAbort) r = g_nccl.CommAbort(static_cast<ncclComm_t>(nccl_comm));
+  nccl_comm = nullptr;
+  dp_rank = 0;
+  dp_world = 1;
+  if (r != ncclSuccess) return fail(GLT_ENCCL, "ncclCommAbort: %s", nccl_err(r));
   return GLT_OK;
 }
 
@@ -126,6 +176,16 @@ extern "C" int glt_dp_unique_id(void* out, int out_bytes) {
 extern "C" int glt_dp_init(GltModel* m, const void* unique_id, int rank, int world) {
   if (!m || (!unique_id && world > 1)) return glt::fail(GLT_EINVAL, "null argument");
   return reinterpret_cast<glt::Model*>(m)->dp_init(unique_id, rank, world);
+}
+
+extern "C" int glt_dp_async_error(GltModel* m, int* nccl_result) {
+  if (!m || !nccl_result) return glt::fail(GLT_EINVAL, "null argument");
+  return reinterpret_cast<glt::Model*>(m)->dp_async_error(nccl_result);
+}
+
+extern "C" int glt_dp_abort(GltModel* m) {
+  if (!m) return glt::fail(GLT_EINVAL, "null model");
+  return reinterpret_cast<glt::Model*>(m)->dp_abort();
 }
 
 extern "C" int glt_dp_finalize(GltModel* m) {

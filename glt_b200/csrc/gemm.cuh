@@ -46,6 +46,8 @@ struct ScopedTileCounter {
 };
 // Sets the dynamic-smem attribute of `func` to `bytes` once per (device, function).
 int ensure_smem_attr(const void* func, int bytes);
+// Prefers the largest shared-memory carveout for `func`, once per (device, function).
+int ensure_smem_carveout_max(const void* func);
 
 // ---------------------------------------------------------------------------
 // Launcher

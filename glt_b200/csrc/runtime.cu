@@ -11,6 +11,7 @@
 #include <atomic>
 #include <map>
 #include <mutex>
+#include <set>
 #include <unordered_map>
 #include <utility>
 
@@ -81,6 +82,17 @@ int ensure_smem_attr(const void* func, int bytes) {
   if (e != cudaSuccess)
     return fail(GLT_ECUDA, "cudaFuncSetAttribute(smem=%d): %s", bytes, cudaGetErrorString(e));
   done[key] = bytes;
+  return GLT_OK;
+}
+
+int ensure_smem_carveout_max(const void* func) {
+  int dev = 0;
+  GLT_CUDA_TRY(cudaGetDevice(&dev));
+  static std::set<std::pair<int, const void*>> done;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (done.count(std::make_pair(dev, func))) return GLT_OK;
+  GLT_CUDA_TRY(cudaFuncSetAttribute(func, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+  done.insert(std::make_pair(dev, func));
   return GLT_OK;
 }
 

@@ -257,3 +257,76 @@ class GraftModel:
 
     def dp_finalize(self) -> None:
         check(lib.glt_dp_finalize(self.handle))
+
+    def dp_async_error(self) -> int:
+        """The communicator's asynchronous NCCL result (0 = ncclSuccess)."""
+        r = C.c_int32()
+        st = lib.glt_dp_async_error(self.handle, C.byref(r))
+        if st != GLT_OK and r.value == 0:
+            check(st)
+        return r.value
+
+    def dp_abort(self) -> None:
+        """Abort the data-parallel communicator without waiting for the other
+        ranks (a peer has left); the model then trains on its own GPU."""
+        check(lib.glt_dp_abort(self.handle))
+
+
+class PeerLost(RuntimeError):
+    """A data-parallel peer left or stopped posting steps."""
+
+    def __init__(self, peer: int, last_step: int, wanted: int, left: bool):
+        what = "left" if left else f"posted step {last_step} and nothing newer"
+        super().__init__(f"rank {peer} {what}; step {wanted} was expected")
+        self.peer, self.last_step, self.wanted, self.left = peer, last_step, wanted, left
+
+
+class PeerMonitor:
+    """Host-side liveness of the data-parallel ranks, checked between steps.
+
+    The library's all-reduce runs inside the training step; a peer that has
+    crashed or left would make the others' next collective wait for it.  Each
+    rank posts the index of every step it has finished to the job's key-value
+    store (a torch.distributed Store, e.g. a TCPStore); before a rank enqueues
+    step k it checks that every peer has finished step k-1, and raises
+    PeerLost -- with no collective in flight -- when a peer has posted its
+    leave marker or has been silent for `timeout_s`.  The caller then aborts
+    the communicator (GraftModel.dp_abort) and exits or trains alone.  The
+    reference is single-GPU and has no counterpart."""
+
+    def __init__(self, store, rank: int, world: int, timeout_s: float = 60.0, prefix: str = "glt_dp"):
+        self.store, self.rank, self.world = store, rank, world
+        self.timeout_s, self.prefix = timeout_s, prefix
+
+    def _key(self, kind: str, r: int) -> str:
+        return f"{self.prefix}/{kind}/{r}"
+
+    def _read(self, key: str) -> int | None:
+        return int(self.store.get(key)) if self.store.check([key]) else None
+
+    def beat(self, step: int) -> None:
+        """This rank has finished `step`."""
+        self.store.set(self._key("step", self.rank), str(int(step)))
+
+    def leave(self) -> None:
+        """This rank takes no further steps: peers waiting for a later step raise
+        PeerLost at once instead of after the timeout."""
+        self.store.set(self._key("left", self.rank), "1")
+
+    def wait_peers(self, step: int) -> None:
+        """Return once every peer has finished `step`; raise PeerLost otherwise."""
+        import time
+        deadline = time.monotonic() + self.timeout_s
+        for r in range(self.world):
+            if r == self.rank:
+                continue
+            while True:
+                last = self._read(self._key("step", r))
+                last = -1 if last is None else last
+                if last >= step:
+                    break
+                if self._read(self._key("left", r)) is not None:
+                    raise PeerLost(r, last, step, True)
+                if time.monotonic() > deadline:
+                    raise PeerLost(r, last, step, False)
+                time.sleep(0.005)

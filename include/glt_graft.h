@@ -658,6 +658,14 @@ GLT_API int glt_batch_step(const int32_t* domain_tokens, int n_domain, const int
 GLT_API int glt_dp_unique_id(void* out, int out_bytes); /* out_bytes >= 128 */
 GLT_API int glt_dp_init(GltModel* m, const void* unique_id, int rank, int world);
 GLT_API int glt_dp_finalize(GltModel* m);
+/* Failure handling between steps.  glt_dp_async_error: the communicator's  */
+/* asynchronous state (ncclCommGetAsyncError) in *nccl_result; GLT_ENCCL    */
+/* when a collective failed.  glt_dp_abort: tears the communicator down     */
+/* without waiting for the other ranks (ncclCommAbort), for a rank that     */
+/* learned on the host that a peer has left (glt_b200.graft.PeerMonitor);   */
+/* call it with no step in flight.  The model then trains on its own GPU.   */
+GLT_API int glt_dp_async_error(GltModel* m, int* nccl_result);
+GLT_API int glt_dp_abort(GltModel* m);
 
 #ifdef __cplusplus
 }

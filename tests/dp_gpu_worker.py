@@ -7,7 +7,9 @@ microbatch (seed 500 + rank), joins the library's NCCL communicator
 step: the graft gradients are all-reduced in layer buckets during the
 backward, then clip and AdamW run on every rank.  It saves its ids, the
 summed gradients, the updated graft and the step statistics to
-<out_dir>/rank<r>.pt for the parent test to check.
+<out_dir>/rank<r>.pt for the parent test to check; then, with no
+collective in flight, it aborts the communicator (glt_dp_abort, the path of
+a rank whose peer has left) and runs one more step on its own GPU.
 
     python -m torch.distributed.run --nproc-per-node 2 tests/dp_gpu_worker.py OUT_DIR
 """
@@ -66,7 +68,12 @@ def main():
     st = m.train_step(ids, ood, step=0, total_steps=10)
     torch.cuda.synchronize()
     out = dict(ids=ids, ood=ood, grad=m.read_graft("grad").cpu(), weight=m.read_graft("weight").cpu(),
-               stats=st)
+               stats=st, async_error=m.dp_async_error())
+    # between steps, no collective in flight: a rank that learned on the host
+    # that a peer left aborts the communicator and carries on alone
+    m.dp_abort()
+    out["solo_stats"] = m.train_step(ids, ood, step=1, total_steps=10)
+    out["solo_grad"] = m.read_graft("grad").cpu()
     m.dp_finalize()
     m.close()
     torch.save(out, os.path.join(out_dir, f"rank{rank}.pt"))

@@ -7,6 +7,7 @@ grads of its own microbatch, sums them with all_reduce, and the resulting
 replicated update must equal the update from the mean of both ranks' grads
 computed in one process; it also checks the max-over-ranks timing reduction
 that bench.py uses."""
+import datetime
 import os
 
 import pytest
@@ -82,3 +83,54 @@ def test_two_rank_graft_grad_allreduce_matches_mean():
     ref = _update_from_mean_grad(cfg, delta, gsum, world)
     torch.testing.assert_close(res[0][1], ref, rtol=1e-6, atol=1e-9)
     assert res[0][2] == pytest.approx(0.2) and res[1][2] == pytest.approx(0.2)
+
+
+def _monitor_worker(rank, world, port, mode, q):
+    """Rank 1 finishes steps 0 and 1, then leaves (posting its leave marker)
+    or goes silent (a crash); rank 0 keeps stepping and must learn of it
+    before it would start step 3's collectives."""
+    import time
+    from torch.distributed import TCPStore
+
+    from glt_b200.graft import PeerLost, PeerMonitor
+    store = TCPStore("127.0.0.1", port, world, is_master=(rank == 0), timeout=datetime.timedelta(seconds=30))
+    mon = PeerMonitor(store, rank, world, timeout_s=1.0)
+    last_done = -1
+    try:
+        for step in range(6):
+            if step > 0:
+                mon.wait_peers(step - 1)          # every peer finished the previous step
+            if rank == 1 and step == 2:
+                if mode == "leave":
+                    mon.leave()
+                q.put((rank, "stopped", step, None))
+                return
+            time.sleep(0.02)                      # the step's work
+            mon.beat(step)
+            last_done = step
+        q.put((rank, "finished", last_done, None))
+    except PeerLost as e:
+        q.put((rank, "peer_lost", last_done, (e.peer, e.last_step, e.wanted, e.left)))
+    finally:
+        if rank == 0:
+            time.sleep(0.5)                       # the store outlives its client
+
+
+@pytest.mark.parametrize("mode", ["leave", "silent"])
+def test_peer_monitor_detects_a_rank_that_leaves(mode):
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 31500 + (os.getpid() % 2000) + (0 if mode == "leave" else 1)
+    procs = [ctx.Process(target=_monitor_worker, args=(r, world, port, mode, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {r[0]: r for r in (q.get(timeout=60) for _ in range(world))}
+    for p in procs:
+        p.join(timeout=30)
+        assert p.exitcode == 0
+    assert res[1][1] == "stopped"
+    kind, last_done, info = res[0][1], res[0][2], res[0][3]
+    assert kind == "peer_lost"
+    assert last_done == 2                          # rank 0 finished step 2, then stopped before step 3
+    assert info == (1, 1, 2, mode == "leave")      # rank 1 last finished step 1; step 2 was awaited

@@ -83,3 +83,9 @@ def test_two_rank_step_matches_single_process_mean_update(tmp_path):
     rm.clip_grads(g, rc.gradient_clip_norm)
     rm.adamw(w_ref, g, torch.zeros_like(w_ref), torch.zeros_like(w_ref), 0, rc.get_lr(0, 10), rc)
     torch.testing.assert_close(ranks[0]["weight"], w_ref, rtol=1e-5, atol=1e-8)
+    # after glt_dp_abort each rank trains alone: its next gradient is its own
+    for r in range(world):
+        assert ranks[r]["async_error"] == 0
+        assert ranks[r]["solo_stats"]["total_loss"] > 0
+        assert not torch.equal(ranks[r]["solo_grad"], ranks[0]["grad"])
+    assert not torch.equal(ranks[0]["solo_grad"], ranks[1]["solo_grad"])

@@ -92,6 +92,7 @@ SIGNATURES: dict[str, tuple] = {
     "glt_selftest_wait_timeout": (_i32, [_i32, _i32, _vp]),
     "glt_gemm": (_i32, [_vp, _i64, _i32, _vp, _i64, _i32, _vp, _i64, _i32,
                         _i32, _i32, _i32, _f32, _f32, _vp]),
+    "glt_gemm_pair_mode": (_i32, [_i32]),
     "glt_config_default": (_i32, [_cfgp]),
     "glt_config_validate": (_i32, [_cfgp, _i32, _i32]),
     "glt_get_lr": (_f32, [_cfgp, _i32, _i32]),

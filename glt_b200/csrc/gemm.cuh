@@ -5,6 +5,7 @@
 #include <climits>
 
 #include "tc_gemm.cuh"
+#include "tc_gemm_pair.cuh"
 
 namespace glt {
 
@@ -48,6 +49,14 @@ struct ScopedTileCounter {
 int ensure_smem_attr(const void* func, int bytes);
 // Prefers the largest shared-memory carveout for `func`, once per (device, function).
 int ensure_smem_carveout_max(const void* func);
+// Number of two-CTA clusters of `func` (threads, dynamic smem) resident at
+// once on this device, cached per (device, function).
+int max_active_pairs(const void* func, int threads, int smem, int* pairs);
+
+// Whether launch_gemm runs its 256-column GEMMs on CTA pairs
+// (tc_gemm_pair.cuh); glt_gemm_pair_mode sets it, GLT_GEMM_PAIR=0 in the
+// environment turns the default (on) off.
+bool gemm_pair_mode();
 
 // ---------------------------------------------------------------------------
 // Launcher
@@ -60,6 +69,89 @@ int ensure_smem_carveout_max(const void* func);
 // K = 4096 weight such as W_gu (252 MB) streams from HBM once per 32 m-tiles
 // rather than once per 8; at the config-3 step this is worth ~1.5% under the
 // 1 kW power cap (less DRAM energy, same tensor work).
+// Deepest stage ring of 32 KB stages (at most 8) that fits beside the
+// barriers and the epilogue's scratch.
+template <class Epi>
+constexpr int pair_stages() {
+  constexpr int scratch = 4 * tc::EpiParts<Epi>::value * tc::EpiScratch<Epi>::value;
+  constexpr int avail = 232448 - 64 - 1024 - 512 - scratch;
+  constexpr int s = avail / static_cast<int>(tc::PairSmemLayout<1>::STAGE_BYTES);
+  return s > 8 ? 8 : s;
+}
+
+// The same contraction on CTA pairs: 256 x 256 output tiles, each CTA of a
+// pair staging 128 rows of A and 128 rows of B per k-block.  group_m counts
+// 256-row tiles.  Static round-robin schedule over clusters.
+template <bool A_MN, bool B_MN, class Epi>
+int launch_gemm_pair(const Operand& A, const Operand& B, int M, int N, int K, const Epi& epi,
+                     cudaStream_t stream, int k_splits, const Operand* A2, int a2_n_tile,
+                     int group_m, const int* m_dev, int m_off, unsigned int* err, uint64_t timeout_ns) {
+  using namespace tc;
+  constexpr int STAGES = pair_stages<Epi>();
+  static_assert(STAGES >= 3, "pair GEMM: too little shared memory for the stage ring");
+  if (M <= 0 || N <= 0 || K <= 0) return GLT_OK;
+  if (A.mn_major != A_MN || B.mn_major != B_MN)
+    return fail(GLT_EINVAL, "launch_gemm_pair: operand major-ness mismatch");
+  CUtensorMap ta, ta2, tb;
+  if (!A_MN) {
+    GLT_TRY(make_tmap_bf16(&ta, A.ptr, K, M, A.ld, BM));
+  } else {
+    GLT_TRY(make_tmap_bf16(&ta, A.ptr, M, K, A.ld, 64));
+  }
+  if (A2) {
+    if (A2->mn_major != A_MN) return fail(GLT_EINVAL, "launch_gemm_pair: A2 major-ness mismatch");
+    if (!A_MN) {
+      GLT_TRY(make_tmap_bf16(&ta2, A2->ptr, K, M, A2->ld, BM));
+    } else {
+      GLT_TRY(make_tmap_bf16(&ta2, A2->ptr, M, K, A2->ld, 64));
+    }
+  } else {
+    ta2 = ta;
+  }
+  if (!B_MN) {
+    GLT_TRY(make_tmap_bf16(&tb, B.ptr, K, N, B.ld, PAIR_BN / 2));
+  } else {
+    GLT_TRY(make_tmap_bf16(&tb, B.ptr, N, K, B.ld, 64));
+  }
+  GemmShape shape;
+  shape.M = M;
+  shape.N = N;
+  shape.K = K;
+  shape.k_splits = k_splits < 1 ? 1 : k_splits;
+  shape.a2_n_tile = A2 ? a2_n_tile : INT_MAX;
+  shape.group_m = group_m < 1 ? 1 : group_m;
+  shape.m_dev = m_dev;
+  shape.m_off = m_off;
+  shape.tile_ctr = nullptr;
+  shape.err = err ? err : device_error_word();
+  if (!shape.err) return fail(GLT_ECUDA, "device error word unavailable");
+  shape.timeout_ns = timeout_ns;
+  shape.selftest_skip_first_load = 0;
+  auto kern = tc_gemm_pair_kernel<STAGES, A_MN, B_MN, Epi>;
+  constexpr int smem = gemm_pair_smem_bytes<STAGES, Epi>();
+  constexpr int threads = gemm_threads<Epi>();
+  GLT_TRY(ensure_smem_attr(reinterpret_cast<const void*>(kern), smem));
+  int pairs = 0;
+  GLT_TRY(max_active_pairs(reinterpret_cast<const void*>(kern), threads, smem, &pairs));
+  const int units = ((M + PAIR_BM - 1) / PAIR_BM) * ((N + PAIR_BN - 1) / PAIR_BN) * shape.k_splits;
+  const int clusters = units < pairs ? units : pairs;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * clusters);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  GLT_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, ta, ta2, tb, shape, epi));
+  GLT_LAUNCH_CHECK();
+  return GLT_OK;
+}
+
 template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi>
 int launch_gemm(const Operand& A, const Operand& B, int M, int N, int K, const Epi& epi,
                 cudaStream_t stream, int k_splits = 1, const Operand* A2 = nullptr,
@@ -70,6 +162,11 @@ int launch_gemm(const Operand& A, const Operand& B, int M, int N, int K, const E
   if (M <= 0 || N <= 0 || K <= 0) return GLT_OK;
   if (A.mn_major != A_MN || B.mn_major != B_MN)
     return fail(GLT_EINVAL, "launch_gemm: operand major-ness mismatch");
+  if constexpr (BN == 256) {
+    if (gemm_pair_mode() && gemm_tile_counter() == nullptr && selftest_skip_first_load == 0)
+      return launch_gemm_pair<A_MN, B_MN>(A, B, M, N, K, epi, stream, k_splits, A2, a2_n_tile,
+                                          (group_m + 1) / 2, m_dev, m_off, err, timeout_ns);
+  }
   CUtensorMap ta, ta2, tb;
   // A: K-major [M][K] -> dims {K, M}, box {64, 128};  MN-major [K][M] -> {M, K}, box {64, 64}
   if (!A_MN) {

@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 #include <stdarg.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <atomic>
@@ -94,6 +95,56 @@ int ensure_smem_carveout_max(const void* func) {
   GLT_CUDA_TRY(cudaFuncSetAttribute(func, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
   done.insert(std::make_pair(dev, func));
   return GLT_OK;
+}
+
+int max_active_pairs(const void* func, int threads, int smem, int* pairs) {
+  // clusters of two CTAs that can be resident at once (one CTA per SM at
+  // this shared-memory size; pairs must share a GPC), per (device, function)
+  int dev = 0;
+  GLT_CUDA_TRY(cudaGetDevice(&dev));
+  static std::map<std::pair<int, const void*>, int> done;
+  std::lock_guard<std::mutex> lk(g_mu);
+  const auto key = std::make_pair(dev, func);
+  auto it = done.find(key);
+  if (it != done.end()) {
+    *pairs = it->second;
+    return GLT_OK;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * 1024);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  cudaError_t e = cudaOccupancyMaxActiveClusters(&n, func, &cfg);
+  if (e != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    return fail(GLT_ECUDA, "cudaOccupancyMaxActiveClusters: %s (%d)", cudaGetErrorString(e), n);
+  }
+  done[key] = n;
+  *pairs = n;
+  return GLT_OK;
+}
+
+static std::atomic<int>& pair_mode_flag() {
+  static std::atomic<int> on([] {
+    const char* e = getenv("GLT_GEMM_PAIR");
+    return (e != nullptr && e[0] == '0') ? 0 : 1;
+  }());
+  return on;
+}
+
+bool gemm_pair_mode() { return pair_mode_flag().load(std::memory_order_relaxed) != 0; }
+
+extern "C" GLT_API int glt_gemm_pair_mode(int mode) {
+  if (mode == 0 || mode == 1) pair_mode_flag().store(mode);
+  return pair_mode_flag().load();
 }
 
 int status_from_device_error(unsigned int code, const char* where) {

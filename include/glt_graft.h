@@ -102,6 +102,14 @@ GLT_API int glt_device_memory(int64_t* used_bytes, int64_t* total_bytes);
 GLT_API int glt_gemm(const void* A, int64_t lda, int a_mn, const void* B, int64_t ldb, int b_mn,
              void* C, int64_t ldc, int c_dtype, int M, int N, int K, float alpha, float beta,
              void* stream);
+/* Tile shape of the library's 256-column GEMMs (every call above and every */
+/* GEMM of a model step): mode 1 runs them on CTA pairs                     */
+/* (tcgen05.mma.cta_group::2, 256 x 256 tiles, 128 rows of A and B staged   */
+/* per CTA), mode 0 on single CTAs (128 x 256 tiles).  -1 only queries.     */
+/* Returns the mode in force.  Default 1; the environment variable          */
+/* GLT_GEMM_PAIR=0 at the first call makes it 0.  Process-wide; change it   */
+/* only while no GEMM is being enqueued.                                    */
+GLT_API int glt_gemm_pair_mode(int mode);
 
 
 /* ------------------------------------------------------------------------ */

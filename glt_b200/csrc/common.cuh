@@ -4,8 +4,12 @@
 //  * bf16 rounding is the bias trick `bits += ((bits>>16)&1) + 0x7FFF`
 //    (src/kernels_elementwise_impl.inc:575-580, src/gemm_impl.inc:69-80,
 //    src/checkpoint_impl.inc:49-57).  It equals IEEE RNE for every finite
-//    value and differs only in NaN payload handling, so every bf16 store in
-//    this library uses it to stay bit-identical with the reference files.
+//    value and differs only in NaN payload handling, so the bf16 stores that
+//    reach files or the reference's element-wise entry points use it to stay
+//    bit-identical with the reference.  The GEMM and attention epilogues,
+//    whose outputs are intermediate activations, round with the hardware
+//    RNE conversion (pack_bf16x2_rn): one instruction per two values, the
+//    same bits for every finite value.
 //  * Errors never throw across the C ABI: every entry point returns a
 //    GltStatus and records a message readable through glt_last_error().
 #pragma once

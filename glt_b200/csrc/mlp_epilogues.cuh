@@ -16,7 +16,11 @@
 
 namespace glt {
 
-__device__ __forceinline__ float sigmoidf_(float x) { return 1.f / (1.f + __expf(-x)); }
+// Logistic sigmoid for the GEMM epilogues: exp on the special-function unit
+// and the fast (reciprocal-based) division; its error (a few ulp of fp32)
+// stays far below the bf16 rounding every epilogue output gets.  The
+// stand-alone SwiGLU ops (ops_elementwise.cu) keep expf and IEEE division.
+__device__ __forceinline__ float sigmoidf_(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
 
 // Layout of the stored gate_pre/up (EpiSwiGLUFwd::gu, EpiSwiGLUBwdStored):
 // a private buffer, so it is laid out for the epilogues' access pattern, in
@@ -97,8 +101,8 @@ struct EpiSwiGLUFwd {
         float o[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) o[k] = g[i + k] * sigmoidf_(g[i + k]) * u[i + k];
-        stage_put(c.scratch, 0, i / 8, make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]),
-                                                   pack_bf16x2(o[4], o[5]), pack_bf16x2(o[6], o[7])));
+        stage_put(c.scratch, 0, i / 8, make_uint4(pack_bf16x2_rn(o[0], o[1]), pack_bf16x2_rn(o[2], o[3]),
+                                                   pack_bf16x2_rn(o[4], o[5]), pack_bf16x2_rn(o[6], o[7])));
       }
       uint16_t* const hdst[1] = {h + static_cast<int64_t>(band0) * ldh + cb + j};
       stage_flush<1>(c.scratch, hdst, ldh, M - band0);
@@ -108,10 +112,10 @@ struct EpiSwiGLUFwd {
 #pragma unroll
           for (int i = 0; i < 32; i += 8) {
             uint4 a, b;
-            a.x = pack_bf16x2(g[i], g[i + 1]); a.y = pack_bf16x2(g[i + 2], g[i + 3]);
-            a.z = pack_bf16x2(g[i + 4], g[i + 5]); a.w = pack_bf16x2(g[i + 6], g[i + 7]);
-            b.x = pack_bf16x2(u[i], u[i + 1]); b.y = pack_bf16x2(u[i + 2], u[i + 3]);
-            b.z = pack_bf16x2(u[i + 4], u[i + 5]); b.w = pack_bf16x2(u[i + 6], u[i + 7]);
+            a.x = pack_bf16x2_rn(g[i], g[i + 1]); a.y = pack_bf16x2_rn(g[i + 2], g[i + 3]);
+            a.z = pack_bf16x2_rn(g[i + 4], g[i + 5]); a.w = pack_bf16x2_rn(g[i + 6], g[i + 7]);
+            b.x = pack_bf16x2_rn(u[i], u[i + 1]); b.y = pack_bf16x2_rn(u[i + 2], u[i + 3]);
+            b.z = pack_bf16x2_rn(u[i + 4], u[i + 5]); b.w = pack_bf16x2_rn(u[i + 6], u[i + 7]);
             // streaming stores: read once, a whole forward/backward later
             __stcs(reinterpret_cast<uint4*>(gu + gu_block_offset(c.row, g8 + i / 8, gu_groups)), a);
             __stcs(reinterpret_cast<uint4*>(gu + gu_block_offset(c.row, g8 + 16 + i / 8, gu_groups)), b);
@@ -217,10 +221,10 @@ struct EpiSwiGLUBwd {
           }
         }
         uint4 a, b;
-        a.x = pack_bf16x2(og[0], og[1]); a.y = pack_bf16x2(og[2], og[3]);
-        a.z = pack_bf16x2(og[4], og[5]); a.w = pack_bf16x2(og[6], og[7]);
-        b.x = pack_bf16x2(ou[0], ou[1]); b.y = pack_bf16x2(ou[2], ou[3]);
-        b.z = pack_bf16x2(ou[4], ou[5]); b.w = pack_bf16x2(ou[6], ou[7]);
+        a.x = pack_bf16x2_rn(og[0], og[1]); a.y = pack_bf16x2_rn(og[2], og[3]);
+        a.z = pack_bf16x2_rn(og[4], og[5]); a.w = pack_bf16x2_rn(og[6], og[7]);
+        b.x = pack_bf16x2_rn(ou[0], ou[1]); b.y = pack_bf16x2_rn(ou[2], ou[3]);
+        b.z = pack_bf16x2_rn(ou[4], ou[5]); b.w = pack_bf16x2_rn(ou[6], ou[7]);
         *reinterpret_cast<uint4*>(dgr + i) = a;
         *reinterpret_cast<uint4*>(dgr + 128 + i) = b;
       }
@@ -321,10 +325,10 @@ struct EpiSwiGLUBwdStored {
             }
           }
         }
-        stage_put(c.scratch, 0, q, make_uint4(pack_bf16x2(og[0], og[1]), pack_bf16x2(og[2], og[3]),
-                                              pack_bf16x2(og[4], og[5]), pack_bf16x2(og[6], og[7])));
-        stage_put(c.scratch, 1, q, make_uint4(pack_bf16x2(ou[0], ou[1]), pack_bf16x2(ou[2], ou[3]),
-                                              pack_bf16x2(ou[4], ou[5]), pack_bf16x2(ou[6], ou[7])));
+        stage_put(c.scratch, 0, q, make_uint4(pack_bf16x2_rn(og[0], og[1]), pack_bf16x2_rn(og[2], og[3]),
+                                              pack_bf16x2_rn(og[4], og[5]), pack_bf16x2_rn(og[6], og[7])));
+        stage_put(c.scratch, 1, q, make_uint4(pack_bf16x2_rn(ou[0], ou[1]), pack_bf16x2_rn(ou[2], ou[3]),
+                                              pack_bf16x2_rn(ou[4], ou[5]), pack_bf16x2_rn(ou[6], ou[7])));
       }
       uint16_t* const g_dst = dgu + static_cast<int64_t>(band0) * ldgu_out + pos(col0);
       uint16_t* const dsts[2] = {g_dst, g_dst + 128};
@@ -352,8 +356,8 @@ struct EpiDeltaDown {
 #pragma unroll
       for (int i = 0; i < 32; i += 8) {
         uint4 w;
-        w.x = pack_bf16x2(v[i], v[i + 1]); w.y = pack_bf16x2(v[i + 2], v[i + 3]);
-        w.z = pack_bf16x2(v[i + 4], v[i + 5]); w.w = pack_bf16x2(v[i + 6], v[i + 7]);
+        w.x = pack_bf16x2_rn(v[i], v[i + 1]); w.y = pack_bf16x2_rn(v[i + 2], v[i + 3]);
+        w.z = pack_bf16x2_rn(v[i + 4], v[i + 5]); w.w = pack_bf16x2_rn(v[i + 6], v[i + 7]);
         *reinterpret_cast<uint4*>(dst + i) = w;
       }
 #pragma unroll
@@ -436,8 +440,8 @@ struct EpiDeltaF32 {
         *reinterpret_cast<float4*>(dst + 4) = make_float4(v[i + 4], v[i + 5], v[i + 6], v[i + 7]);
         if (Cb) {
           uint4 w;
-          w.x = pack_bf16x2(v[i], v[i + 1]); w.y = pack_bf16x2(v[i + 2], v[i + 3]);
-          w.z = pack_bf16x2(v[i + 4], v[i + 5]); w.w = pack_bf16x2(v[i + 6], v[i + 7]);
+          w.x = pack_bf16x2_rn(v[i], v[i + 1]); w.y = pack_bf16x2_rn(v[i + 2], v[i + 3]);
+          w.z = pack_bf16x2_rn(v[i + 4], v[i + 5]); w.w = pack_bf16x2_rn(v[i + 6], v[i + 7]);
           *reinterpret_cast<uint4*>(Cb + static_cast<int64_t>(c.row) * ldcb + col) = w;
         }
         float ss = 0.f;

@@ -344,10 +344,10 @@ struct EpiBF16 {
 #pragma unroll
         for (int i = 0; i < 32; i += 8) {
           uint4 o;
-          o.x = pack_bf16x2(v[i + 0], v[i + 1]);
-          o.y = pack_bf16x2(v[i + 2], v[i + 3]);
-          o.z = pack_bf16x2(v[i + 4], v[i + 5]);
-          o.w = pack_bf16x2(v[i + 6], v[i + 7]);
+          o.x = pack_bf16x2_rn(v[i + 0], v[i + 1]);
+          o.y = pack_bf16x2_rn(v[i + 2], v[i + 3]);
+          o.z = pack_bf16x2_rn(v[i + 4], v[i + 5]);
+          o.w = pack_bf16x2_rn(v[i + 6], v[i + 7]);
           *reinterpret_cast<uint4*>(dst + i) = o;
         }
       } else {
@@ -412,10 +412,10 @@ struct EpiBF16Rope {
         uint16_t* d2 = d1 + half;
 #pragma unroll
         for (int i = 0; i < 32; i += 8) {
-          *reinterpret_cast<uint4*>(d1 + i) = make_uint4(pack_bf16x2(a[i], a[i + 1]), pack_bf16x2(a[i + 2], a[i + 3]),
-                                                         pack_bf16x2(a[i + 4], a[i + 5]), pack_bf16x2(a[i + 6], a[i + 7]));
-          *reinterpret_cast<uint4*>(d2 + i) = make_uint4(pack_bf16x2(b[i], b[i + 1]), pack_bf16x2(b[i + 2], b[i + 3]),
-                                                         pack_bf16x2(b[i + 4], b[i + 5]), pack_bf16x2(b[i + 6], b[i + 7]));
+          *reinterpret_cast<uint4*>(d1 + i) = make_uint4(pack_bf16x2_rn(a[i], a[i + 1]), pack_bf16x2_rn(a[i + 2], a[i + 3]),
+                                                         pack_bf16x2_rn(a[i + 4], a[i + 5]), pack_bf16x2_rn(a[i + 6], a[i + 7]));
+          *reinterpret_cast<uint4*>(d2 + i) = make_uint4(pack_bf16x2_rn(b[i], b[i + 1]), pack_bf16x2_rn(b[i + 2], b[i + 3]),
+                                                         pack_bf16x2_rn(b[i + 4], b[i + 5]), pack_bf16x2_rn(b[i + 6], b[i + 7]));
         }
       }
     }
@@ -452,8 +452,8 @@ struct EpiBF16Dsum {
 #pragma unroll
         for (int i = 0; i < 32; i += 8) {
           uint4 w;
-          w.x = pack_bf16x2(v[i], v[i + 1]); w.y = pack_bf16x2(v[i + 2], v[i + 3]);
-          w.z = pack_bf16x2(v[i + 4], v[i + 5]); w.w = pack_bf16x2(v[i + 6], v[i + 7]);
+          w.x = pack_bf16x2_rn(v[i], v[i + 1]); w.y = pack_bf16x2_rn(v[i + 2], v[i + 3]);
+          w.z = pack_bf16x2_rn(v[i + 4], v[i + 5]); w.w = pack_bf16x2_rn(v[i + 6], v[i + 7]);
           *reinterpret_cast<uint4*>(dst + i) = w;
           const uint4 o = __ldg(orow + i / 8);
           acc += bf16_lo(w.x) * bf16_lo(o.x) + bf16_hi(w.x) * bf16_hi(o.x) + bf16_lo(w.y) * bf16_lo(o.y) +

@@ -15,7 +15,7 @@ from dataclasses import dataclass, field, fields
 import torch
 
 from . import _lib
-from ._lib import GltModelConfig, GltStepStats, GltEvalStats, check, lib
+from ._lib import GLT_OK, GltModelConfig, GltStepStats, GltEvalStats, check, lib
 
 LAYOUT_OVERLAY, LAYOUT_CONCAT = 0, 1
 MODEL_DECODER, MODEL_MLP_BLOCK = 0, 1

@@ -225,10 +225,15 @@ def nccl_summary(path):
     except OSError:
         return {"log": "unavailable"}
     picks = {}
-    for m in re.finditer(r"AllReduce: (\d+) Bytes -> Algo (\d+) proto (\d+)", text):
+    # NCCL prints the algorithm and protocol by index (older releases) or by
+    # name (2.2x: "Algo RING proto SIMPLE")
+    def name(table, v):
+        return table.get(int(v), v) if v.isdigit() else v
+
+    for m in re.finditer(r"AllReduce: (\d+) Bytes -> Algo (\w+) proto (\w+)", text):
         key = f"{int(m.group(1))} B"
-        picks.setdefault(key, {"algo": NCCL_ALGOS.get(int(m.group(2)), m.group(2)),
-                               "proto": NCCL_PROTOS.get(int(m.group(3)), m.group(3)), "calls": 0})
+        picks.setdefault(key, {"algo": name(NCCL_ALGOS, m.group(2)),
+                               "proto": name(NCCL_PROTOS, m.group(3)), "calls": 0})
         picks[key]["calls"] += 1
     nvls = [ln.split("NCCL INFO")[-1].strip() for ln in text.splitlines() if "NVLS" in ln][:4]
     tuning = [ln.split("NCCL INFO")[-1].strip() for ln in text.splitlines() if " Algo " in ln][:3]

@@ -55,14 +55,17 @@ METRIC = "graft-train tokens/s at Llama-3-8B shape, 1-8 B200; MLP GEMM % of bf16
 # ncu DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one
 # gate/up GEMM launch at the config-3 layer shape (M = 32768 tokens, K = 4096,
 # N = 2F' = 30720), captured on the identical launch of `python -m
-# glt_b200.mlp_bench --tokens 32768 --slice 1024` (the full training step is
-# too large for a capture under the profiling rules):
-#   MLP store on:  2,496,413,184 B read + 2,991,854,080 B written; algorithmic
-#                  3.54 GB (x 268 MB + W_gu 252 MB read, h 1007 MB + bf16
-#                  gate_pre/up 2014 MB written);
-#   recompute:     2,329,381,376 B read + 996,020,480 B written; algorithmic
-#                  1.53 GB (no gate_pre/up written).
-GATE_UP_TRAFFIC_BYTES = {True: 2496413184 + 2991854080, False: 2329381376 + 996020480}
+# glt_b200.mlp_bench --tokens 32768 --slice 1024 [--mlp-store 0]` (the full
+# training step is too large for a capture under the profiling rules), keyed
+# by (CTA-pair GEMMs, MLP store); algorithmic bytes 3.54 GB with the store
+# (x 268 MB + W_gu 252 MB read, h 1007 MB + bf16 gate_pre/up 2014 MB
+# written), 1.53 GB without:
+#   pairs, store on:      3,356,551,424 B read + 2,997,146,368 B written
+#   pairs, recompute:     4,736,081,152 B read + 1,001,093,888 B written
+#   one SM, store on:     2,496,413,184 B read + 2,991,854,080 B written
+#   one SM, recompute:    2,329,381,376 B read +   996,020,480 B written
+GATE_UP_TRAFFIC_BYTES = {(True, True): 3356551424 + 2997146368, (True, False): 4736081152 + 1001093888,
+                         (False, True): 2496413184 + 2991854080, (False, False): 2329381376 + 996020480}
 
 
 def peaks():
@@ -385,12 +388,14 @@ def main():
     mlp_ms = sum(kms[k] for k in mlp_kinds) / args.steps
     store_on, store_bytes = model.mlp_store()
     mlp_exec = mlp_alg + (2.0 * D * S + (0.0 if store_on else 4.0 * D * Fp)) * M * L  # + delta_down (+ recompute)
+    pair = _lib.lib.glt_gemm_pair_mode(-1) == 1
     roofline = {
-        "kernel": "tc_gemm_kernel<256,4,K,K,EpiSwiGLUFwd> (gate/up GEMM + fused SwiGLU)",
+        "kernel": ("tc_gemm_pair_kernel<6,K,K,EpiSwiGLUFwd> (gate/up GEMM + fused SwiGLU, CTA pairs)" if pair
+                   else "tc_gemm_kernel<256,4,K,K,EpiSwiGLUFwd> (gate/up GEMM + fused SwiGLU)"),
         "bound": "tensor", "achieved": achieved, "peak": pk["tf_sus"], "unit": "TFLOP/s",
         "frac": achieved / pk["tf_sus"],
         "peak_note": f"{pk['src']} bf16_tflops_sustained (kernel timed inside a long step)",
-        "traffic": GATE_UP_TRAFFIC_BYTES[store_on],
+        "traffic": GATE_UP_TRAFFIC_BYTES[(pair, bool(store_on))],
         "algorithmic_flops_per_launch": gu_flops, "avg_launch_ms": gu_ms,
         "timing": "CUDA events around every launch on its stream, over a second pass of the "
                   f"same {args.steps} steps ({profiled_ms:.1f} ms per step with the events)",

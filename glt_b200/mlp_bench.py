@@ -1,7 +1,7 @@
 """Grafted-MLP microbench sweep (hidden 4096, base intermediate 14336).
 
     python -m glt_b200.mlp_bench [--tokens 4096,16384,65536] [--slice 256,1024,4096]
-                                 [--steps 5] [--warmup 3]
+                                 [--steps 5] [--warmup 3] [--mlp-store 0|1|auto]
 
 One step = one grafted MLP block (RMSNorm -> [base | graft] gate/up GEMM with
 fused SiLU*mul -> down GEMM, plus the backward to the graft weights and the
@@ -21,13 +21,16 @@ import torch
 from . import graft as G
 
 
-def run_point(M: int, S: int, steps: int, warmup: int, D: int = 4096, F: int = 14336) -> dict:
+def run_point(M: int, S: int, steps: int, warmup: int, D: int = 4096, F: int = 14336,
+              store: int = -1) -> dict:
     cfg = G.GraftConfig(hidden_dim=D, intermediate_dim=F, slice_dim=S, num_layers=1, num_heads=32,
                         num_kv_heads=8, vocab_size=0, layout=G.LAYOUT_CONCAT, graft_layer_start=0,
                         graft_layer_end=0, graft_proj_gate=1, graft_proj_up=1, graft_proj_down=1,
                         allow_expansion_trap=1, adam_weight_decay=0.0, lambda_silence=0.0)
     m = G.GraftModel(cfg, 1, M, kind=G.MODEL_MLP_BLOCK)
     m.init_random(seed=5, std=0.02, graft_std=0.02, graft_down_std=0.02)
+    if store >= 0:
+        m.mlp_store(store)
     g = torch.Generator(device="cuda").manual_seed(M + S)
     x = torch.randn(M, D, device="cuda", generator=g).to(torch.bfloat16)
     y = torch.randn(M, D, device="cuda", generator=g)
@@ -66,11 +69,15 @@ def main(argv=None) -> int:
     ap.add_argument("--slice", default="256,1024,4096")
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--mlp-store", choices=["0", "1", "auto"], default="auto",
+                    help="1: the forward stores gate_pre/up for the backward; 0: the backward "
+                         "recomputes them; auto: as the library decides")
     a = ap.parse_args(argv)
+    store = -1 if a.mlp_store == "auto" else int(a.mlp_store)
     torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
     for S in [int(s) for s in a.slice.split(",")]:
         for M in [int(t) for t in a.tokens.split(",")]:
-            print(json.dumps(run_point(M, S, a.steps, a.warmup)), flush=True)
+            print(json.dumps(run_point(M, S, a.steps, a.warmup, store=store)), flush=True)
     return 0
 
 

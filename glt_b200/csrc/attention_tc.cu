@@ -421,7 +421,7 @@ struct BwdSmem {
   static constexpr uint32_t OFF_DS = OFF_P + T_BYTES;
   static constexpr uint32_t OFF_DQ = OFF_DS + T_BYTES;      // [8 warps]
   static constexpr uint32_t OFF_BAR = OFF_DQ + 8 * DQW_BYTES;
-  static constexpr uint32_t NUM_BARS = 1 + 2 * QD_STAGES + 1 + 1 + 2 + 1 + 1 + 1;
+  static constexpr uint32_t NUM_BARS = 1 + 2 * QD_STAGES + 1 + 1 + 2 + 1 + 1 + 2;
   static constexpr uint32_t TOTAL = 1024 + OFF_BAR + NUM_BARS * 8 + 16;
 };
 static_assert(BwdSmem::TOTAL <= 232448, "attention backward: shared memory over 227 KB");
@@ -440,7 +440,12 @@ __device__ __forceinline__ void bulk_wait_read0() {
 }
 __device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
-constexpr int BWD_THREADS = 320;   // producer, MMA, 8 compute warps
+// producer, two MMA issuers (S/dP; dV/dK/dQ), 8 compute warps.  An MMA
+// thread stalls ~200 cycles on every mbarrier wait it depends on, and the
+// tensor pipe holds about one instruction ahead, so a single issuer waiting
+// between N=64 products leaves the pipe idle for most of each wait; with two
+// issuers one keeps the pipe fed while the other waits.
+constexpr int BWD_THREADS = 352;
 
 __global__ void __launch_bounds__(BWD_THREADS, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_k,
@@ -468,8 +473,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   uint64_t* dq_free = sdp_free + 1;           // [2] dQ^T buffer drained
   uint64_t* p_full = dq_free + 2;
   uint64_t* mm_done = p_full + 1;
-  uint64_t* drain = mm_done + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* drain = mm_done + 1;              // [2] abort-path drain of each issuer
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 2);
   __shared__ int abort_flag;
   volatile int& s_abort = abort_flag;
 
@@ -494,7 +499,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     for (int i = 0; i < 2; ++i) mbar_init(&dq_free[i], 8);
     mbar_init(p_full, 8);
     mbar_init(mm_done, 1);
-    mbar_init(drain, 1);
+    mbar_init(&drain[0], 1);
+    mbar_init(&drain[1], 1);
     s_abort = 0;
     fence_mbar_init();
   }
@@ -541,7 +547,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       }
     }
   } else if (warp == 1) {
-    // ------------------------------ MMA issuer ----------------------------
+    // ------------------------- MMA issuer: S^T, dP^T -------------------------
     if (lane == 0) {
       // S^T(j), dP^T(j) into TMEM columns [0, 128) (both operands K-major),
       // once the warps have loaded item j-1's S/dP
@@ -563,9 +569,18 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         return true;
       };
       bool ok = mbar_wait(kv_full, 0, err, &s_abort);
-      if (ok && n_items > 0) { tc_fence_after(); ok = issue_sdp(0); }
+      if (ok) tc_fence_after();
+      for (int i = 0; ok && i < n_items; ++i) ok = issue_sdp(i);
+      if (!ok) s_abort = 1;
+    }
+  } else if (warp == 2) {
+    // ----------------------- MMA issuer: dV, dK, dQ^T -----------------------
+    // Item i's S/dP are complete before its P^T/dS^T exist (the compute warps
+    // waited on sdp_full), so this issuer's commit after dQ^T(i) also covers
+    // every product that read Q/dO stage i.
+    if (lane == 0) {
+      bool ok = mbar_wait(kv_full, 0, err, &s_abort);
       for (int i = 0; ok && i < n_items; ++i) {
-        if (i + 1 < n_items && !issue_sdp(i + 1)) { ok = false; break; }
         const int st = i % QD_STAGES;
         if (!mbar_wait(p_full, i & 1, err, &s_abort)) { ok = false; break; }
         tc_fence_after();
@@ -592,12 +607,12 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   } else {
     // ------------------------------- compute ------------------------------
     const int sub = warp & 3;                       // TMEM lane quarter
-    const int half = (warp - 2) >> 2;               // query columns [32 half, 32 half + 32)
+    const int half = (warp - 3) >> 2;               // query columns [32 half, 32 half + 32)
     const int r = sub * 32 + lane;                  // key row (TMEM lane); for dQ^T: d index
     const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
     const float sl2 = s.scale * LOG2E_F;
     const int key = kt * BK_KEYS + r;
-    float* w_dq = reinterpret_cast<float*>(sm + L::OFF_DQ + (warp - 2) * L::DQW_BYTES);
+    float* w_dq = reinterpret_cast<float*>(sm + L::OFF_DQ + (warp - 3) * L::DQW_BYTES);
     const uint32_t sDQW = smem_u32(w_dq);
     // lse / dsum of item i for query 32 half + lane (held by that lane and
     // broadcast by shuffle), prefetched one item ahead
@@ -748,15 +763,19 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     for (int d = 0; d < QD_STAGES && d < issued; ++d)
       mbar_wait(&qd_full[(issued - 1 - d) % QD_STAGES], ((issued - 1 - d) / QD_STAGES) & 1, err, nullptr);
   }
+  if ((warp == 1 || warp == 2) && s_abort) {
+    // each issuer waits (bounded) for its own MMAs before TMEM is freed
+    tc_fence_after();
+    if (lane == 0) {
+      umma_commit(&drain[warp - 1]);
+      mbar_wait(&drain[warp - 1], 0, err, nullptr);
+    }
+    __syncwarp();
+  }
+  tc_fence_before();
+  __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    if (s_abort) {
-      if (lane == 0) {
-        umma_commit(drain);
-        mbar_wait(drain, 0, err, nullptr);
-      }
-      __syncwarp();
-    }
     tmem_dealloc(tmem, TMEM_COLS);
   }
 }
@@ -784,6 +803,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
 // reduce-adds are [32 rows][32 fp32] in the 128-byte swizzle (16-byte chunk
 // c of row r at chunk c ^ (r & 7): conflict-free row-per-lane stores).
 // ---------------------------------------------------------------------------
+constexpr int BWD64_THREADS = 320;   // producer, MMA, 8 compute warps
 constexpr int B64_ROWS = 128;      // keys per CTA and queries per item
 constexpr int B64_STAGES = 3;      // Q/dO ring depth
 
@@ -813,7 +833,7 @@ __device__ __forceinline__ void stage_row32(float* stg, int lane, const float (&
         make_float4(t[4 * c] * scale, t[4 * c + 1] * scale, t[4 * c + 2] * scale, t[4 * c + 3] * scale);
 }
 
-__global__ void __launch_bounds__(BWD_THREADS, 1)
+__global__ void __launch_bounds__(BWD64_THREADS, 1)
     attn_bwd_tc64_kernel(const __grid_constant__ CUtensorMap tm_qkv,
                          const __grid_constant__ CUtensorMap tm_do,
                          const __grid_constant__ CUtensorMap tm_dq,
@@ -1190,7 +1210,7 @@ int flash_bwd_tc64(const uint16_t* qkv, const uint16_t* o, const uint16_t* dout,
   constexpr int smem = Bwd64Smem::TOTAL;
   GLT_TRY(ensure_smem_attr(reinterpret_cast<const void*>(attn_bwd_tc64_kernel), smem));
   dim3 grid(s.nh, s.B, s.T / B64_ROWS);
-  attn_bwd_tc64_kernel<<<grid, BWD_THREADS, smem, st>>>(tqkv, tdo, tdq, tdkv, lse, dsum, s,
+  attn_bwd_tc64_kernel<<<grid, BWD64_THREADS, smem, st>>>(tqkv, tdo, tdq, tdkv, lse, dsum, s,
                                                          device_error_word());
   GLT_LAUNCH_CHECK();
   GLT_TRY(acc_to_bf16(acc, qcols, s.nh, s.hd, dqkv, s.ld_qkv, M, s.T, rope_cos, rope_sin, st));

@@ -60,11 +60,11 @@ METRIC = "graft-train tokens/s at Llama-3-8B shape, 1-8 B200; MLP GEMM % of bf16
 # by (CTA-pair GEMMs, MLP store); algorithmic bytes 3.54 GB with the store
 # (x 268 MB + W_gu 252 MB read, h 1007 MB + bf16 gate_pre/up 2014 MB
 # written), 1.53 GB without:
-#   pairs, store on:      3,356,551,424 B read + 2,997,146,368 B written
+#   pairs, store on:      3,273,385,472 B read + 2,996,351,232 B written
 #   pairs, recompute:     4,736,081,152 B read + 1,001,093,888 B written
 #   one SM, store on:     2,496,413,184 B read + 2,991,854,080 B written
 #   one SM, recompute:    2,329,381,376 B read +   996,020,480 B written
-GATE_UP_TRAFFIC_BYTES = {(True, True): 3356551424 + 2997146368, (True, False): 4736081152 + 1001093888,
+GATE_UP_TRAFFIC_BYTES = {(True, True): 3273385472 + 2996351232, (True, False): 4736081152 + 1001093888,
                          (False, True): 2496413184 + 2991854080, (False, False): 2329381376 + 996020480}
 
 

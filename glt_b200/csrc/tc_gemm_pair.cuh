@@ -71,10 +71,14 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* t
       "l"(reinterpret_cast<uint64_t>(tm)), "r"(bar_cluster), "r"(c0), "r"(c1), "l"(policy)
       : "memory");
 }
-__device__ __forceinline__ uint64_t l2_policy_evict_normal() {
-  uint64_t p;
-  asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
-  return p;
+// Same load without an L2 policy.
+__device__ __forceinline__ void tma_load_2d_pair_nohint(void* dst, const CUtensorMap* tm, uint32_t bar_cluster,
+                                                        int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(bar_cluster), "r"(c0), "r"(c1)
+      : "memory");
 }
 // Bound of each abort-path drain of the pair kernel.
 constexpr uint64_t GLT_PAIR_DRAIN_NS = 2000000ull;   // 2 ms
@@ -229,7 +233,6 @@ __global__ void __launch_bounds__(gemm_threads<Epi>(), 1)
     // ------------------------------ TMA producer ------------------------------
     if (lane == 0) {
       const uint64_t pol_a = l2_policy_evict_last();
-      const uint64_t pol_b = l2_policy_evict_normal();
       int it = 0;
       for (int t = 0; !s_abort; ++t) {
         const int slot = t % UNIT_RING;
@@ -267,9 +270,9 @@ __global__ void __launch_bounds__(gemm_threads<Epi>(), 1)
           if (B_MN) {
 #pragma unroll
             for (int c = 0; c < BN / 2 / 64; ++c)
-              tma_load_2d_pair(b_tile + c * 8192, &tmB, fb, n0 + 64 * c, k0, pol_b);
+              tma_load_2d_pair_nohint(b_tile + c * 8192, &tmB, fb, n0 + 64 * c, k0);
           } else {
-            tma_load_2d_pair(b_tile, &tmB, fb, k0, n0, pol_b);
+            tma_load_2d_pair_nohint(b_tile, &tmB, fb, k0, n0);
           }
           p_last_issue = globaltimer();
         }

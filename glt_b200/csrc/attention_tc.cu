@@ -412,16 +412,16 @@ struct BwdSmem {
   static constexpr uint32_t KV_BYTES = BK_KEYS * 128 * 2;  // [128 keys][128 d] = 2 blocks x 16 KB
   static constexpr uint32_t QD_BYTES = BQ * 128 * 2;       // [64 q][128 d] = 2 blocks x 8 KB
   static constexpr uint32_t T_BYTES = BK_KEYS * BQ * 2;    // [128 keys][64 q] bf16
-  static constexpr uint32_t DQW_BYTES = 32 * 32 * 4;       // per compute warp: [32 q][32 d] fp32
+  static constexpr uint32_t DQW_BYTES = 32 * 32 * 4;       // one [32 q][32 d] fp32 staging block
   static constexpr uint32_t OFF_K = 0;
   static constexpr uint32_t OFF_V = OFF_K + KV_BYTES;
   static constexpr uint32_t OFF_Q = OFF_V + KV_BYTES;                // [QD_STAGES]
   static constexpr uint32_t OFF_DO = OFF_Q + QD_STAGES * QD_BYTES;   // [QD_STAGES]
   static constexpr uint32_t OFF_P = OFF_DO + QD_STAGES * QD_BYTES;
   static constexpr uint32_t OFF_DS = OFF_P + T_BYTES;
-  static constexpr uint32_t OFF_DQ = OFF_DS + T_BYTES;      // [8 warps]
+  static constexpr uint32_t OFF_DQ = OFF_DS + T_BYTES;      // [4 dQ warps][2 blocks]
   static constexpr uint32_t OFF_BAR = OFF_DQ + 8 * DQW_BYTES;
-  static constexpr uint32_t NUM_BARS = 1 + 2 * QD_STAGES + 1 + 1 + 2 + 1 + 1 + 2;
+  static constexpr uint32_t NUM_BARS = 1 + 2 * QD_STAGES + 1 + 1 + 2 + 1 + 1 + 2 + 2;
   static constexpr uint32_t TOTAL = 1024 + OFF_BAR + NUM_BARS * 8 + 16;
 };
 static_assert(BwdSmem::TOTAL <= 232448, "attention backward: shared memory over 227 KB");
@@ -440,12 +440,16 @@ __device__ __forceinline__ void bulk_wait_read0() {
 }
 __device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
-// producer, two MMA issuers (S/dP; dV/dK/dQ), 8 compute warps.  An MMA
-// thread stalls ~200 cycles on every mbarrier wait it depends on, and the
-// tensor pipe holds about one instruction ahead, so a single issuer waiting
-// between N=64 products leaves the pipe idle for most of each wait; with two
-// issuers one keeps the pipe fed while the other waits.
-constexpr int BWD_THREADS = 352;
+// producer, two MMA issuers (S/dP; dV/dK/dQ), 8 compute warps, 4 dQ warps.
+// An MMA thread stalls ~200 cycles on every mbarrier wait it depends on, and
+// the tensor pipe holds about one instruction ahead, so a single issuer
+// waiting between N=64 products leaves the pipe idle for most of each wait;
+// with two issuers one keeps the pipe fed while the other waits.  The dQ
+// warps drain dQ^T from TMEM into the global accumulator, which keeps that
+// work (a third of the compute warps' time per item) off the chain
+// S/dP -> P/dS -> dV/dK/dQ^T -> next item's P/dS.
+constexpr int BWD_THREADS = 480;
+constexpr int BWD_FIRST_DQ_WARP = 11;
 
 __global__ void __launch_bounds__(BWD_THREADS, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_k,
@@ -474,7 +478,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   uint64_t* p_full = dq_free + 2;
   uint64_t* mm_done = p_full + 1;
   uint64_t* drain = mm_done + 1;              // [2] abort-path drain of each issuer
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 2);
+  uint64_t* dq_full = drain + 2;              // [2] dQ^T of item i in buffer i & 1
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dq_full + 2);
   __shared__ int abort_flag;
   volatile int& s_abort = abort_flag;
 
@@ -496,7 +501,10 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     }
     mbar_init(sdp_full, 1);
     mbar_init(sdp_free, 8);
-    for (int i = 0; i < 2; ++i) mbar_init(&dq_free[i], 8);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&dq_free[i], 4);   // the 4 dQ warps
+      mbar_init(&dq_full[i], 1);
+    }
     mbar_init(p_full, 8);
     mbar_init(mm_done, 1);
     mbar_init(&drain[0], 1);
@@ -599,11 +607,52 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         for (int k = 0; k < BK_KEYS / 16; ++k)
           umma_bf16(tmem + COL_DQ + 64u * (i & 1), make_sdesc(sK + k * (UMMA_K * 128), BK_KEYS * 128, 1024),
                     make_sdesc(sDS + k * (UMMA_K * 128), 8192, 1024), ID_DQ, k > 0);
+        umma_commit(&dq_full[i & 1]);
         umma_commit(mm_done);
         umma_commit(&qd_empty[st]);
       }
       if (!ok) s_abort = 1;
     }
+  } else if (warp >= BWD_FIRST_DQ_WARP) {
+    // -------------------------------- dQ warps --------------------------------
+    // warp (quarter) drains d rows [32 quarter, +32) of dQ^T for all 64 queries
+    // of each item: TMEM -> two [32 q][32 d] fp32 blocks -> TMA reduce-adds.
+    // dQ^T(i + 2) reuses buffer i & 1 only after these warps released it, so
+    // dq_full never runs two phases ahead of them.
+    const int sub = warp & 3;
+    const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
+    float* stg = reinterpret_cast<float*>(sm + L::OFF_DQ + (warp - BWD_FIRST_DQ_WARP) * 2 * L::DQW_BYTES);
+    const uint32_t s_stg = smem_u32(stg);
+    bool ok = true;
+    for (int j = 0; j < n_items; ++j) {
+      if (!mbar_wait(&dq_full[j & 1], (j >> 1) & 1, err, &s_abort)) { ok = false; break; }
+      tc_fence_after();
+      float t0[32], t1[32];
+      tmem_ld32(tmem + lane_off + COL_DQ + 64u * (j & 1), t0);
+      tmem_ld32(tmem + lane_off + COL_DQ + 64u * (j & 1) + 32, t1);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&dq_free[j & 1]);
+        bulk_wait_read0();                          // the previous item's reduces have read the blocks
+      }
+      __syncwarp();
+#pragma unroll
+      for (int q = 0; q < 32; ++q) {
+        stg[q * 32 + lane] = t0[q] * s.scale;
+        stg[1024 + q * 32 + lane] = t1[q] * s.scale;
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        const int h = kvh * rep + j / per_head, qt = q_first + j % per_head;
+        tma_reduce_add_2d(&tm_dq, s_stg, h * HD + sub * 32, row0 + qt * BQ);
+        tma_reduce_add_2d(&tm_dq, s_stg + L::DQW_BYTES, h * HD + sub * 32, row0 + qt * BQ + 32);
+        bulk_commit();
+      }
+    }
+    if (!ok) s_abort = 1;
+    if (lane == 0) bulk_wait0();   // this warp's reduce-adds complete before the CTA exits
   } else {
     // ------------------------------- compute ------------------------------
     const int sub = warp & 3;                       // TMEM lane quarter
@@ -612,8 +661,6 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
     const float sl2 = s.scale * LOG2E_F;
     const int key = kt * BK_KEYS + r;
-    float* w_dq = reinterpret_cast<float*>(sm + L::OFF_DQ + (warp - 3) * L::DQW_BYTES);
-    const uint32_t sDQW = smem_u32(w_dq);
     // lse / dsum of item i for query 32 half + lane (held by that lane and
     // broadcast by shuffle), prefetched one item ahead
     auto lse_index = [&](int i) -> int64_t {
@@ -625,28 +672,6 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       pl = lse[lse_index(0)];
       pd = dsum[lse_index(0)];
     }
-    // dQ of item j: TMEM buffer j & 1 -> this warp's [32 q][32 d] tile -> TMA
-    // reduce-add (mm_done of item j already waited)
-    auto flush_dq = [&](int j) {
-      float t[32];
-      tmem_ld32(tmem + lane_off + COL_DQ + 64u * (j & 1) + 32 * half, t);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&dq_free[j & 1]);
-        bulk_wait_read0();                          // this warp's previous reduce has read its tile
-      }
-      __syncwarp();
-#pragma unroll
-      for (int q = 0; q < 32; ++q) w_dq[q * 32 + lane] = t[q] * s.scale;
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        const int h = kvh * rep + j / per_head, qt = q_first + j % per_head;
-        tma_reduce_add_2d(&tm_dq, sDQW, h * HD + sub * 32, row0 + qt * BQ + 32 * half);
-        bulk_commit();
-      }
-    };
     bool ok = true;
     for (int i = 0; i < n_items; ++i) {
       const int qt = q_first + i % per_head;
@@ -713,15 +738,10 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
-      // drain dQ of item i-1 (its products completed: mm_done waited above)
-      if (i > 0) flush_dq(i - 1);
     }
     if (ok && n_items > 0) {
       ok = mbar_wait(mm_done, (n_items - 1) & 1, err, &s_abort);
-      if (ok) {
-        tc_fence_after();
-        flush_dq(n_items - 1);
-      }
+      if (ok) tc_fence_after();
     }
     if (ok && n_items > 0) {
       // dK (scaled) and dV of this CTA's keys, d columns [64 half, 64 half + 64)
@@ -752,7 +772,6 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       }
     }
     if (!ok) s_abort = 1;
-    if (lane == 0) bulk_wait0();   // this warp's reduce-adds complete before the CTA exits
   }
 
   tc_fence_before();

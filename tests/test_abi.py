@@ -111,3 +111,20 @@ def test_profile_kinds_match_header():
     idx = {int(v): k.lower() for k, v in re.findall(r"#define GLT_PROF_(\w+) (\d+)", text) if k != "KINDS"}
     assert len(idx) == kinds
     assert idx[0] == "gate_up_fwd" and idx[12] == "attn_bwd" and idx[16] == "ce"
+
+
+def test_gemm_pair_mode_switch_is_host_only():
+    """glt_gemm_pair_mode sets and queries the process-wide GEMM tile mode
+    without touching a device (mode -1 queries; other values are ignored)."""
+    lib = _lib.lib
+    prev = lib.glt_gemm_pair_mode(-1)
+    assert prev in (0, 1)
+    try:
+        assert lib.glt_gemm_pair_mode(0) == 0
+        assert lib.glt_gemm_pair_mode(-1) == 0
+        assert lib.glt_gemm_pair_mode(7) == 0        # not a mode: query only
+        assert lib.glt_gemm_pair_mode(1) == 1
+        assert lib.glt_gemm_pair_mode(-1) == 1
+    finally:
+        lib.glt_gemm_pair_mode(prev)
+    assert lib.glt_gemm_pair_mode(-1) == prev

@@ -89,11 +89,3 @@ def test_pair_gemm_alpha_beta(pair_mode):
     out = _gemm(a_st, lda, 0, b_st, ldb, 0, M, N, K, True, alpha=0.5, beta=1.0, base=base)
     ref = 0.5 * (a_log @ b_log.t()) + base
     torch.testing.assert_close(out, ref, rtol=2e-3, atol=2e-2)
-
-
-def test_pair_mode_query_and_restore():
-    prev = _lib.lib.glt_gemm_pair_mode(-1)
-    assert prev in (0, 1)
-    assert _lib.lib.glt_gemm_pair_mode(1 - prev) == 1 - prev
-    assert _lib.lib.glt_gemm_pair_mode(-1) == 1 - prev
-    assert _lib.lib.glt_gemm_pair_mode(prev) == prev

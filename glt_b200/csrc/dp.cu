@@ -90,6 +90,18 @@ int Model::dp_init(const void* unique_id, int rank, int world) {
     const int v = atoi(e);
     dp_bucket = v < 1 ? 1 : (v > L ? L : v);
   }
+  // SMs left to NCCL by the GEMM that follows each all-reduce
+  // (GLT_DP_RESERVE_SMS; NCCL's ring runs 32 CTAs at 2 and 4 ranks, NVLS 24
+  // at 8) and how many GEMMs do so (GLT_DP_RESERVE_GEMMS, default 1: the dO
+  // GEMM, which starts right after the all-reduce).
+  if (const char* e = getenv("GLT_DP_RESERVE_SMS")) {
+    const int v = atoi(e);
+    dp_reserve_sms = v < 0 ? 0 : (v > 96 ? 96 : v);
+  }
+  if (const char* e = getenv("GLT_DP_RESERVE_GEMMS")) {
+    const int v = atoi(e);
+    dp_reserve_gemms = v < 0 ? 0 : (v > 8 ? 8 : v);
+  }
   // GLT_DP_COMM_PRIORITY=high puts the all-reduce stream at the device's
   // highest stream priority, so that at each kernel boundary of the backward
   // the block scheduler starts the collective's CTAs before the next GEMM's.

@@ -45,6 +45,32 @@ struct ScopedTileCounter {
   explicit ScopedTileCounter(int* c) : prev(gemm_tile_counter()) { gemm_tile_counter() = c; }
   ~ScopedTileCounter() { gemm_tile_counter() = prev; }
 };
+// SMs left to a collective that starts beside the next GEMMs this host thread
+// launches: the next `launches` GEMMs run `sms` fewer CTAs (CTA pairs: sms / 2
+// fewer clusters).  A persistent GEMM otherwise holds every SM, the
+// collective's CTAs wait for it, and on the other ranks that collective's
+// CTAs spin on SMs their own GEMMs' statically scheduled tiles are waiting
+// for; with the SMs left free the collective starts at once and the GEMM's
+// round-robin tiles balance over the rest.
+struct SmReserve {
+  int sms = 0;
+  int launches = 0;
+};
+inline SmReserve& gemm_sm_reserve() {
+  static thread_local SmReserve r;
+  return r;
+}
+// SMs the GEMM being launched leaves free (consumes one reserved launch).
+inline int take_sm_reserve() {
+  SmReserve& r = gemm_sm_reserve();
+  if (r.launches <= 0 || r.sms <= 0) return 0;
+  --r.launches;
+  return r.sms;
+}
+// Drops any reserve left when a step ends (also on its error paths).
+struct ScopedSmReserveReset {
+  ~ScopedSmReserveReset() { gemm_sm_reserve() = SmReserve{}; }
+};
 // Sets the dynamic-smem attribute of `func` to `bytes` once per (device, function).
 int ensure_smem_attr(const void* func, int bytes);
 // Prefers the largest shared-memory carveout for `func`, once per (device, function).
@@ -134,6 +160,8 @@ int launch_gemm_pair(const Operand& A, const Operand& B, int M, int N, int K, co
   int pairs = 0;
   GLT_TRY(max_active_pairs(reinterpret_cast<const void*>(kern), threads, smem, &pairs));
   const int units = ((M + PAIR_BM - 1) / PAIR_BM) * ((N + PAIR_BN - 1) / PAIR_BN) * shape.k_splits;
+  pairs -= take_sm_reserve() / 2;
+  if (pairs < 1) pairs = 1;
   const int clusters = units < pairs ? units : pairs;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * clusters);
@@ -207,7 +235,9 @@ int launch_gemm(const Operand& A, const Operand& B, int M, int N, int K, const E
   constexpr int smem = gemm_smem_bytes<BN, STAGES, Epi>();
   GLT_TRY(ensure_smem_attr(reinterpret_cast<const void*>(kern), smem));
   const int units = ((M + BM - 1) / BM) * ((N + BN - 1) / BN) * shape.k_splits;
-  const int grid = units < num_sms() ? units : num_sms();
+  int sms = num_sms() - take_sm_reserve();
+  if (sms < 1) sms = 1;
+  const int grid = units < sms ? units : sms;
   kern<<<grid, gemm_threads<Epi>(), smem, stream>>>(ta, ta2, tb, shape, epi);
   GLT_LAUNCH_CHECK();
   return GLT_OK;

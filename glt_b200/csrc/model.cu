@@ -779,6 +779,7 @@ int Model::backward_layer(int l, cudaStream_t st) {
     // graft grads of layers [l, l + dp_bucket) are final (layers run L-1 .. 0)
     GLT_CUDA_TRY(cudaEventRecord(layer_done[l], st));
     GLT_TRY(dp_allreduce_layers(l, std::min(L, l + dp_bucket)));
+    gemm_sm_reserve() = SmReserve{dp_reserve_sms, dp_reserve_gemms};
   }
   // post-attention RMSNorm backward + residual: dx = grad wrt x_post
   GLT_PROF(GLT_PROF_RMSNORM, rmsnorm_bwd(dtmp, y.x_post, y.post_norm, y.var2, dx, dx, dy_b, M, D, cfg.rms_norm_eps, st));
@@ -827,6 +828,7 @@ int Model::forward_all(bool use_graft, cudaStream_t st) {
 int Model::train_step(const int32_t* ids_in, const int32_t* ood_in, int host, int step,
                       int total_steps, GltStepStats* out, cudaStream_t st) {
   ScopedTileCounter tile_claims(gemm_counter());
+  ScopedSmReserveReset sm_reserve_reset;
   if (kind != GLT_MODEL_DECODER) return fail(GLT_ESTATE, "train_step needs the decoder model");
   if (shadow_baked) return fail(GLT_ESTATE, "backward on a shadow-baked model is forbidden");
   GLT_TRY(load_inputs(ids_in, ood_in, host, st));

@@ -212,6 +212,8 @@ struct Model {
   int dp_init(const void* unique_id, int rank, int world);
   int dp_allreduce_layers(int l0, int l1);   // layers [l0, l1), after layer_done[l0]
   int dp_bucket = 4;                          // layers per graft-gradient all-reduce
+  int dp_reserve_sms = 0;                     // SMs the GEMMs after an all-reduce leave to NCCL
+  int dp_reserve_gemms = 1;                   // how many GEMMs after each all-reduce do so
   int dp_async_error(int* nccl_result);
   int dp_abort();
   void dp_shutdown();
